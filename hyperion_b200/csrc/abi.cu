@@ -1,0 +1,664 @@
+// The hyperion_mlx.h ABI over the CUDA engine, plus the hyperion_b200.h extensions.
+//
+// Handle, status and error semantics follow the reference ABI implementation
+// (native/hyperion_mlx/src/model.cc:129-207 handles, :234-254 sampler-config
+// validation, :361-995 entry points; runtime.mm:223-298 canary / last error;
+// abi_error.cc thread-local message). No exception crosses the C boundary.
+#include "engine.h"
+#include "hyperion_b200.h"
+#include "hyperion_mlx.h"
+
+#include <algorithm>
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <filesystem>
+#include <limits>
+#include <memory>
+#include <new>
+#include <numeric>
+#include <optional>
+#include <random>
+#include <string>
+#include <vector>
+
+// Opaque handle bodies (global namespace to match the header's struct tags).
+struct HypModelOpaque {
+    uint32_t magic;
+    bool loaded = false;
+    std::unique_ptr<hyb::Model> model;
+};
+
+struct HypKvStateOpaque {
+    uint32_t magic;
+    std::unique_ptr<hyb::KvState> kv;
+    const HypModelOpaque* owner = nullptr;
+};
+
+struct HypStepResultOpaque {
+    uint32_t magic;
+    HypStepResultFields fields;
+};
+
+namespace {
+
+constexpr uint32_t kModelMagic = 0x48504D4FU;       // "HPMO"
+constexpr uint32_t kKvStateMagic = 0x48504B56U;     // "HPKV"
+constexpr uint32_t kStepResultMagic = 0x48505352U;  // "HPSR"
+constexpr uint32_t kAbiVersion = 3;
+constexpr size_t kLastErrorCapacity = 1024;
+
+thread_local char g_last_error[kLastErrorCapacity] = {0};
+thread_local bool g_fault_armed = false;
+
+HypStatus fail(HypStatus s, const char* msg) noexcept {
+    std::snprintf(g_last_error, kLastErrorCapacity, "%s", msg ? msg : "unknown native error");
+    return s;
+}
+HypStatus fail(HypStatus s, const std::string& msg) noexcept { return fail(s, msg.c_str()); }
+HypStatus ok() noexcept {
+    g_last_error[0] = '\0';
+    return HYP_STATUS_OK;
+}
+
+}  // namespace
+
+namespace hyb {
+// Shared with the op-level entry points (ops_abi.cu).
+HypStatus abi_fail(HypStatus s, const char* msg) noexcept { return fail(s, msg); }
+HypStatus abi_ok() noexcept { return ok(); }
+}  // namespace hyb
+
+namespace {
+
+HypStatus validate_model(HypModel m) noexcept {
+    if (m == nullptr) return fail(HYP_STATUS_INVALID_ARGUMENT, "model handle is null");
+    if (m->magic != kModelMagic)
+        return fail(HYP_STATUS_INVALID_ARGUMENT, "model handle magic mismatch (wrong type, freed, or corrupted)");
+    return ok();
+}
+HypStatus validate_kv(HypKvState kv) noexcept {
+    if (kv == nullptr || kv->magic != kKvStateMagic) return fail(HYP_STATUS_INVALID_ARGUMENT, "kvstate handle is invalid");
+    if (kv->kv && kv->kv->poisoned)
+        return fail(HYP_STATUS_INTERNAL, "KV state is unusable after an internal execution failure; free and recreate it");
+    return ok();
+}
+HypStatus validate_result(HypStepResult r) noexcept {
+    if (r == nullptr || r->magic != kStepResultMagic) return fail(HYP_STATUS_INVALID_ARGUMENT, "step-result handle is invalid");
+    return ok();
+}
+
+template <typename H>
+HypStatus create_handle(H** out, uint32_t magic) noexcept {
+    if (out == nullptr) return fail(HYP_STATUS_INVALID_ARGUMENT, "create requires a non-null out handle");
+    try {
+        auto* h = new H{};
+        h->magic = magic;
+        *out = h;
+        return ok();
+    } catch (const std::bad_alloc&) {
+        return fail(HYP_STATUS_INTERNAL, "native allocation failed outside predictive governor admission");
+    } catch (...) {
+        return fail(HYP_STATUS_INTERNAL, "unexpected exception in handle create");
+    }
+}
+
+template <typename H>
+HypStatus free_handle(H** h, uint32_t magic) noexcept {
+    if (h == nullptr) return fail(HYP_STATUS_INVALID_ARGUMENT, "free requires a non-null handle pointer");
+    H* p = *h;
+    if (p == nullptr) return ok();
+    if (p->magic != magic) return fail(HYP_STATUS_INVALID_ARGUMENT, "handle magic mismatch (wrong type, freed, or corrupted)");
+    p->magic = 0;
+    try {
+        delete p;
+    } catch (...) {
+    }
+    *h = nullptr;
+    return ok();
+}
+
+// Run `fn` mapping exceptions to statuses (model.cc:442-452).
+template <typename Fn>
+HypStatus guarded(const char* op, Fn&& fn) noexcept {
+    try {
+        return fn();
+    } catch (const std::filesystem::filesystem_error& e) {
+        return fail(HYP_STATUS_IO, e.what());
+    } catch (const std::bad_alloc&) {
+        return fail(HYP_STATUS_INTERNAL, "native allocation failed outside predictive governor admission");
+    } catch (const std::exception& e) {
+        return fail(HYP_STATUS_INTERNAL, e.what());
+    } catch (...) {
+        return fail(HYP_STATUS_INTERNAL, std::string(op) + " failed with a non-standard exception");
+    }
+}
+
+struct DeviceGuard {
+    int prev = -1;
+    explicit DeviceGuard(int dev) {
+        if (cudaGetDevice(&prev) != cudaSuccess) prev = -1;
+        if (prev != dev) hyb::cuda_check(cudaSetDevice(dev), "cudaSetDevice");
+    }
+    ~DeviceGuard() {
+        int cur = -1;
+        if (prev >= 0 && cudaGetDevice(&cur) == cudaSuccess && cur != prev) cudaSetDevice(prev);
+    }
+};
+
+void write_result(HypStepResult r, const hyb::StepOut* s, uint32_t near_ties, HypGovernorState state,
+                  const hyb::Model& m, const hyb::KvState& kv, bool sampled) {
+    HypStepResultFields f{};
+    if (s) {
+        f.token_id = s->token;
+        f.logit = s->logit;
+        if (sampled) {
+            const uint32_t n = std::min<uint32_t>(HYP_TOP_K_LOGPROBS, m.geometry().vocab);
+            f.top_k_logprob_count = n;
+            for (uint32_t i = 0; i < n; ++i) {
+                f.top_k_logprob_ids[i] = s->topk_idx[i];
+                f.top_k_logprob_values[i] = s->topk_val[i];
+            }
+        }
+    }
+    f.peak_mlx_bytes = hyb::dev_peak_bytes();
+    f.active_mlx_bytes = hyb::dev_active_bytes();
+    f.local_kv_bytes = m.local_kv_bytes(kv);
+    f.global_kv_bytes = m.global_kv_bytes(kv);
+    f.governor_state = state;
+    f.near_tie_events = sampled ? 0u : near_ties;
+    r->fields = f;
+}
+
+std::optional<std::string> validate_sampling(const HypSamplingConfig* c, uint32_t vocab) {
+    if (c == nullptr || c->temperature == 0.0f) return std::nullopt;
+    if (c->temperature < 0.0f) return std::string("sampling temperature must be >= 0 (0 = greedy)");
+    if (c->top_k < 0) return std::string("sampling top_k must be >= 0 (0 = disabled)");
+    if (c->top_k > 0 && static_cast<uint64_t>(c->top_k) > vocab) return std::string("sampling top_k exceeds the vocabulary size");
+    if (!std::isnan(c->top_p) && (c->top_p < 0.0f || c->top_p > 1.0f))
+        return std::string("sampling top_p must be in [0, 1] (0 = disabled)");
+    if (c->min_p < 0.0f || c->min_p >= 1.0f) return std::string("sampling min_p must be in [0, 1) (0 = disabled)");
+    return std::nullopt;
+}
+
+float bf16_bits_to_float(uint16_t h) {
+    uint32_t u = static_cast<uint32_t>(h) << 16;
+    float f;
+    std::memcpy(&f, &u, 4);
+    return f;
+}
+
+// Host sampler over one post-softcap logit row: temperature, then top-p, min-p,
+// top-k masks, softmax and an inverse-CDF draw from std::mt19937_64 (the steps of
+// forward.cc:191-322).
+hyb::StepOut sample_row(const std::vector<uint16_t>& row, const HypSamplingConfig& cfg, uint64_t rng_state) {
+    const size_t n = row.size();
+    std::vector<float> src(n);
+    for (size_t i = 0; i < n; ++i) src[i] = bf16_bits_to_float(row[i]);
+    const float ninf = -std::numeric_limits<float>::infinity();
+    std::vector<float> lg(src);
+    const float inv_t = 1.0f / cfg.temperature;
+    for (float& v : lg) v *= inv_t;
+    float mx = ninf;
+    for (float v : lg) mx = std::max(mx, v);
+    std::vector<float> pr(n);
+    float z = 0.f;
+    for (size_t i = 0; i < n; ++i) {
+        pr[i] = std::exp(lg[i] - mx);
+        z += pr[i];
+    }
+    if (z > 0.f)
+        for (float& v : pr) v /= z;
+    if (cfg.top_p > 0.0f && cfg.top_p <= 1.0f) {
+        std::vector<uint32_t> idx(n);
+        std::iota(idx.begin(), idx.end(), 0u);
+        std::sort(idx.begin(), idx.end(), [&](uint32_t a, uint32_t b) { return pr[a] > pr[b]; });
+        std::vector<char> keep(n, 0);
+        float cum = 0.f;
+        for (uint32_t i : idx) {
+            keep[i] = 1;
+            cum += pr[i];
+            if (cum >= cfg.top_p) break;
+        }
+        for (size_t i = 0; i < n; ++i)
+            if (!keep[i]) lg[i] = ninf;
+    }
+    if (cfg.min_p > 0.0f && cfg.min_p < 1.0f) {
+        float mp = 0.f;
+        for (float v : pr) mp = std::max(mp, v);
+        const float th = cfg.min_p * mp;
+        for (size_t i = 0; i < n; ++i)
+            if (pr[i] < th) lg[i] = ninf;
+    }
+    if (cfg.top_k > 0 && static_cast<uint32_t>(cfg.top_k) < n) {
+        std::vector<uint32_t> idx(n);
+        std::iota(idx.begin(), idx.end(), 0u);
+        std::partial_sort(idx.begin(), idx.begin() + cfg.top_k, idx.end(),
+                          [&](uint32_t a, uint32_t b) { return lg[a] > lg[b]; });
+        std::vector<char> keep(n, 0);
+        for (int32_t i = 0; i < cfg.top_k; ++i) keep[idx[i]] = 1;
+        for (size_t i = 0; i < n; ++i)
+            if (!keep[i]) lg[i] = ninf;
+    }
+    float fm = ninf;
+    for (float v : lg) fm = std::max(fm, v);
+    std::vector<float> sp(n);
+    float sz = 0.f;
+    for (size_t i = 0; i < n; ++i) {
+        sp[i] = (lg[i] == ninf) ? 0.f : std::exp(lg[i] - fm);
+        sz += sp[i];
+    }
+    std::mt19937_64 rng(rng_state);
+    std::uniform_real_distribution<float> uni(0.0f, sz);
+    const float u = uni(rng);
+    float c = 0.f;
+    uint32_t arg = 0;
+    for (size_t i = 0; i < n; ++i) {
+        c += sp[i];
+        arg = static_cast<uint32_t>(i);
+        if (u <= c) break;
+    }
+    hyb::StepOut out;
+    out.token = arg;
+    out.logit = src[arg];
+    std::vector<uint32_t> idx(n);
+    std::iota(idx.begin(), idx.end(), 0u);
+    const size_t k = std::min<size_t>(HYP_TOP_K_LOGPROBS, n);
+    std::partial_sort(idx.begin(), idx.begin() + k, idx.end(), [&](uint32_t a, uint32_t b) { return src[a] > src[b]; });
+    for (size_t i = 0; i < k; ++i) {
+        out.topk_idx[i] = idx[i];
+        out.topk_val[i] = src[idx[i]];
+    }
+    return out;
+}
+
+// Predictive admission stand-in: reject when the KV growth of this call would not
+// fit into the device's free memory (keeps the OOM_GOVERNOR status contract).
+bool admit(const hyb::Model& m, const hyb::KvState& kv, uint32_t n_tokens, std::string& why) {
+    uint64_t grow = 0;
+    for (const auto& c : kv.global) {
+        const uint64_t need = (static_cast<uint64_t>(c.committed) + n_tokens + 255) / 256 * 256;
+        if (need > 0xFFFFFFFFull) {
+            why = "KV operation exceeds representable cache dimensions";
+            return false;
+        }
+        if (need > c.capacity) grow += (need - c.capacity) * static_cast<uint64_t>(c.nkv) * c.hd * 2 * 2;
+    }
+    for (const auto& c : kv.local) {
+        if (static_cast<uint64_t>(c.committed) + n_tokens > 0xFFFFFFFFull) {
+            why = "KV operation exceeds representable cache dimensions";
+            return false;
+        }
+    }
+    if (grow == 0) return true;
+    size_t free_b = 0, total_b = 0;
+    if (cudaMemGetInfo(&free_b, &total_b) != cudaSuccess) return true;
+    if (grow + (1ull << 30) > free_b) {
+        why = "predicted KV growth exceeds the device memory budget";
+        return false;
+    }
+    return true;
+}
+
+void maybe_inject_fault() {
+    if (g_fault_armed) {
+        g_fault_armed = false;
+        throw std::runtime_error("injected post-append forward failure");
+    }
+}
+
+HypStatus load_common(HypModel model, const HypGeometryParams* geometry, const char* path, bool synthetic,
+                      uint64_t seed) {
+    HypStatus st = validate_model(model);
+    if (st != HYP_STATUS_OK) return st;
+    if (geometry == nullptr) return fail(HYP_STATUS_INVALID_ARGUMENT, "geometry is null");
+    if (!synthetic && path == nullptr) return fail(HYP_STATUS_INVALID_ARGUMENT, "weights_path is null");
+    if (model->loaded) return fail(HYP_STATUS_INVALID_ARGUMENT, "model is already loaded");
+    hyb::Geometry g;
+    if (auto e = hyb::geometry_from_abi(*geometry, g)) return fail(HYP_STATUS_INVALID_ARGUMENT, *e);
+    if (auto e = hyb::geometry_validate(g)) return fail(HYP_STATUS_INVALID_ARGUMENT, *e);
+    if (!synthetic && !std::filesystem::is_directory(path))
+        return fail(HYP_STATUS_NOT_FOUND, "weights artifact directory not found");
+    if (auto e = hyb::geometry_engine_support(g)) return fail(HYP_STATUS_UNSUPPORTED, *e);
+    return guarded("hyp_model_load", [&]() -> HypStatus {
+        int ndev = 0;
+        if (cudaGetDeviceCount(&ndev) != cudaSuccess || ndev == 0) {
+            (void)cudaGetLastError();
+            return fail(HYP_STATUS_UNSUPPORTED, "no CUDA device is available");
+        }
+        auto m = std::make_unique<hyb::Model>();
+        if (synthetic) m->load_synthetic(g, seed);
+        else m->load_dir(g, path);
+        model->model = std::move(m);
+        model->loaded = true;
+        return ok();
+    });
+}
+
+// ---- canary probes
+__global__ void canary_sum_kernel(const float* in, float* out) {
+    float s = 0.f;
+    for (int i = 0; i < 4; ++i) s += in[i];
+    *out = s;
+}
+__global__ void canary_add_one_kernel(float* v) { *v += 1.0f; }
+
+void copy_str(char* dst, size_t cap, const std::string& s) {
+    if (cap == 0) return;
+    const size_t n = std::min(cap - 1, s.size());
+    std::memcpy(dst, s.data(), n);
+    dst[n] = '\0';
+}
+
+}  // namespace
+
+extern "C" {
+
+HypStatus hyp_runtime_canary(HypCanaryInfo* out) {
+    if (out == nullptr) return fail(HYP_STATUS_INVALID_ARGUMENT, "hyp_runtime_canary requires a non-null output pointer");
+    return guarded("hyp_runtime_canary", [&]() -> HypStatus {
+        *out = HypCanaryInfo{};
+        int ndev = 0;
+        if (cudaGetDeviceCount(&ndev) != cudaSuccess || ndev == 0) {
+            (void)cudaGetLastError();
+            return fail(HYP_STATUS_UNSUPPORTED, "no CUDA device is available");
+        }
+        int dev = 0;
+        HYB_CUDA(cudaGetDevice(&dev));
+        cudaDeviceProp prop{};
+        HYB_CUDA(cudaGetDeviceProperties(&prop, dev));
+        if (prop.major < 10) return fail(HYP_STATUS_UNSUPPORTED, "the engine requires an sm_100 (Blackwell) GPU");
+        int rt = 0, drv = 0;
+        HYB_CUDA(cudaRuntimeGetVersion(&rt));
+        HYB_CUDA(cudaDriverGetVersion(&drv));
+        size_t free_b = 0, total_b = 0;
+        HYB_CUDA(cudaMemGetInfo(&free_b, &total_b));
+        float host[4] = {1.f, 1.f, 1.f, 1.f};
+        float* d = nullptr;
+        HYB_CUDA(cudaMalloc(&d, 8 * sizeof(float)));
+        float sum = 0.f, probe = 41.f;
+        HYB_CUDA(cudaMemcpy(d, host, sizeof(host), cudaMemcpyHostToDevice));
+        canary_sum_kernel<<<1, 1>>>(d, d + 4);
+        HYB_CUDA(cudaMemcpy(d + 5, &probe, sizeof(float), cudaMemcpyHostToDevice));
+        canary_add_one_kernel<<<1, 1>>>(d + 5);
+        HYB_CUDA(cudaGetLastError());
+        HYB_CUDA(cudaMemcpy(&sum, d + 4, sizeof(float), cudaMemcpyDeviceToHost));
+        HYB_CUDA(cudaMemcpy(&probe, d + 5, sizeof(float), cudaMemcpyDeviceToHost));
+        cudaFree(d);
+        if (std::fabs(sum - 4.f) > 1e-4f) return fail(HYP_STATUS_INTERNAL, "CUDA tensor canary returned the wrong value");
+        if (std::fabs(probe - 42.f) > 1e-4f) return fail(HYP_STATUS_INTERNAL, "CUDA kernel canary returned the wrong value");
+        out->abi_version = kAbiVersion;
+        out->mlx_compile_major = CUDART_VERSION / 1000;
+        out->mlx_compile_minor = (CUDART_VERSION % 1000) / 10;
+        out->mlx_compile_patch = CUDART_VERSION % 10;
+        out->macos_major = static_cast<uint32_t>(drv / 1000);
+        out->macos_minor = static_cast<uint32_t>((drv % 1000) / 10);
+        out->macos_patch = static_cast<uint32_t>(drv % 10);
+        out->gpu_family = static_cast<uint32_t>(prop.major * 10 + prop.minor);
+        out->recommended_working_set_bytes = total_b;
+        out->effective_budget_bytes = free_b;
+        out->soft_watermark_bytes = free_b / 10 * 9;
+        out->mlx_probe_value = sum;
+        out->metallib_probe_value = probe;
+        copy_str(out->mlx_runtime_version, sizeof(out->mlx_runtime_version),
+                 "cuda " + std::to_string(rt / 1000) + "." + std::to_string((rt % 1000) / 10));
+        copy_str(out->gpu_name, sizeof(out->gpu_name), prop.name);
+        return ok();
+    });
+}
+
+HypStatus hyp_last_error(char* buffer, size_t len) {
+    if (buffer == nullptr || len == 0) return fail(HYP_STATUS_INVALID_ARGUMENT, "hyp_last_error requires a writable non-empty buffer");
+    std::snprintf(buffer, len, "%s", g_last_error);
+    return HYP_STATUS_OK;
+}
+
+HypStatus hyp_model_create(HypModel* out) { return create_handle(out, kModelMagic); }
+HypStatus hyp_model_free(HypModel* m) { return free_handle(m, kModelMagic); }
+
+HypStatus hyp_model_load(HypModel model, const HypGeometryParams* geometry, const char* weights_path) {
+    return load_common(model, geometry, weights_path, false, 0);
+}
+
+HypStatus hyp_kvstate_create(HypModel model, HypKvState* out) {
+    HypStatus st = validate_model(model);
+    if (st != HYP_STATUS_OK) return st;
+    if (out == nullptr) return fail(HYP_STATUS_INVALID_ARGUMENT, "out_kvstate is null");
+    if (!model->loaded) return fail(HYP_STATUS_INVALID_ARGUMENT, "model is not loaded; cannot allocate KV state");
+    return guarded("hyp_kvstate_create", [&]() -> HypStatus {
+        DeviceGuard dg(model->model->device());
+        auto kv = model->model->new_kv();
+        auto* h = new HypKvStateOpaque{};
+        h->magic = kKvStateMagic;
+        h->kv = std::move(kv);
+        h->owner = model;
+        *out = h;
+        return ok();
+    });
+}
+
+HypStatus hyp_kvstate_free(HypKvState* kv) { return free_handle(kv, kKvStateMagic); }
+
+}  // extern "C"
+
+namespace {
+
+// Shared prefill driver (greedy or sampled; optional logits copy-out).
+HypStatus prefill_impl(HypModel model, HypKvState kv, const HypTokenStream* tokens, const HypSamplingConfig* cfg,
+                       HypStepResult out, void* host_logits) {
+    HypStatus st = validate_model(model);
+    if (st != HYP_STATUS_OK) return st;
+    st = validate_kv(kv);
+    if (st != HYP_STATUS_OK) return st;
+    if (tokens == nullptr) return fail(HYP_STATUS_INVALID_ARGUMENT, "tokens is null");
+    if (tokens->count == 0) return fail(HYP_STATUS_INVALID_ARGUMENT, "prefill token count is 0");
+    if (tokens->tokens == nullptr) return fail(HYP_STATUS_INVALID_ARGUMENT, "tokens->tokens is null");
+    st = validate_result(out);
+    if (st != HYP_STATUS_OK) return st;
+    if (!model->loaded) return fail(HYP_STATUS_INVALID_ARGUMENT, "model is not loaded");
+    if (kv->kv->offset != 0) return fail(HYP_STATUS_INVALID_ARGUMENT, "prefill requires a fresh (offset 0) KV state");
+    hyb::Model& m = *model->model;
+    for (uint32_t i = 0; i < tokens->count; ++i)
+        if (tokens->tokens[i] >= m.geometry().vocab) return fail(HYP_STATUS_INVALID_ARGUMENT, "token id is outside the vocabulary");
+    return guarded("hyp_prefill_chunk", [&]() -> HypStatus {
+        DeviceGuard dg(m.device());
+        std::string why;
+        if (!admit(m, *kv->kv, tokens->count, why)) {
+            write_result(out, nullptr, 0, HYP_GOVERNOR_HARD_REJECT, m, *kv->kv, false);
+            return fail(HYP_STATUS_OOM_GOVERNOR, why);
+        }
+        hyb::dev_reset_peak();
+        const bool sampled = cfg != nullptr && cfg->temperature != 0.0f;
+        std::vector<uint16_t> logits;
+        hyb::StepOut o;
+        try {
+            o = m.prefill(*kv->kv, tokens->tokens, tokens->count, (sampled || host_logits) ? &logits : nullptr);
+        } catch (...) {
+            kv->kv->poisoned = true;  // cache contents are partially written
+            throw;
+        }
+        if (sampled) {
+            o = sample_row(logits, *cfg, cfg->seed);
+            kv->kv->last_token = o.token;
+        }
+        if (host_logits) std::memcpy(host_logits, logits.data(), logits.size() * 2);
+        write_result(out, &o, o.near_tie ? 1u : 0u, HYP_GOVERNOR_READY, m, *kv->kv, sampled);
+        return ok();
+    });
+}
+
+HypStatus decode_impl(HypModel model, HypKvState kv, uint32_t n_tokens, const HypSamplingConfig* cfg,
+                      HypStepResult out, void* host_logits, const uint32_t* forced) {
+    HypStatus st = validate_model(model);
+    if (st != HYP_STATUS_OK) return st;
+    st = validate_kv(kv);
+    if (st != HYP_STATUS_OK) return st;
+    st = validate_result(out);
+    if (st != HYP_STATUS_OK) return st;
+    if (!model->loaded) return fail(HYP_STATUS_INVALID_ARGUMENT, "model is not loaded");
+    if (kv->kv->offset == 0) return fail(HYP_STATUS_INVALID_ARGUMENT, "decode requires a populated KV state (prefill first)");
+    hyb::Model& m = *model->model;
+    if (n_tokens == 0) {
+        write_result(out, nullptr, 0, HYP_GOVERNOR_READY, m, *kv->kv, cfg != nullptr && cfg->temperature != 0.0f);
+        return ok();
+    }
+    if (forced && *forced >= m.geometry().vocab) return fail(HYP_STATUS_INVALID_ARGUMENT, "token id is outside the vocabulary");
+    return guarded("hyp_decode_block", [&]() -> HypStatus {
+        DeviceGuard dg(m.device());
+        std::string why;
+        if (!admit(m, *kv->kv, n_tokens, why)) {
+            write_result(out, nullptr, 0, HYP_GOVERNOR_HARD_REJECT, m, *kv->kv, false);
+            return fail(HYP_STATUS_OOM_GOVERNOR, why);
+        }
+        hyb::dev_reset_peak();
+        const bool sampled = cfg != nullptr && cfg->temperature != 0.0f;
+        uint64_t rng = sampled ? cfg->seed : 0;
+        uint32_t near_ties = 0;
+        hyb::StepOut o;
+        std::vector<uint16_t> logits;
+        for (uint32_t step = 0; step < n_tokens; ++step) {
+            if (forced) kv->kv->last_token = *forced;
+            try {
+                o = m.decode_step(*kv->kv, (sampled || host_logits) ? &logits : nullptr);
+                if (step == 0) maybe_inject_fault();
+            } catch (...) {
+                kv->kv->poisoned = true;  // model.cc:79-105: a failed direct decode consumes the state
+                throw;
+            }
+            if (sampled) {
+                o = sample_row(logits, *cfg, rng);
+                kv->kv->last_token = o.token;
+                rng = rng * 6364136223846793005ULL + 1442695040888963407ULL;
+            }
+            if (o.near_tie) ++near_ties;
+        }
+        if (host_logits) std::memcpy(host_logits, logits.data(), logits.size() * 2);
+        write_result(out, &o, near_ties, HYP_GOVERNOR_READY, m, *kv->kv, sampled);
+        return ok();
+    });
+}
+
+}  // namespace
+
+extern "C" {
+
+HypStatus hyp_prefill_chunk(HypModel model, HypKvState kv, const HypTokenStream* tokens, HypStepResult out) {
+    return prefill_impl(model, kv, tokens, nullptr, out, nullptr);
+}
+
+HypStatus hyp_decode_block(HypModel model, HypKvState kv, uint32_t n_tokens, HypStepResult out) {
+    return decode_impl(model, kv, n_tokens, nullptr, out, nullptr, nullptr);
+}
+
+HypStatus hyp_prefill_chunk_sampled(HypModel model, HypKvState kv, const HypTokenStream* tokens,
+                                    const HypSamplingConfig* config, HypStepResult out) {
+    HypStatus st = validate_model(model);
+    if (st != HYP_STATUS_OK) return st;
+    st = validate_kv(kv);
+    if (st != HYP_STATUS_OK) return st;
+    st = validate_result(out);
+    if (st != HYP_STATUS_OK) return st;
+    if (!model->loaded) return fail(HYP_STATUS_INVALID_ARGUMENT, "model is not loaded");
+    if (auto e = validate_sampling(config, model->model->geometry().vocab)) return fail(HYP_STATUS_INVALID_ARGUMENT, *e);
+    if (config == nullptr || config->temperature == 0.0f) return hyp_prefill_chunk(model, kv, tokens, out);
+    return prefill_impl(model, kv, tokens, config, out, nullptr);
+}
+
+HypStatus hyp_decode_block_sampled(HypModel model, HypKvState kv, uint32_t n_tokens, const HypSamplingConfig* config,
+                                   HypStepResult out) {
+    HypStatus st = validate_model(model);
+    if (st != HYP_STATUS_OK) return st;
+    st = validate_kv(kv);
+    if (st != HYP_STATUS_OK) return st;
+    st = validate_result(out);
+    if (st != HYP_STATUS_OK) return st;
+    if (!model->loaded) return fail(HYP_STATUS_INVALID_ARGUMENT, "model is not loaded");
+    if (auto e = validate_sampling(config, model->model->geometry().vocab)) return fail(HYP_STATUS_INVALID_ARGUMENT, *e);
+    if (config == nullptr || config->temperature == 0.0f) return hyp_decode_block(model, kv, n_tokens, out);
+    return decode_impl(model, kv, n_tokens, config, out, nullptr, nullptr);
+}
+
+HypStatus hyp_step_result_create(HypStepResult* out) { return create_handle(out, kStepResultMagic); }
+HypStatus hyp_step_result_free(HypStepResult* r) { return free_handle(r, kStepResultMagic); }
+
+HypStatus hyp_step_result_fields(HypStepResult r, HypStepResultFields* out) {
+    if (out == nullptr) return HYP_STATUS_INVALID_ARGUMENT;
+    if (r == nullptr || r->magic != kStepResultMagic) return HYP_STATUS_INVALID_ARGUMENT;
+    *out = r->fields;
+    return HYP_STATUS_OK;
+}
+
+// ------------------------------------------------------------------ extensions (hyperion_b200.h)
+HypStatus hyb_model_load_synthetic(HypModel model, const HypGeometryParams* geometry, uint64_t seed) {
+    return load_common(model, geometry, nullptr, true, seed);
+}
+
+HypStatus hyb_model_stream(HypModel model, void** out_stream) {
+    HypStatus st = validate_model(model);
+    if (st != HYP_STATUS_OK) return st;
+    if (out_stream == nullptr) return fail(HYP_STATUS_INVALID_ARGUMENT, "out_stream is null");
+    if (!model->loaded) return fail(HYP_STATUS_INVALID_ARGUMENT, "model is not loaded");
+    *out_stream = model->model->stream();
+    return ok();
+}
+
+HypStatus hyb_kv_cursor(HypKvState kv, uint32_t* offset, uint32_t* last_token) {
+    if (kv == nullptr || kv->magic != kKvStateMagic) return fail(HYP_STATUS_INVALID_ARGUMENT, "kvstate handle is invalid");
+    if (offset) *offset = kv->kv->offset;
+    if (last_token) *last_token = kv->kv->last_token;
+    return ok();
+}
+
+HypStatus hyb_kv_copy_layer(HypModel model, HypKvState kv, uint32_t layer, int32_t which, void* host_out, uint32_t* rows) {
+    HypStatus st = validate_model(model);
+    if (st != HYP_STATUS_OK) return st;
+    if (kv == nullptr || kv->magic != kKvStateMagic) return fail(HYP_STATUS_INVALID_ARGUMENT, "kvstate handle is invalid");
+    if (!model->loaded || rows == nullptr) return fail(HYP_STATUS_INVALID_ARGUMENT, "model not loaded or rows is null");
+    const hyb::Geometry& g = model->model->geometry();
+    if (layer >= g.n_layers) return fail(HYP_STATUS_INVALID_ARGUMENT, "layer out of range");
+    return guarded("hyb_kv_copy_layer", [&]() -> HypStatus {
+        DeviceGuard dg(model->model->device());
+        size_t li = 0, gi = 0;
+        for (uint32_t i = 0; i < layer; ++i) (g.kinds[i] == hyb::LayerKind::Sliding ? li : gi)++;
+        const hyb::bf16* src;
+        uint32_t cap;
+        size_t row;
+        if (g.kinds[layer] == hyb::LayerKind::Sliding) {
+            const auto& c = kv->kv->local[li];
+            src = which == 0 ? c.k.p : c.v.p;
+            cap = c.cap;
+            row = static_cast<size_t>(c.nkv) * c.hd;
+        } else {
+            const auto& c = kv->kv->global[gi];
+            src = which == 0 ? c.k.p : c.v.p;
+            cap = c.capacity;
+            row = static_cast<size_t>(c.nkv) * c.hd;
+        }
+        const uint32_t n = std::min(cap, *rows);
+        if (host_out && n > 0) HYB_CUDA(cudaMemcpy(host_out, src, n * row * 2, cudaMemcpyDeviceToHost));
+        *rows = cap;
+        return ok();
+    });
+}
+
+HypStatus hyb_prefill_logits(HypModel model, HypKvState kv, const HypTokenStream* tokens, HypStepResult out,
+                             void* host_logits) {
+    return prefill_impl(model, kv, tokens, nullptr, out, host_logits);
+}
+
+HypStatus hyb_decode_logits(HypModel model, HypKvState kv, HypStepResult out, void* host_logits) {
+    return decode_impl(model, kv, 1, nullptr, out, host_logits, nullptr);
+}
+
+HypStatus hyb_decode_forced(HypModel model, HypKvState kv, uint32_t token, HypStepResult out, void* host_logits) {
+    return decode_impl(model, kv, 1, nullptr, out, host_logits, &token);
+}
+
+// Test hook: the next decode throws once after its first forward (host-side fault,
+// no device involvement), like the reference's post-append fault (test_fault.cc).
+HypStatus hyb_test_arm_post_append_fault(void) {
+    g_fault_armed = true;
+    return ok();
+}
+
+}  // extern "C"

@@ -1,0 +1,772 @@
+// CUDA engine: weight packing, KV state and the forward pass.
+//
+// Forward semantics follow the reference (paths inside jscott3201/hyperion):
+//   decoder layer  forward.cc:510-542     attention  forward.cc:376-508
+//   masks/kv_len   forward.cc:46-59, 345-374
+//   embed/lm_head  forward.cc:126-160     chunked prefill / decode  model.cc:574-610, 703-718
+//   caches         kv_cache.cc:161-347, kv.cc:7-96
+#include "engine.h"
+#include "safetensors.h"
+
+#include <algorithm>
+#include <atomic>
+#include <cmath>
+#include <cstring>
+#include <mutex>
+#include <stdexcept>
+
+namespace hyb {
+
+// ---------------------------------------------------------------- allocation + device info
+namespace {
+std::atomic<size_t> g_active{0};
+std::atomic<size_t> g_peak{0};
+std::mutex g_size_mu;
+std::vector<std::pair<void*, size_t>> g_sizes;  // small table: pointer -> bytes
+
+void note_alloc(void* p, size_t b) {
+    std::lock_guard<std::mutex> lk(g_size_mu);
+    g_sizes.emplace_back(p, b);
+    size_t now = g_active.fetch_add(b) + b;
+    size_t pk = g_peak.load();
+    while (now > pk && !g_peak.compare_exchange_weak(pk, now)) {
+    }
+}
+size_t note_free(void* p) {
+    std::lock_guard<std::mutex> lk(g_size_mu);
+    for (size_t i = 0; i < g_sizes.size(); ++i) {
+        if (g_sizes[i].first == p) {
+            size_t b = g_sizes[i].second;
+            g_sizes[i] = g_sizes.back();
+            g_sizes.pop_back();
+            g_active.fetch_sub(b);
+            return b;
+        }
+    }
+    return 0;
+}
+}  // namespace
+
+void* dev_alloc(size_t bytes) {
+    if (bytes == 0) return nullptr;
+    void* p = nullptr;
+    cudaError_t e = cudaMalloc(&p, bytes);
+    if (e != cudaSuccess) {
+        (void)cudaGetLastError();
+        throw std::bad_alloc();
+    }
+    note_alloc(p, bytes);
+    return p;
+}
+void dev_free(void* p) {
+    if (!p) return;
+    note_free(p);
+    cudaFree(p);
+}
+size_t dev_active_bytes() { return g_active.load(); }
+size_t dev_peak_bytes() { return g_peak.load(); }
+void dev_reset_peak() { g_peak.store(g_active.load()); }
+
+int num_sms() {
+    static int cached[64] = {0};
+    int dev = 0;
+    HYB_CUDA(cudaGetDevice(&dev));
+    if (dev < 0 || dev >= 64) dev = 0;
+    if (cached[dev] == 0) {
+        int n = 0;
+        HYB_CUDA(cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev));
+        cached[dev] = n;
+    }
+    return cached[dev];
+}
+
+// ---------------------------------------------------------------- synthetic init kernels
+namespace {
+
+__device__ __forceinline__ uint64_t mix64(uint64_t z) {
+    z += 0x9E3779B97F4A7C15ull;
+    z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+    z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+    return z ^ (z >> 31);
+}
+__device__ __forceinline__ float hash_normal(uint64_t key) {
+    const uint64_t a = mix64(key), b = mix64(key ^ 0xD1B54A32D192ED03ull);
+    const float u1 = (static_cast<float>(a >> 40) + 1.0f) * (1.0f / 16777217.0f);
+    const float u2 = static_cast<float>(b >> 40) * (1.0f / 16777216.0f);
+    return sqrtf(-2.0f * logf(u1)) * cospif(2.0f * u2);
+}
+
+__global__ void synth_words_kernel(uint32_t* w, size_t n, uint64_t seed) {
+    for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < n;
+         i += static_cast<size_t>(gridDim.x) * blockDim.x)
+        w[i] = static_cast<uint32_t>(mix64(seed * 0x100000001B3ull + i));
+}
+// scales = bf16(|N(0, std)|), biases = bf16(-8 * scales)
+__global__ void synth_sb_kernel(bf16* s, bf16* b, size_t n, uint64_t seed, float std) {
+    for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < n;
+         i += static_cast<size_t>(gridDim.x) * blockDim.x) {
+        const bf16 sv = f2bf(fabsf(std * hash_normal(seed * 0x100000001B3ull + i)));
+        s[i] = sv;
+        b[i] = f2bf(-8.0f * bf2f(sv));
+    }
+}
+// bf16(mean + std * N(0,1))
+__global__ void synth_normal_kernel(bf16* x, size_t n, uint64_t seed, float mean, float std) {
+    for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < n;
+         i += static_cast<size_t>(gridDim.x) * blockDim.x)
+        x[i] = f2bf(mean + std * hash_normal(seed * 0x100000001B3ull + i));
+}
+
+__global__ void geglu_interleaved_kernel(const bf16* __restrict__ gu, bf16* __restrict__ act, int I) {
+    const int l = blockIdx.y;
+    const bf16* row = gu + static_cast<size_t>(l) * 2 * I;
+    for (int n = blockIdx.x * blockDim.x + threadIdx.x; n < I; n += gridDim.x * blockDim.x) {
+        const int base = 32 * (n >> 4) + (n & 15);
+        const float g = bf2f(row[base]);
+        const float u = bf2f(row[base + 16]);
+        const float kC = 0.044677734375f, kK = 0.796875f;
+        float x2 = rbf(g * g), x3 = rbf(g * x2);
+        float in = rbf(kC * x3);
+        in = rbf(in + g);
+        in = rbf(kK * in);
+        float th = rbf(tanhf(in));
+        float ge = rbf(rbf(0.5f * g) * rbf(1.0f + th));
+        act[static_cast<size_t>(l) * I + n] = f2bf(ge * u);
+    }
+}
+
+int grid_for(size_t n) { return static_cast<int>(std::min<size_t>((n + 255) / 256, 4096)); }
+
+void synth_qlin(QLin& q, int N, int K, uint64_t seed, cudaStream_t st) {
+    q.N = N;
+    q.K = K;
+    q.w.reset(static_cast<size_t>(N) * K / 8);
+    q.s.reset(static_cast<size_t>(N) * K / 64);
+    q.b.reset(static_cast<size_t>(N) * K / 64);
+    synth_words_kernel<<<grid_for(q.w.n), 256, 0, st>>>(q.w.p, q.w.n, seed);
+    synth_sb_kernel<<<grid_for(q.s.n), 256, 0, st>>>(q.s.p, q.b.p, q.s.n, seed ^ 0x5151, 0.02f);
+    HYB_LAUNCH_CHECK("synth_qlin");
+}
+
+void synth_norm(DevPtr<bf16>& d, size_t n, uint64_t seed, cudaStream_t st) {
+    d.reset(n);
+    synth_normal_kernel<<<grid_for(n), 256, 0, st>>>(d.p, n, seed, 1.0f, 0.02f);
+    HYB_LAUNCH_CHECK("synth_norm");
+}
+
+// -------- checkpoint helpers
+const TensorView& expect(const Checkpoint& ck, const std::string& name, const char* dtype,
+                         std::initializer_list<int64_t> shape) {
+    const TensorView& t = ck.get(name);
+    if (t.dtype != dtype) throw std::runtime_error("tensor " + name + " has dtype " + t.dtype + ", expected " + dtype);
+    std::vector<int64_t> want(shape);
+    bool ok = t.shape == want;
+    if (!ok && want.size() == 1 && want[0] == 1 && t.shape.empty()) ok = true;  // layer_scalar [] or [1]
+    if (!ok) throw std::runtime_error("tensor " + name + " has an unexpected shape");
+    return t;
+}
+
+void upload(void* dst, const TensorView& t) { HYB_CUDA(cudaMemcpy(dst, t.data, t.nbytes, cudaMemcpyHostToDevice)); }
+
+void load_vec(DevPtr<bf16>& d, const Checkpoint& ck, const std::string& name, int64_t n) {
+    const TensorView& t = expect(ck, name, "BF16", {n});
+    d.reset(static_cast<size_t>(n));
+    upload(d.p, t);
+}
+
+}  // namespace
+
+// ---------------------------------------------------------------- Model
+Model::~Model() {
+    if (ws_.h_topk_idx) cudaFreeHost(ws_.h_topk_idx);
+    if (ws_.h_topk_val) cudaFreeHost(ws_.h_topk_val);
+    if (ws_.h_ids) cudaFreeHost(ws_.h_ids);
+    if (stream_) cudaStreamDestroy(stream_);
+}
+
+void Model::init_common(const Geometry& g) {
+    geo_ = g;
+    HYB_CUDA(cudaGetDevice(&device_));
+    if (!stream_) HYB_CUDA(cudaStreamCreateWithFlags(&stream_, cudaStreamNonBlocking));
+    auto inv_l = rope_inv_freq(g.hd_local, g.rope_local);
+    auto inv_g = rope_inv_freq(g.hd_global, g.rope_global);
+    inv_freq_local_.reset(inv_l.size());
+    inv_freq_global_.reset(inv_g.size());
+    HYB_CUDA(cudaMemcpy(inv_freq_local_.p, inv_l.data(), inv_l.size() * 4, cudaMemcpyHostToDevice));
+    HYB_CUDA(cudaMemcpy(inv_freq_global_.p, inv_g.data(), inv_g.size() * 4, cudaMemcpyHostToDevice));
+    embed_scale_ = __float2bfloat16_rn(std::sqrt(static_cast<float>(g.hidden)));
+    layers_.clear();
+    layers_.resize(g.n_layers);
+    for (uint32_t i = 0; i < g.n_layers; ++i) {
+        LayerW& L = layers_[i];
+        L.kind = g.kinds[i];
+        L.hd = static_cast<int>(g.head_dim(i));
+        L.nkv = static_cast<int>(g.n_kv(i));
+        L.q_rows = static_cast<int>(g.n_heads) * L.hd;
+        L.k_rows = L.nkv * L.hd;
+        L.v_rows = (L.kind == LayerKind::Full && g.k_eq_v_global) ? 0 : L.nkv * L.hd;
+        L.inv_freq = L.kind == LayerKind::Full ? inv_freq_global_.p : inv_freq_local_.p;
+    }
+}
+
+void Model::load_synthetic(const Geometry& g, uint64_t seed) {
+    init_common(g);
+    const int H = static_cast<int>(g.hidden), I = static_cast<int>(g.intermediate);
+    uint64_t tag = seed * 1000003ull;
+    synth_qlin(embed_, static_cast<int>(g.vocab), H, ++tag, stream_);
+    synth_norm(final_norm_, H, ++tag, stream_);
+    for (auto& L : layers_) {
+        synth_qlin(L.qkv, L.q_rows + L.k_rows + L.v_rows, H, ++tag, stream_);
+        synth_qlin(L.o, H, static_cast<int>(g.n_heads) * L.hd, ++tag, stream_);
+        synth_qlin(L.gateup, 2 * I, H, ++tag, stream_);
+        synth_qlin(L.down, H, I, ++tag, stream_);
+        synth_norm(L.q_norm, L.hd, ++tag, stream_);
+        synth_norm(L.k_norm, L.hd, ++tag, stream_);
+        synth_norm(L.in_ln, H, ++tag, stream_);
+        synth_norm(L.post_attn, H, ++tag, stream_);
+        synth_norm(L.pre_ff, H, ++tag, stream_);
+        synth_norm(L.post_ff, H, ++tag, stream_);
+        synth_norm(L.scalar, 1, ++tag, stream_);
+    }
+    HYB_CUDA(cudaStreamSynchronize(stream_));
+    loaded_ = true;
+}
+
+void Model::load_dir(const Geometry& g, const std::string& dir) {
+    Checkpoint ck(dir);
+    init_common(g);
+    const int64_t H = g.hidden, I = g.intermediate, V = g.vocab;
+    const std::string pre = "language_model.model.";
+    // tied embedding / lm_head table
+    {
+        const auto& w = expect(ck, pre + "embed_tokens.weight", "U32", {V, H / 8});
+        const auto& s = expect(ck, pre + "embed_tokens.scales", "BF16", {V, H / 64});
+        const auto& b = expect(ck, pre + "embed_tokens.biases", "BF16", {V, H / 64});
+        embed_.N = static_cast<int>(V);
+        embed_.K = static_cast<int>(H);
+        embed_.w.reset(w.nbytes / 4);
+        embed_.s.reset(s.nbytes / 2);
+        embed_.b.reset(b.nbytes / 2);
+        upload(embed_.w.p, w);
+        upload(embed_.s.p, s);
+        upload(embed_.b.p, b);
+    }
+    load_vec(final_norm_, ck, pre + "norm.weight", H);
+    for (uint32_t i = 0; i < g.n_layers; ++i) {
+        LayerW& L = layers_[i];
+        const std::string p = pre + "layers." + std::to_string(i) + ".";
+        const std::string a = p + "self_attn.";
+        const bool has_v = ck.has(a + "v_proj.weight");
+        const bool schema_sliding = has_v;
+        if ((schema_sliding ? LayerKind::Sliding : LayerKind::Full) != L.kind) {
+            throw std::runtime_error("layer " + std::to_string(i) + " weight schema (" +
+                                     (schema_sliding ? "sliding" : "global") +
+                                     ") disagrees with geometry layer_types");
+        }
+        if (!has_v) L.v_rows = 0;
+        const int64_t qkv_rows = L.q_rows + L.k_rows + L.v_rows;
+        L.qkv.N = static_cast<int>(qkv_rows);
+        L.qkv.K = static_cast<int>(H);
+        L.qkv.w.reset(static_cast<size_t>(qkv_rows) * H / 8);
+        L.qkv.s.reset(static_cast<size_t>(qkv_rows) * H / 64);
+        L.qkv.b.reset(static_cast<size_t>(qkv_rows) * H / 64);
+        int64_t row = 0;
+        auto put = [&](const std::string& base, int64_t rows) {
+            const auto& w = expect(ck, base + ".weight", "U32", {rows, H / 8});
+            const auto& s = expect(ck, base + ".scales", "BF16", {rows, H / 64});
+            const auto& b = expect(ck, base + ".biases", "BF16", {rows, H / 64});
+            upload(L.qkv.w.p + row * (H / 8), w);
+            upload(L.qkv.s.p + row * (H / 64), s);
+            upload(L.qkv.b.p + row * (H / 64), b);
+            row += rows;
+        };
+        put(a + "q_proj", L.q_rows);
+        put(a + "k_proj", L.k_rows);
+        if (has_v) put(a + "v_proj", L.v_rows);
+        {
+            const int64_t K = static_cast<int64_t>(g.n_heads) * L.hd;
+            const auto& w = expect(ck, a + "o_proj.weight", "U32", {H, K / 8});
+            const auto& s = expect(ck, a + "o_proj.scales", "BF16", {H, K / 64});
+            const auto& b = expect(ck, a + "o_proj.biases", "BF16", {H, K / 64});
+            L.o.N = static_cast<int>(H);
+            L.o.K = static_cast<int>(K);
+            L.o.w.reset(w.nbytes / 4);
+            L.o.s.reset(s.nbytes / 2);
+            L.o.b.reset(b.nbytes / 2);
+            upload(L.o.w.p, w);
+            upload(L.o.s.p, s);
+            upload(L.o.b.p, b);
+        }
+        {
+            // gate/up interleaved by 16-row tiles: tile 2t = gate rows [16t, 16t+16), 2t+1 = up rows
+            const auto& gw = expect(ck, p + "mlp.gate_proj.weight", "U32", {I, H / 8});
+            const auto& gs = expect(ck, p + "mlp.gate_proj.scales", "BF16", {I, H / 64});
+            const auto& gb = expect(ck, p + "mlp.gate_proj.biases", "BF16", {I, H / 64});
+            const auto& uw = expect(ck, p + "mlp.up_proj.weight", "U32", {I, H / 8});
+            const auto& us = expect(ck, p + "mlp.up_proj.scales", "BF16", {I, H / 64});
+            const auto& ub = expect(ck, p + "mlp.up_proj.biases", "BF16", {I, H / 64});
+            L.gateup.N = static_cast<int>(2 * I);
+            L.gateup.K = static_cast<int>(H);
+            L.gateup.w.reset(static_cast<size_t>(2 * I) * H / 8);
+            L.gateup.s.reset(static_cast<size_t>(2 * I) * H / 64);
+            L.gateup.b.reset(static_cast<size_t>(2 * I) * H / 64);
+            auto inter = [&](void* dst, const TensorView& src, size_t row_bytes, int which) {
+                HYB_CUDA(cudaMemcpy2D(static_cast<char*>(dst) + which * 16 * row_bytes, 32 * row_bytes, src.data,
+                                      16 * row_bytes, 16 * row_bytes, static_cast<size_t>(I / 16),
+                                      cudaMemcpyHostToDevice));
+            };
+            inter(L.gateup.w.p, gw, H / 2, 0);
+            inter(L.gateup.w.p, uw, H / 2, 1);
+            inter(L.gateup.s.p, gs, H / 64 * 2, 0);
+            inter(L.gateup.s.p, us, H / 64 * 2, 1);
+            inter(L.gateup.b.p, gb, H / 64 * 2, 0);
+            inter(L.gateup.b.p, ub, H / 64 * 2, 1);
+        }
+        {
+            const auto& w = expect(ck, p + "mlp.down_proj.weight", "U32", {H, I / 8});
+            const auto& s = expect(ck, p + "mlp.down_proj.scales", "BF16", {H, I / 64});
+            const auto& b = expect(ck, p + "mlp.down_proj.biases", "BF16", {H, I / 64});
+            L.down.N = static_cast<int>(H);
+            L.down.K = static_cast<int>(I);
+            L.down.w.reset(w.nbytes / 4);
+            L.down.s.reset(s.nbytes / 2);
+            L.down.b.reset(b.nbytes / 2);
+            upload(L.down.w.p, w);
+            upload(L.down.s.p, s);
+            upload(L.down.b.p, b);
+        }
+        load_vec(L.q_norm, ck, a + "q_norm.weight", L.hd);
+        load_vec(L.k_norm, ck, a + "k_norm.weight", L.hd);
+        load_vec(L.in_ln, ck, p + "input_layernorm.weight", H);
+        load_vec(L.post_attn, ck, p + "post_attention_layernorm.weight", H);
+        load_vec(L.pre_ff, ck, p + "pre_feedforward_layernorm.weight", H);
+        load_vec(L.post_ff, ck, p + "post_feedforward_layernorm.weight", H);
+        {
+            const TensorView& t = expect(ck, p + "layer_scalar", "BF16", {1});
+            L.scalar.reset(1);
+            HYB_CUDA(cudaMemcpy(L.scalar.p, t.data, 2, cudaMemcpyHostToDevice));
+        }
+    }
+    loaded_ = true;
+}
+
+std::unique_ptr<KvState> Model::new_kv() const {
+    auto kv = std::make_unique<KvState>();
+    for (uint32_t i = 0; i < geo_.n_layers; ++i) {
+        const LayerW& L = layers_[i];
+        if (L.kind == LayerKind::Sliding) {
+            LocalCache c;
+            c.nkv = L.nkv;
+            c.hd = L.hd;
+            c.cap = geo_.window + 8;  // window + gamma_max (kv_cache.h:16, kv.cc:233-235)
+            const size_t n = static_cast<size_t>(c.cap) * c.nkv * c.hd;
+            c.k.reset(n);
+            c.v.reset(n);
+            HYB_CUDA(cudaMemsetAsync(c.k.p, 0, n * 2, stream_));
+            HYB_CUDA(cudaMemsetAsync(c.v.p, 0, n * 2, stream_));
+            kv->local.push_back(std::move(c));
+        } else {
+            GlobalCache c;
+            c.nkv = L.nkv;
+            c.hd = L.hd;
+            kv->global.push_back(std::move(c));
+        }
+    }
+    HYB_CUDA(cudaStreamSynchronize(stream_));
+    return kv;
+}
+
+void Model::reserve(KvState& kv, uint32_t n_tokens) const {
+    for (auto& c : kv.global) {
+        const uint64_t need_tokens = static_cast<uint64_t>(c.committed) + n_tokens;
+        const uint64_t need = (need_tokens + 255) / 256 * 256;
+        if (need > 0xFFFFFFFFull) throw std::overflow_error("KV operation exceeds representable cache dimensions");
+        if (need <= c.capacity) continue;
+        const size_t row = static_cast<size_t>(c.nkv) * c.hd;
+        DevPtr<bf16> nk(need * row), nv(need * row);
+        HYB_CUDA(cudaMemsetAsync(nk.p, 0, need * row * 2, stream_));
+        HYB_CUDA(cudaMemsetAsync(nv.p, 0, need * row * 2, stream_));
+        if (c.capacity > 0) {
+            HYB_CUDA(cudaMemcpyAsync(nk.p, c.k.p, static_cast<size_t>(c.capacity) * row * 2, cudaMemcpyDeviceToDevice, stream_));
+            HYB_CUDA(cudaMemcpyAsync(nv.p, c.v.p, static_cast<size_t>(c.capacity) * row * 2, cudaMemcpyDeviceToDevice, stream_));
+        }
+        HYB_CUDA(cudaStreamSynchronize(stream_));
+        c.k = std::move(nk);
+        c.v = std::move(nv);
+        c.capacity = static_cast<uint32_t>(need);
+    }
+}
+
+uint64_t Model::local_kv_bytes(const KvState& kv) const {
+    uint64_t b = 0;
+    for (const auto& c : kv.local) b += static_cast<uint64_t>(c.cap) * c.nkv * c.hd * 2 * 2;
+    return b;
+}
+uint64_t Model::global_kv_bytes(const KvState& kv) const {
+    uint64_t b = 0;
+    for (const auto& c : kv.global) b += static_cast<uint64_t>(c.capacity) * c.nkv * c.hd * 2 * 2;
+    return b;
+}
+
+void Model::ensure_workspace(int tokens, uint32_t max_keys) {
+    const Geometry& g = geo_;
+    const int H = static_cast<int>(g.hidden), I = static_cast<int>(g.intermediate);
+    int max_qkv = 0, max_attn = 0, max_kv_row = 0, max_hd = 0;
+    for (const auto& L : layers_) {
+        max_qkv = std::max(max_qkv, L.q_rows + L.k_rows + L.v_rows);
+        max_attn = std::max(max_attn, L.q_rows);
+        max_kv_row = std::max(max_kv_row, L.nkv * L.hd);
+        max_hd = std::max(max_hd, L.hd);
+    }
+    if (tokens > ws_.chunk_cap) {
+        const size_t C = static_cast<size_t>(tokens);
+        ws_.h_a.reset(C * H);
+        ws_.h_b.reset(C * H);
+        ws_.h_e.reset(C * H);
+        ws_.xn.reset(C * H);
+        ws_.qkv.reset(C * max_qkv);
+        ws_.q.reset(C * max_attn);
+        ws_.attn.reset(C * max_attn);
+        ws_.o.reset(C * H);
+        ws_.gu.reset(C * 2 * I);
+        ws_.act.reset(C * I);
+        ws_.dn.reset(C * H);
+        ws_.ids.reset(C);
+        // keys of one attention call: trailing window prefix + chunk (local) or the
+        // chunk itself at offset 0
+        const size_t kv_rows = C + g.window;
+        ws_.kbuf.reset(kv_rows * max_kv_row);
+        ws_.vbuf.reset(kv_rows * max_kv_row);
+        ws_.chunk_cap = tokens;
+        if (ws_.h_ids) cudaFreeHost(ws_.h_ids);
+        HYB_CUDA(cudaMallocHost(&ws_.h_ids, C * sizeof(uint32_t)));
+        ws_.h_ids_cap = tokens;
+    }
+    if (ws_.logits.n == 0) {
+        ws_.logits.reset(g.vocab);
+        const int tsf = softcap_topk_scratch_floats(static_cast<int>(g.vocab));
+        ws_.topk_scratch.reset(tsf);
+        ws_.topk_idx.reset(8);
+        ws_.topk_val.reset(8);
+        HYB_CUDA(cudaMallocHost(&ws_.h_topk_idx, 8 * sizeof(uint32_t)));
+        HYB_CUDA(cudaMallocHost(&ws_.h_topk_val, 8 * sizeof(float)));
+    }
+    size_t need = 0;
+    for (const auto& L : layers_)
+        need = std::max(need, decode_attn_scratch_bytes(static_cast<int>(g.n_heads), L.nkv, L.hd,
+                                                        static_cast<int>(std::max<uint32_t>(max_keys, 1))));
+    if (need > ws_.attn_scratch_bytes) {
+        // grow geometrically so decode does not reallocate every 256 tokens
+        size_t target = std::max(need, ws_.attn_scratch_bytes * 2);
+        ws_.attn_scratch.reset(target);
+        HYB_CUDA(cudaMemsetAsync(ws_.attn_scratch.p, 0, target, stream_));
+        ws_.attn_scratch_bytes = target;
+    }
+}
+
+void Model::forward_chunk(KvState& kv, int L, uint32_t offset) {
+    const Geometry& g = geo_;
+    const int H = static_cast<int>(g.hidden), I = static_cast<int>(g.intermediate);
+    const int nh = static_cast<int>(g.n_heads);
+    cudaStream_t st = stream_;
+    bf16* h_cur = ws_.h_a.p;
+    bf16* h_alt = ws_.h_b.p;
+    launch_embed(ws_.ids.p, L, embed_.w.p, embed_.s.p, embed_.b.p, H, embed_scale_, h_cur, st);
+    launch_rms_norm(h_cur, layers_[0].in_ln.p, ws_.xn.p, L, H, g.eps, st);
+    size_t li = 0, gi = 0;
+    for (uint32_t layer = 0; layer < g.n_layers; ++layer) {
+        LayerW& W = layers_[layer];
+        const int hd = W.hd, nkv = W.nkv;
+        const int qkv_ld = W.q_rows + W.k_rows + W.v_rows;
+        launch_quantized_matmul(ws_.xn.p, W.qkv.w.p, W.qkv.s.p, W.qkv.b.p, ws_.qkv.p, L, H, qkv_ld, st);
+        const uint32_t committed = offset + static_cast<uint32_t>(L);
+        QkvPostParams qp;
+        qp.qkv = ws_.qkv.p;
+        qp.L = L;
+        qp.ld = qkv_ld;
+        qp.n_heads = nh;
+        qp.n_kv = nkv;
+        qp.hd = hd;
+        qp.v_from_k = W.v_rows == 0;
+        qp.q_norm = W.q_norm.p;
+        qp.k_norm = W.k_norm.p;
+        qp.inv_freq = W.inv_freq;
+        qp.pos0 = static_cast<int>(offset);
+        qp.eps = g.eps;
+        qp.q_out = ws_.q.p;
+        PrefillAttnParams ap;
+        ap.q = ws_.q.p;
+        ap.out = ws_.attn.p;
+        ap.Lq = L;
+        ap.n_heads = nh;
+        ap.n_kv = nkv;
+        ap.hd = hd;
+        ap.q_pos0 = static_cast<int>(offset);
+        ap.scale = 1.0f;
+        const size_t row = static_cast<size_t>(nkv) * hd;
+        if (W.kind == LayerKind::Sliding) {
+            LocalCache& c = kv.local[li++];
+            // continuation: gather the committed trailing window BEFORE the append
+            // (forward.cc:444-457); the chunk's own K/V follow it contiguously
+            const uint32_t pre = offset > 0 ? std::min(g.window, offset) : 0;
+            if (pre > 0) {
+                launch_gather_ring(c.k.p, static_cast<int>(c.cap), static_cast<int>(offset - pre), static_cast<int>(pre),
+                                   static_cast<int>(row), ws_.kbuf.p, st);
+                launch_gather_ring(c.v.p, static_cast<int>(c.cap), static_cast<int>(offset - pre), static_cast<int>(pre),
+                                   static_cast<int>(row), ws_.vbuf.p, st);
+            }
+            qp.k_out = ws_.kbuf.p + pre * row;
+            qp.v_out = ws_.vbuf.p + pre * row;
+            qp.k_cache = c.k.p;
+            qp.v_cache = c.v.p;
+            qp.cache_cap = static_cast<int>(c.cap);
+            // a chunk longer than the ring leaves only its last `cap` tokens resident
+            qp.cache_first = std::max(0, L - static_cast<int>(c.cap));
+            launch_qkv_post(qp, st);
+            c.committed = committed;
+            ap.k = ws_.kbuf.p;
+            ap.v = ws_.vbuf.p;
+            ap.Lk = static_cast<int>(pre) + L;
+            ap.k_pos0 = static_cast<int>(offset - pre);
+            ap.window = static_cast<int>(g.window);
+        } else {
+            GlobalCache& c = kv.global[gi++];
+            if (c.capacity < committed) throw std::runtime_error("global cache not reserved");
+            qp.k_cache = c.k.p;
+            qp.v_cache = c.v.p;
+            qp.cache_cap = static_cast<int>(c.capacity);
+            qp.cache_first = 0;
+            launch_qkv_post(qp, st);
+            c.committed = committed;
+            ap.k = c.k.p;
+            ap.v = c.v.p;
+            ap.Lk = static_cast<int>(committed);
+            ap.k_pos0 = 0;
+            ap.window = 0;
+        }
+        launch_prefill_attn(ap, st);
+        launch_quantized_matmul(ws_.attn.p, W.o.w.p, W.o.s.p, W.o.b.p, ws_.o.p, L, W.o.K, H, st);
+        launch_resid_norm(ws_.o.p, W.post_attn.p, h_cur, nullptr, h_alt, W.pre_ff.p, ws_.xn.p, L, H, g.eps, st);
+        launch_quantized_matmul(ws_.xn.p, W.gateup.w.p, W.gateup.s.p, W.gateup.b.p, ws_.gu.p, L, H, 2 * I, st);
+        {
+            dim3 grid(std::min((I + 255) / 256, 64), L);
+            geglu_interleaved_kernel<<<grid, 256, 0, st>>>(ws_.gu.p, ws_.act.p, I);
+            HYB_LAUNCH_CHECK("geglu_interleaved_kernel");
+        }
+        launch_quantized_matmul(ws_.act.p, W.down.w.p, W.down.s.p, W.down.b.p, ws_.dn.p, L, I, H, st);
+        const bf16* next_w = (layer + 1 < g.n_layers) ? layers_[layer + 1].in_ln.p : final_norm_.p;
+        launch_resid_norm(ws_.dn.p, W.post_ff.p, h_alt, W.scalar.p, h_cur, next_w, ws_.xn.p, L, H, g.eps, st);
+    }
+}
+
+StepOut Model::epilogue(const bf16* final_row, bool fused_prologue, const bf16* dn, const bf16* resid,
+                        std::vector<uint16_t>* logits_out) {
+    const Geometry& g = geo_;
+    QmvParams p;
+    p.w = embed_.w.p;
+    p.s = embed_.s.p;
+    p.b = embed_.b.p;
+    p.y = ws_.logits.p;
+    p.K = static_cast<int>(g.hidden);
+    p.N = static_cast<int>(g.vocab);
+    p.eps = g.eps;
+    if (fused_prologue) {
+        const LayerW& last = layers_.back();
+        p.prologue = QmvPrologue::kResidNorm;
+        p.x = dn;
+        p.resid = resid;
+        p.post_w = last.post_ff.p;
+        p.scalar = last.scalar.p;
+        p.norm_w = final_norm_.p;
+        p.h_out = ws_.h_a.p;
+    } else {
+        p.x = final_row;
+    }
+    launch_qmv(p, stream_, fused_prologue);
+    launch_softcap_topk(ws_.logits.p, static_cast<int>(g.vocab), g.softcap, ws_.topk_scratch.p,
+                        static_cast<int>(ws_.topk_scratch.n), ws_.topk_idx.p, ws_.topk_val.p, stream_);
+    HYB_CUDA(cudaMemcpyAsync(ws_.h_topk_idx, ws_.topk_idx.p, 8 * sizeof(uint32_t), cudaMemcpyDeviceToHost, stream_));
+    HYB_CUDA(cudaMemcpyAsync(ws_.h_topk_val, ws_.topk_val.p, 8 * sizeof(float), cudaMemcpyDeviceToHost, stream_));
+    if (logits_out) {
+        logits_out->resize(g.vocab);
+        HYB_CUDA(cudaMemcpyAsync(logits_out->data(), ws_.logits.p, static_cast<size_t>(g.vocab) * 2,
+                                 cudaMemcpyDeviceToHost, stream_));
+    }
+    HYB_CUDA(cudaStreamSynchronize(stream_));
+    StepOut out;
+    const int n = static_cast<int>(std::min<uint32_t>(8, g.vocab));
+    for (int i = 0; i < n; ++i) {
+        out.topk_idx[i] = ws_.h_topk_idx[i];
+        out.topk_val[i] = ws_.h_topk_val[i];
+    }
+    out.token = out.topk_idx[0];
+    out.logit = out.topk_val[0];
+    const float top2 = n > 1 ? out.topk_val[1] : -INFINITY;
+    out.near_tie = (out.logit - top2) < 0.5f;
+    return out;
+}
+
+StepOut Model::prefill(KvState& kv, const uint32_t* tokens, uint32_t count, std::vector<uint16_t>* logits_out) {
+    constexpr uint32_t kChunk = 2048;  // model.cc:574
+    const uint32_t first = std::min(kChunk, count);
+    ensure_workspace(static_cast<int>(first), std::min<uint32_t>(count, 32768));
+    reserve(kv, count);
+    uint32_t off = 0;
+    while (off < count) {
+        const uint32_t take = std::min(kChunk, count - off);
+        std::memcpy(ws_.h_ids, tokens + off, take * sizeof(uint32_t));
+        HYB_CUDA(cudaMemcpyAsync(ws_.ids.p, ws_.h_ids, take * sizeof(uint32_t), cudaMemcpyHostToDevice, stream_));
+        forward_chunk(kv, static_cast<int>(take), off);
+        off += take;
+        if (off < count) HYB_CUDA(cudaStreamSynchronize(stream_));  // h_ids is reused
+        else {
+            // lm_head on the last row only: rows are independent (forward.cc:137-152)
+            const bf16* last = ws_.xn.p + static_cast<size_t>(take - 1) * geo_.hidden;
+            StepOut o = epilogue(last, false, nullptr, nullptr, logits_out);
+            kv.offset = count;
+            kv.last_token = o.token;
+            return o;
+        }
+    }
+    throw std::logic_error("prefill: empty prompt");
+}
+
+void Model::decode_layers(KvState& kv) {
+    const Geometry& g = geo_;
+    const int H = static_cast<int>(g.hidden);
+    const int nh = static_cast<int>(g.n_heads);
+    cudaStream_t st = stream_;
+    const uint32_t pos = kv.offset;  // position of the token being decoded
+    launch_embed(ws_.ids.p, 1, embed_.w.p, embed_.s.p, embed_.b.p, H, embed_scale_, ws_.h_e.p, st);
+    const bf16* resid = ws_.h_e.p;  // residual entering the current layer's attention block
+    size_t li = 0, gi = 0;
+    for (uint32_t layer = 0; layer < g.n_layers; ++layer) {
+        LayerW& W = layers_[layer];
+        const int qkv_rows = W.q_rows + W.k_rows + W.v_rows;
+        // qkv projection with the layer's input norm (and the previous layer's
+        // post-MLP residual/scalar) fused into its prologue
+        QmvParams p;
+        p.w = W.qkv.w.p;
+        p.s = W.qkv.s.p;
+        p.b = W.qkv.b.p;
+        p.y = ws_.qkv.p;
+        p.K = H;
+        p.N = qkv_rows;
+        p.eps = g.eps;
+        p.norm_w = W.in_ln.p;
+        if (layer == 0) {
+            p.prologue = QmvPrologue::kNorm;
+            p.x = ws_.h_e.p;
+        } else {
+            const LayerW& P = layers_[layer - 1];
+            p.prologue = QmvPrologue::kResidNorm;
+            p.x = ws_.dn.p;
+            p.resid = ws_.h_b.p;
+            p.post_w = P.post_ff.p;
+            p.scalar = P.scalar.p;
+            p.h_out = ws_.h_a.p;
+            resid = ws_.h_a.p;
+        }
+        launch_qmv(p, st, true);
+        QkvPostParams qp;
+        qp.qkv = ws_.qkv.p;
+        qp.L = 1;
+        qp.ld = qkv_rows;
+        qp.n_heads = nh;
+        qp.n_kv = W.nkv;
+        qp.hd = W.hd;
+        qp.v_from_k = W.v_rows == 0;
+        qp.q_norm = W.q_norm.p;
+        qp.k_norm = W.k_norm.p;
+        qp.inv_freq = W.inv_freq;
+        qp.pos0 = static_cast<int>(pos);
+        qp.eps = g.eps;
+        qp.q_out = ws_.q.p;
+        DecodeAttnParams ap;
+        ap.q = ws_.q.p;
+        ap.out = ws_.attn.p;
+        ap.n_heads = nh;
+        ap.n_kv = W.nkv;
+        ap.hd = W.hd;
+        ap.last_pos = static_cast<int>(pos);
+        ap.scratch = ws_.attn_scratch.p;
+        ap.scratch_bytes = ws_.attn_scratch_bytes;
+        if (W.kind == LayerKind::Sliding) {
+            LocalCache& c = kv.local[li++];
+            qp.k_cache = c.k.p;
+            qp.v_cache = c.v.p;
+            qp.cache_cap = static_cast<int>(c.cap);
+            launch_qkv_post(qp, st);
+            c.committed = pos + 1;
+            ap.k_cache = c.k.p;
+            ap.v_cache = c.v.p;
+            ap.cap = static_cast<int>(c.cap);
+            ap.n_keys = static_cast<int>(std::min(g.window, pos + 1));  // forward.cc:55-57
+        } else {
+            GlobalCache& c = kv.global[gi++];
+            if (c.capacity < pos + 1) throw std::runtime_error("global cache not reserved");
+            qp.k_cache = c.k.p;
+            qp.v_cache = c.v.p;
+            qp.cache_cap = static_cast<int>(c.capacity);
+            launch_qkv_post(qp, st);
+            c.committed = pos + 1;
+            ap.k_cache = c.k.p;
+            ap.v_cache = c.v.p;
+            ap.cap = static_cast<int>(c.capacity);
+            ap.n_keys = static_cast<int>(pos + 1);
+        }
+        launch_decode_attn(ap, st);
+        QmvParams po;
+        po.w = W.o.w.p;
+        po.s = W.o.s.p;
+        po.b = W.o.b.p;
+        po.x = ws_.attn.p;
+        po.y = ws_.o.p;
+        po.K = W.o.K;
+        po.N = H;
+        launch_qmv(po, st, false);
+        // gate/up with the post-attention residual + pre-MLP norm in the prologue
+        // and GeGLU in the epilogue
+        QmvParams pg;
+        pg.w = W.gateup.w.p;
+        pg.s = W.gateup.s.p;
+        pg.b = W.gateup.b.p;
+        pg.x = ws_.o.p;
+        pg.y = ws_.act.p;
+        pg.K = H;
+        pg.N = W.gateup.N;
+        pg.prologue = QmvPrologue::kResidNorm;
+        pg.epilogue = QmvEpilogue::kGeglu;
+        pg.resid = resid;
+        pg.post_w = W.post_attn.p;
+        pg.scalar = nullptr;
+        pg.norm_w = W.pre_ff.p;
+        pg.h_out = ws_.h_b.p;
+        pg.eps = g.eps;
+        launch_qmv(pg, st, true);
+        QmvParams pd;
+        pd.w = W.down.w.p;
+        pd.s = W.down.s.p;
+        pd.b = W.down.b.p;
+        pd.x = ws_.act.p;
+        pd.y = ws_.dn.p;
+        pd.K = W.down.K;
+        pd.N = H;
+        launch_qmv(pd, st, true);
+    }
+}
+
+StepOut Model::decode_step(KvState& kv, std::vector<uint16_t>* logits_out) {
+    ensure_workspace(1, std::min<uint32_t>(kv.offset + 1, 32768));
+    if (kv.offset + 1 > 32768) throw std::runtime_error("decode beyond 32768 tokens is not supported");
+    reserve(kv, 1);
+    ws_.h_ids[0] = kv.last_token;
+    HYB_CUDA(cudaMemcpyAsync(ws_.ids.p, ws_.h_ids, sizeof(uint32_t), cudaMemcpyHostToDevice, stream_));
+    decode_layers(kv);
+    StepOut o = epilogue(nullptr, true, ws_.dn.p, ws_.h_b.p, logits_out);
+    kv.offset += 1;
+    kv.last_token = o.token;
+    return o;
+}
+
+}  // namespace hyb

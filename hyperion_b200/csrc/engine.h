@@ -1,0 +1,166 @@
+// The CUDA engine behind the hyperion_mlx.h ABI: device-resident weights, the
+// per-sequence KV state and the prefill/decode forward pass.
+//
+// Mirrors the reference engine's structure (native/hyperion_mlx/src/model.cc,
+// forward.cc, kv_cache.cc) with B200-first data layouts:
+//   * q/k/v projections of a layer are fused into one packed [Nq+Nk+Nv, K/8]
+//     matrix (one decode launch instead of three);
+//   * gate/up are interleaved by 16-row tiles so one decode CTA produces both
+//     halves of GeGLU and applies it in its epilogue;
+//   * norms ride in the prologue of the next projection in decode;
+//   * local KV rings are [window + 8, nkv, hd] bf16 (slot = pos % cap) and global
+//     caches grow in 256-token steps, as in the reference.
+#pragma once
+
+#include "common.cuh"
+#include "geometry.h"
+#include "kernels.h"
+
+#include <cstdint>
+#include <memory>
+#include <string>
+#include <vector>
+
+namespace hyb {
+
+// Device allocation with a process-wide byte counter (telemetry).
+void* dev_alloc(size_t bytes);
+void dev_free(void* p);
+size_t dev_active_bytes();
+size_t dev_peak_bytes();
+void dev_reset_peak();
+
+template <typename T>
+struct DevPtr {
+    T* p = nullptr;
+    size_t n = 0;
+    DevPtr() = default;
+    explicit DevPtr(size_t count) : p(static_cast<T*>(dev_alloc(count * sizeof(T)))), n(count) {}
+    ~DevPtr() { dev_free(p); }
+    DevPtr(const DevPtr&) = delete;
+    DevPtr& operator=(const DevPtr&) = delete;
+    DevPtr(DevPtr&& o) noexcept : p(o.p), n(o.n) { o.p = nullptr; o.n = 0; }
+    DevPtr& operator=(DevPtr&& o) noexcept {
+        if (this != &o) {
+            dev_free(p);
+            p = o.p;
+            n = o.n;
+            o.p = nullptr;
+            o.n = 0;
+        }
+        return *this;
+    }
+    void reset(size_t count) { *this = DevPtr<T>(count); }
+};
+
+struct QLin {
+    DevPtr<uint32_t> w;
+    DevPtr<bf16> s, b;
+    int N = 0, K = 0;
+};
+
+struct LayerW {
+    LayerKind kind = LayerKind::Sliding;
+    int hd = 0, nkv = 0;
+    int q_rows = 0, k_rows = 0, v_rows = 0;  // row split of the fused qkv matrix
+    QLin qkv, o, gateup, down;               // gateup: interleaved 16-row tiles (gate, up)
+    DevPtr<bf16> q_norm, k_norm, in_ln, post_attn, pre_ff, post_ff, scalar;
+    float* inv_freq = nullptr;               // points into Model::inv_freq_*
+};
+
+struct LocalCache {
+    DevPtr<bf16> k, v;
+    uint32_t cap = 0, committed = 0;
+    int nkv = 0, hd = 0;
+};
+
+struct GlobalCache {
+    DevPtr<bf16> k, v;
+    uint32_t capacity = 0, committed = 0;
+    int nkv = 0, hd = 0;
+};
+
+struct KvState {
+    std::vector<LocalCache> local;
+    std::vector<GlobalCache> global;
+    uint32_t offset = 0;
+    uint32_t last_token = 0;
+    bool poisoned = false;
+};
+
+struct StepOut {
+    uint32_t token = 0;
+    float logit = 0.f;
+    bool near_tie = false;
+    uint32_t topk_idx[8] = {};
+    float topk_val[8] = {};
+};
+
+struct Workspace {
+    int chunk_cap = 0;  // max tokens per forward
+    DevPtr<bf16> h_a, h_b, h_e, xn, qkv, q, kbuf, vbuf, attn, o, gu, act, dn, logits;
+    DevPtr<uint32_t> ids;
+    DevPtr<float> topk_scratch;
+    DevPtr<uint32_t> topk_idx;
+    DevPtr<float> topk_val;
+    DevPtr<unsigned char> attn_scratch;
+    size_t attn_scratch_bytes = 0;
+    uint32_t* h_topk_idx = nullptr;  // pinned host mirrors
+    float* h_topk_val = nullptr;
+    uint32_t* h_ids = nullptr;
+    int h_ids_cap = 0;
+};
+
+class Model {
+  public:
+    Model() = default;
+    ~Model();
+
+    // Load from a directory of *.safetensors (mlx-lm converted names).
+    void load_dir(const Geometry& g, const std::string& dir);
+    // Fill every tensor with seeded synthetic values on the device (benchmarks).
+    void load_synthetic(const Geometry& g, uint64_t seed);
+
+    std::unique_ptr<KvState> new_kv() const;
+    // Grow global caches so that `n_tokens` more tokens fit (reference
+    // plan_kv_growth / GlobalKvCache::append semantics: 256-token steps).
+    void reserve(KvState& kv, uint32_t n_tokens) const;
+
+    // Prefill a prompt on a fresh state; returns the greedy sample of the last row.
+    StepOut prefill(KvState& kv, const uint32_t* tokens, uint32_t count, std::vector<uint16_t>* logits_out);
+    // One decode step at kv.offset from kv.last_token.
+    StepOut decode_step(KvState& kv, std::vector<uint16_t>* logits_out);
+
+    uint64_t local_kv_bytes(const KvState& kv) const;
+    uint64_t global_kv_bytes(const KvState& kv) const;
+
+    const Geometry& geometry() const { return geo_; }
+    cudaStream_t stream() const { return stream_; }
+    int device() const { return device_; }
+    bool loaded() const { return loaded_; }
+
+    // Exposed for tests/benchmarks through the extension ABI.
+    LayerW& layer(int i) { return layers_[i]; }
+    QLin& embed() { return embed_; }
+
+  private:
+    void init_common(const Geometry& g);
+    void ensure_workspace(int tokens, uint32_t max_keys);
+    void forward_chunk(KvState& kv, int L, uint32_t offset);  // ids already in ws_.ids
+    void decode_layers(KvState& kv);
+    StepOut epilogue(const bf16* final_row, bool fused_prologue, const bf16* dn, const bf16* resid,
+                     std::vector<uint16_t>* logits_out);
+
+    Geometry geo_;
+    bool loaded_ = false;
+    int device_ = 0;
+    cudaStream_t stream_ = nullptr;
+    std::vector<LayerW> layers_;
+    QLin embed_;
+    DevPtr<bf16> final_norm_;
+    DevPtr<float> inv_freq_local_, inv_freq_global_;
+    bf16 embed_scale_{};
+    Workspace ws_;
+};
+
+}  // namespace hyb

@@ -1,0 +1,147 @@
+// Host-side launch interface of every sm_100a kernel in this library.
+//
+// All pointers are device pointers; all tensors are dense row-major. bf16
+// values travel as __nv_bfloat16. Every launcher enqueues on `stream` and
+// throws hyb::CudaError on a launch failure.
+#pragma once
+
+#include "common.cuh"
+
+namespace hyb {
+
+// ---------------------------------------------------------------- quantized matmul
+// Affine Q4/g64: y[m, n] = sum_k x[m, k] * (s[n, k/64] * q[n, k] + b[n, k/64]),
+// q[n, 8j+i] = bits [4i, 4i+4) of w[n, j]. x bf16 [M, K], w u32 [N, K/8],
+// s/b bf16 [N, K/64], y bf16 [M, N]. K must be a multiple of 64.
+
+// Prologue applied to the activation before the batch-1 qmv.
+enum class QmvPrologue : int {
+    kNone = 0,       // x is used as given
+    kNorm = 1,       // x <- rms_norm(x, norm_w)
+    kResidNorm = 2,  // h = resid + rms_norm(x, post_w) [* scalar]; written to h_out by CTA 0;
+                     // x <- rms_norm(h, norm_w)
+};
+// Epilogue of the batch-1 qmv.
+enum class QmvEpilogue : int {
+    kStore = 0,   // y[n] = bf16(acc)
+    kGeglu = 1,   // rows are (gate, up) interleaved by 16-row tiles: y[n] = bf16(gelu(g) * u)
+};
+
+struct QmvParams {
+    const bf16* x = nullptr;          // [K] activation (or the branch output for kResidNorm)
+    const uint32_t* w = nullptr;      // [N, K/8]
+    const bf16* s = nullptr;          // [N, K/64]
+    const bf16* b = nullptr;          // [N, K/64]
+    bf16* y = nullptr;                // [N] (or [N/2] for kGeglu)
+    int K = 0;
+    int N = 0;
+    QmvPrologue prologue = QmvPrologue::kNone;
+    QmvEpilogue epilogue = QmvEpilogue::kStore;
+    // prologue operands
+    const bf16* norm_w = nullptr;     // [K] weight of the final norm in the prologue
+    const bf16* resid = nullptr;      // [K] residual stream (kResidNorm)
+    const bf16* post_w = nullptr;     // [K] norm applied to x before the residual add
+    const bf16* scalar = nullptr;     // [1] layer_scalar multiplied after the add, or null
+    bf16* h_out = nullptr;            // [K] new residual, written by CTA 0
+    float eps = 1e-6f;
+};
+
+void launch_qmv(const QmvParams& p, cudaStream_t stream, bool pdl = false);
+
+// Prefill GEMM for M >= 2 (tensor cores; fp16 operands, fp32 accumulation).
+void launch_qmm(const bf16* x, const uint32_t* w, const bf16* s, const bf16* b, bf16* y,
+                int M, int K, int N, cudaStream_t stream);
+
+// Dispatcher used by the op-level ABI: qmv for M == 1, qmm otherwise.
+void launch_quantized_matmul(const bf16* x, const uint32_t* w, const bf16* s, const bf16* b,
+                             bf16* y, int M, int K, int N, cudaStream_t stream);
+
+// ---------------------------------------------------------------- elementwise / norms
+// out[l, :] = bf16(bf16(s*q + b) * embed_scale) for ids[l] rows of the packed table.
+void launch_embed(const uint32_t* ids, int L, const uint32_t* w, const bf16* s, const bf16* b,
+                  int H, bf16 embed_scale, bf16* out, cudaStream_t stream);
+
+// Row-wise RMSNorm: out = bf16(bf16(x * inv) * w) (w may be null), rows of length D.
+void launch_rms_norm(const bf16* x, const bf16* w, bf16* out, int rows, int D, float eps,
+                     cudaStream_t stream);
+
+// h = bf16(resid + norm(x, post_w)); h = bf16(h * scalar) if scalar; out_h = h;
+// out_n = norm(h, next_w) if next_w.
+void launch_resid_norm(const bf16* x, const bf16* post_w, const bf16* resid,
+                       const bf16* scalar, bf16* out_h, const bf16* next_w, bf16* out_n,
+                       int rows, int D, float eps, cudaStream_t stream);
+
+// act[l, n] = bf16(gelu_tanh(gate[l, n]) * up[l, n]) with the reference's bf16 op rounding.
+void launch_geglu(const bf16* gate, const bf16* up, bf16* act, int rows, int N, int ld_in,
+                  cudaStream_t stream);
+
+// Per token l and head: QK-norm (q/k with weights, v without), RoPE on q and k at
+// position pos0 + l, and the cache writes. qkv is [L, ld] with q at column 0,
+// k at q_cols, v at q_cols + kv_cols (v_from_k: v reads the k columns).
+struct QkvPostParams {
+    const bf16* qkv = nullptr;
+    int L = 0, ld = 0;
+    int n_heads = 0, n_kv = 0, hd = 0;
+    bool v_from_k = false;
+    const bf16* q_norm = nullptr;
+    const bf16* k_norm = nullptr;
+    const float* inv_freq = nullptr;   // [hd/2], 0 = identity pair
+    int pos0 = 0;
+    float eps = 1e-6f;
+    bf16* q_out = nullptr;             // [L, n_heads, hd]
+    bf16* k_out = nullptr;             // optional contiguous [L, n_kv, hd]
+    bf16* v_out = nullptr;
+    bf16* k_cache = nullptr;           // optional [cap, n_kv, hd]; slot = (pos0 + l) % cap
+    bf16* v_cache = nullptr;
+    int cache_cap = 0;
+    int cache_first = 0;               // only tokens l >= cache_first are written to the cache
+};
+void launch_qkv_post(const QkvPostParams& p, cudaStream_t stream);
+
+// Gather cache rows for positions [pos0, pos0 + n) (slot = pos % cap) into dst [n, n_kv, hd].
+void launch_gather_ring(const bf16* cache, int cap, int pos0, int n, int row_elems, bf16* dst,
+                        cudaStream_t stream);
+
+// logits -> bf16 softcap (cap > 0) in place, then per-block top candidates for argmax/top-k.
+// Final result: idx/val of the TOPK largest (first index wins ties), plus top2 for near-tie.
+void launch_softcap_topk(bf16* logits, int N, float cap, float* scratch, int scratch_floats,
+                         uint32_t* out_idx, float* out_val, cudaStream_t stream);
+int softcap_topk_scratch_floats(int N);
+
+// ---------------------------------------------------------------- attention
+// Decode (one query token): q [H, hd]; caches [cap, Hkv, hd]; keys are the last
+// n_keys committed positions ending at `last_pos` (slot = pos % cap).
+struct DecodeAttnParams {
+    const bf16* q = nullptr;
+    const bf16* k_cache = nullptr;
+    const bf16* v_cache = nullptr;
+    bf16* out = nullptr;       // [H, hd]
+    int n_heads = 0, n_kv = 0, hd = 0;
+    int cap = 0;
+    int last_pos = 0;          // absolute position of the query (the newest key)
+    int n_keys = 0;            // keys at positions last_pos - n_keys + 1 .. last_pos
+    float scale = 1.0f;
+    float softcap = 0.0f;
+    int rounding = 0;          // 0: MLX CPU-stream (bf16 scores and probabilities), 1: none
+    void* scratch = nullptr;
+    size_t scratch_bytes = 0;
+};
+size_t decode_attn_scratch_bytes(int n_heads, int n_kv, int hd, int max_keys);
+void launch_decode_attn(const DecodeAttnParams& p, cudaStream_t stream);
+
+// Prefill: q [Lq, H, hd] at positions q_pos0 + i; k/v [Lk, Hkv, hd] at k_pos0 + j.
+struct PrefillAttnParams {
+    const bf16* q = nullptr;
+    const bf16* k = nullptr;
+    const bf16* v = nullptr;
+    bf16* out = nullptr;
+    int Lq = 0, Lk = 0, n_heads = 0, n_kv = 0, hd = 0;
+    int q_pos0 = 0, k_pos0 = 0;
+    int window = 0;            // 0 = full causal
+    float scale = 1.0f;
+    float softcap = 0.0f;
+    int rounding = 0;
+};
+void launch_prefill_attn(const PrefillAttnParams& p, cudaStream_t stream);
+
+}  // namespace hyb

@@ -1,0 +1,174 @@
+// Op-level C entry points (include/hyperion_b200.h): each hot-path kernel behind
+// plain pointers, sizes and a stream, with the library's status/error contract.
+#include "hyperion_b200.h"
+#include "kernels.h"
+
+#include <cstdio>
+#include <exception>
+#include <string>
+
+namespace hyb {
+HypStatus abi_fail(HypStatus s, const char* msg) noexcept;
+HypStatus abi_ok() noexcept;
+}  // namespace hyb
+
+namespace {
+
+template <typename Fn>
+HypStatus run(Fn&& fn) noexcept {
+    try {
+        fn();
+        return hyb::abi_ok();
+    } catch (const hyb::ArgError& e) {
+        return hyb::abi_fail(HYP_STATUS_INVALID_ARGUMENT, e.what());
+    } catch (const hyb::CudaError& e) {
+        return hyb::abi_fail(HYP_STATUS_INTERNAL, e.what());
+    } catch (const std::exception& e) {
+        return hyb::abi_fail(HYP_STATUS_INTERNAL, e.what());
+    } catch (...) {
+        return hyb::abi_fail(HYP_STATUS_INTERNAL, "op failed with a non-standard exception");
+    }
+}
+
+inline cudaStream_t as_stream(void* s) { return static_cast<cudaStream_t>(s); }
+inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+}  // namespace
+
+extern "C" {
+
+HypStatus hyb_build_info(char* buffer, size_t len) {
+    if (buffer == nullptr || len == 0) return hyb::abi_fail(HYP_STATUS_INVALID_ARGUMENT, "buffer is null");
+    std::snprintf(buffer, len, "hyperion_b200 sm_100a cuda %d", CUDART_VERSION);
+    return hyb::abi_ok();
+}
+
+HypStatus hyb_quantized_matmul(const void* x, const uint32_t* w, const void* scales, const void* biases, void* y,
+                               int64_t M, int64_t K, int64_t N, int32_t group_size, int32_t bits, void* stream) {
+    if (group_size != 64 || bits != 4)
+        return hyb::abi_fail(HYP_STATUS_UNSUPPORTED, "only affine group_size=64, bits=4 is implemented");
+    if (!x || !w || !scales || !biases || !y) return hyb::abi_fail(HYP_STATUS_INVALID_ARGUMENT, "null pointer argument");
+    if (M <= 0 || N <= 0 || K <= 0 || K % 64 != 0 || M > (1 << 24) || N > (1 << 30) || K > (1 << 20))
+        return hyb::abi_fail(HYP_STATUS_INVALID_ARGUMENT, "quantized_matmul: bad shape (K must be a positive multiple of 64)");
+    if (!aligned16(x) || !aligned16(w) || !aligned16(y))
+        return hyb::abi_fail(HYP_STATUS_INVALID_ARGUMENT, "quantized_matmul: x, w and y must be 16-byte aligned");
+    return run([&] {
+        hyb::launch_quantized_matmul(static_cast<const hyb::bf16*>(x), w, static_cast<const hyb::bf16*>(scales),
+                                     static_cast<const hyb::bf16*>(biases), static_cast<hyb::bf16*>(y),
+                                     static_cast<int>(M), static_cast<int>(K), static_cast<int>(N), as_stream(stream));
+    });
+}
+
+size_t hyb_sdpa_decode_scratch_bytes(int32_t n_heads, int32_t n_kv, int32_t head_dim, int32_t max_keys) {
+    if (n_heads <= 0 || n_kv <= 0 || head_dim <= 0 || max_keys <= 0) return 0;
+    return hyb::decode_attn_scratch_bytes(n_heads, n_kv, head_dim, max_keys);
+}
+
+HypStatus hyb_sdpa_decode(const void* q, const void* k_cache, const void* v_cache, void* out, int32_t n_heads,
+                          int32_t n_kv, int32_t head_dim, int32_t capacity, int32_t last_pos, int32_t n_keys,
+                          float scale, float softcap, int32_t rounding, void* scratch, size_t scratch_bytes,
+                          void* stream) {
+    if (!q || !k_cache || !v_cache || !out || !scratch)
+        return hyb::abi_fail(HYP_STATUS_INVALID_ARGUMENT, "null pointer argument");
+    if (n_heads <= 0 || n_kv <= 0 || n_heads % n_kv != 0 || n_keys <= 0 || capacity <= 0 || last_pos < n_keys - 1)
+        return hyb::abi_fail(HYP_STATUS_INVALID_ARGUMENT, "sdpa_decode: bad shape");
+    if (n_keys > capacity) return hyb::abi_fail(HYP_STATUS_INVALID_ARGUMENT, "sdpa_decode: n_keys exceeds the cache capacity");
+    if (head_dim != 64 && head_dim != 128 && head_dim != 256 && head_dim != 512)
+        return hyb::abi_fail(HYP_STATUS_UNSUPPORTED, "sdpa_decode: head_dim must be 64, 128, 256 or 512");
+    return run([&] {
+        hyb::DecodeAttnParams p;
+        p.q = static_cast<const hyb::bf16*>(q);
+        p.k_cache = static_cast<const hyb::bf16*>(k_cache);
+        p.v_cache = static_cast<const hyb::bf16*>(v_cache);
+        p.out = static_cast<hyb::bf16*>(out);
+        p.n_heads = n_heads;
+        p.n_kv = n_kv;
+        p.hd = head_dim;
+        p.cap = capacity;
+        p.last_pos = last_pos;
+        p.n_keys = n_keys;
+        p.scale = scale;
+        p.softcap = softcap;
+        p.rounding = rounding;
+        p.scratch = scratch;
+        p.scratch_bytes = scratch_bytes;
+        hyb::launch_decode_attn(p, as_stream(stream));
+    });
+}
+
+HypStatus hyb_sdpa_prefill(const void* q, const void* k, const void* v, void* out, int32_t Lq, int32_t Lk,
+                           int32_t n_heads, int32_t n_kv, int32_t head_dim, int32_t q_pos0, int32_t k_pos0,
+                           int32_t window, float scale, float softcap, int32_t rounding, void* stream) {
+    if (!q || !k || !v || !out) return hyb::abi_fail(HYP_STATUS_INVALID_ARGUMENT, "null pointer argument");
+    if (Lq <= 0 || Lk <= 0 || n_heads <= 0 || n_kv <= 0 || n_heads % n_kv != 0 || window < 0)
+        return hyb::abi_fail(HYP_STATUS_INVALID_ARGUMENT, "sdpa_prefill: bad shape");
+    if (head_dim != 64 && head_dim != 128 && head_dim != 256)
+        return hyb::abi_fail(HYP_STATUS_UNSUPPORTED, "sdpa_prefill: head_dim must be 64, 128 or 256");
+    if (!aligned16(q) || !aligned16(k) || !aligned16(v))
+        return hyb::abi_fail(HYP_STATUS_INVALID_ARGUMENT, "sdpa_prefill: q, k, v must be 16-byte aligned");
+    return run([&] {
+        hyb::PrefillAttnParams p;
+        p.q = static_cast<const hyb::bf16*>(q);
+        p.k = static_cast<const hyb::bf16*>(k);
+        p.v = static_cast<const hyb::bf16*>(v);
+        p.out = static_cast<hyb::bf16*>(out);
+        p.Lq = Lq;
+        p.Lk = Lk;
+        p.n_heads = n_heads;
+        p.n_kv = n_kv;
+        p.hd = head_dim;
+        p.q_pos0 = q_pos0;
+        p.k_pos0 = k_pos0;
+        p.window = window;
+        p.scale = scale;
+        p.softcap = softcap;
+        p.rounding = rounding;
+        hyb::launch_prefill_attn(p, as_stream(stream));
+    });
+}
+
+HypStatus hyb_rms_norm(const void* x, const void* w, void* out, int32_t rows, int32_t D, float eps, void* stream) {
+    if (!x || !out) return hyb::abi_fail(HYP_STATUS_INVALID_ARGUMENT, "null pointer argument");
+    if (rows < 0 || D <= 0) return hyb::abi_fail(HYP_STATUS_INVALID_ARGUMENT, "rms_norm: bad shape");
+    return run([&] {
+        hyb::launch_rms_norm(static_cast<const hyb::bf16*>(x), static_cast<const hyb::bf16*>(w),
+                             static_cast<hyb::bf16*>(out), rows, D, eps, as_stream(stream));
+    });
+}
+
+HypStatus hyb_qkv_post(const void* qkv, int32_t L, int32_t ld, int32_t n_heads, int32_t n_kv, int32_t head_dim,
+                       int32_t v_from_k, const void* q_norm, const void* k_norm, const float* inv_freq, int32_t pos0,
+                       float eps, void* q_out, void* k_out, void* v_out, void* k_cache, void* v_cache,
+                       int32_t cache_cap, int32_t cache_first, void* stream) {
+    if (!qkv || !q_norm || !k_norm || !inv_freq || !q_out) return hyb::abi_fail(HYP_STATUS_INVALID_ARGUMENT, "null pointer argument");
+    if (L <= 0 || n_heads <= 0 || n_kv <= 0 || pos0 < 0) return hyb::abi_fail(HYP_STATUS_INVALID_ARGUMENT, "qkv_post: bad shape");
+    if (head_dim % 64 != 0 || head_dim > 512) return hyb::abi_fail(HYP_STATUS_UNSUPPORTED, "qkv_post: head_dim must be a multiple of 64 up to 512");
+    const int64_t need = static_cast<int64_t>(n_heads + (v_from_k ? 1 : 2) * n_kv) * head_dim;
+    if (ld < need) return hyb::abi_fail(HYP_STATUS_INVALID_ARGUMENT, "qkv_post: ld smaller than the q/k/v columns");
+    if ((k_cache || v_cache) && cache_cap <= 0) return hyb::abi_fail(HYP_STATUS_INVALID_ARGUMENT, "qkv_post: cache_cap must be positive");
+    return run([&] {
+        hyb::QkvPostParams p;
+        p.qkv = static_cast<const hyb::bf16*>(qkv);
+        p.L = L;
+        p.ld = ld;
+        p.n_heads = n_heads;
+        p.n_kv = n_kv;
+        p.hd = head_dim;
+        p.v_from_k = v_from_k != 0;
+        p.q_norm = static_cast<const hyb::bf16*>(q_norm);
+        p.k_norm = static_cast<const hyb::bf16*>(k_norm);
+        p.inv_freq = inv_freq;
+        p.pos0 = pos0;
+        p.eps = eps;
+        p.q_out = static_cast<hyb::bf16*>(q_out);
+        p.k_out = static_cast<hyb::bf16*>(k_out);
+        p.v_out = static_cast<hyb::bf16*>(v_out);
+        p.k_cache = static_cast<hyb::bf16*>(k_cache);
+        p.v_cache = static_cast<hyb::bf16*>(v_cache);
+        p.cache_cap = cache_cap;
+        p.cache_first = cache_first;
+        hyb::launch_qkv_post(p, as_stream(stream));
+    });
+}
+
+}  // extern "C"

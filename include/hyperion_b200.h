@@ -1,0 +1,153 @@
+/*
+ * hyperion_b200.h - extension entry points of the B200 engine library.
+ *
+ * These sit beside the 14-function hyperion_mlx.h ABI (which they do not change)
+ * and expose the engine's kernels one by one, in plain C with device pointers,
+ * so that tests and benchmarks can drive each hot-path op directly. Each entry
+ * point names the reference interface it replaces. All pointers are CUDA device
+ * pointers unless a comment says "host"; `stream` is a cudaStream_t (NULL =
+ * the legacy default stream). bf16 tensors are passed as `void*`.
+ *
+ * Every function returns a HypStatus and records a message for hyp_last_error
+ * on failure: INVALID_ARGUMENT for bad shapes or null pointers, UNSUPPORTED for
+ * shapes the kernels do not implement, INTERNAL for CUDA errors.
+ */
+#ifndef HYPERION_B200_H
+#define HYPERION_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#include "hyperion_mlx.h"
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Library build identity: writes a NUL-terminated string like "hyperion_b200 sm_100a". */
+HypStatus hyb_build_info(char* buffer, size_t buffer_len);
+
+/*
+ * Affine Q4/g64 quantized matmul, y = x * dequant(w)^T.
+ * Replaces mx::quantized_matmul(x, w, scales, biases, transpose=true,
+ * group_size=64, bits=4, "affine") as called by QuantizedLinear::apply
+ * (native/hyperion_mlx/src/weights.h:26-37).
+ *   x: bf16 [M, K]; w: u32 [N, K/8] (code i of word j of row n = q[n, 8j+i],
+ *   bits [4i, 4i+4)); scales, biases: bf16 [N, K/64]; y: bf16 [M, N].
+ *   M == 1 runs the decode qmv kernel, M > 1 the prefill GEMM.
+ * group_size must be 64 and bits 4 (UNSUPPORTED otherwise); K a multiple of 64.
+ */
+HypStatus hyb_quantized_matmul(const void* x, const uint32_t* w, const void* scales,
+                               const void* biases, void* y, int64_t M, int64_t K, int64_t N,
+                               int32_t group_size, int32_t bits, void* stream);
+
+/*
+ * Single-token attention over a KV cache, the q_len == 1 case of
+ * mx::fast::scaled_dot_product_attention(q, k, v, scale, bool mask)
+ * (native/hyperion_mlx/src/forward.cc:498-504) together with the cache read that
+ * feeds it (forward.cc:474-494, kv_cache.cc:251-265).
+ *   q: bf16 [n_heads, head_dim]; k_cache, v_cache: bf16 [capacity, n_kv, head_dim]
+ *   where absolute position p lives in slot p % capacity (a ring for sliding
+ *   layers; capacity >= positions for a global cache). The query sits at
+ *   last_pos and attends to the n_keys positions last_pos - n_keys + 1 .. last_pos.
+ *   out: bf16 [n_heads, head_dim]. softcap > 0 applies softcap * tanh(s / softcap)
+ *   to the scores (off for Gemma 4). rounding 0 reproduces MLX's CPU-stream
+ *   rounding (bf16 scores and probabilities), 1 keeps them in fp32.
+ *   scratch: device workspace of hyb_sdpa_decode_scratch_bytes() bytes, zeroed
+ *   once before first use; the call leaves it ready for the next call.
+ */
+size_t hyb_sdpa_decode_scratch_bytes(int32_t n_heads, int32_t n_kv, int32_t head_dim, int32_t max_keys);
+HypStatus hyb_sdpa_decode(const void* q, const void* k_cache, const void* v_cache, void* out,
+                          int32_t n_heads, int32_t n_kv, int32_t head_dim, int32_t capacity,
+                          int32_t last_pos, int32_t n_keys, float scale, float softcap,
+                          int32_t rounding, void* scratch, size_t scratch_bytes, void* stream);
+
+/*
+ * Multi-token causal attention with an optional sliding window, the prefill case
+ * of the same op with the mask of build_mask (forward.cc:345-374).
+ *   q: bf16 [Lq, n_heads, head_dim] at absolute positions q_pos0 + i;
+ *   k, v: bf16 [Lk, n_kv, head_dim] at positions k_pos0 + j;
+ *   key j is visible to query i iff kpos <= qpos and (window == 0 || kpos > qpos - window).
+ *   out: bf16 [Lq, n_heads, head_dim].
+ */
+HypStatus hyb_sdpa_prefill(const void* q, const void* k, const void* v, void* out, int32_t Lq,
+                           int32_t Lk, int32_t n_heads, int32_t n_kv, int32_t head_dim,
+                           int32_t q_pos0, int32_t k_pos0, int32_t window, float scale,
+                           float softcap, int32_t rounding, void* stream);
+
+/*
+ * RMSNorm over rows of length D: out = bf16(bf16(x * rsqrt(mean(x^2) + eps)) * w);
+ * w may be NULL (the weightless v_norm). Replaces mx::fast::rms_norm
+ * (native/hyperion_mlx/src/forward.cc:25-27).
+ */
+HypStatus hyb_rms_norm(const void* x, const void* w, void* out, int32_t rows, int32_t D,
+                       float eps, void* stream);
+
+/*
+ * QK-norm + RoPE + cache write for L tokens of one layer (forward.cc:394-420,
+ * rope.cc:62-123, kv_cache.cc:161-249). qkv: bf16 [L, ld] holding q (n_heads * hd
+ * columns), k (n_kv * hd), then v (n_kv * hd) unless v_from_k (global K=V layers:
+ * V = v_norm of the k columns). inv_freq: f32 [hd/2] per-pair inverse frequencies
+ * (0 = identity pair). Outputs: q_out [L, n_heads, hd]; k_out/v_out (optional)
+ * [L, n_kv, hd]; k_cache/v_cache (optional) [cap, n_kv, hd] with slot (pos0+l) % cap
+ * for tokens l >= cache_first.
+ */
+HypStatus hyb_qkv_post(const void* qkv, int32_t L, int32_t ld, int32_t n_heads, int32_t n_kv,
+                       int32_t head_dim, int32_t v_from_k, const void* q_norm, const void* k_norm,
+                       const float* inv_freq, int32_t pos0, float eps, void* q_out, void* k_out,
+                       void* v_out, void* k_cache, void* v_cache, int32_t cache_cap,
+                       int32_t cache_first, void* stream);
+
+/*
+ * Load seeded synthetic weights generated on the device (no checkpoint files),
+ * for benchmarks at full model size. Every projection gets codes U{0..15},
+ * scales bf16(|N(0, 0.02)|), biases -8 * scales; norms and layer_scalar
+ * bf16(1 + N(0, 0.02)). Same validation and errors as hyp_model_load.
+ */
+HypStatus hyb_model_load_synthetic(HypModel model, const HypGeometryParams* geometry, uint64_t seed);
+
+/* The CUDA stream the model's kernels run on (for event timing). */
+HypStatus hyb_model_stream(HypModel model, void** out_stream);
+
+/*
+ * Copy a KV cache of layer `layer` to host memory for inspection: which = 0 for
+ * K, 1 for V. Writes min(capacity rows, *rows) rows of n_kv * head_dim bf16 and
+ * stores the cache capacity (ring capacity or global capacity) in *rows.
+ */
+HypStatus hyb_kv_copy_layer(HypModel model, HypKvState kv, uint32_t layer, int32_t which,
+                            void* host_out, uint32_t* rows);
+
+/* Current autoregressive cursor of a KV state (offset and last token). */
+HypStatus hyb_kv_cursor(HypKvState kv, uint32_t* offset, uint32_t* last_token);
+
+/*
+ * Greedy steps that also copy the post-softcap logits (bf16, vocab entries,
+ * host memory) of the step to `host_logits` (may be NULL). prefill uses
+ * `tokens`; decode runs one step.
+ */
+HypStatus hyb_prefill_logits(HypModel model, HypKvState kv, const HypTokenStream* tokens,
+                             HypStepResult out_result, void* host_logits);
+HypStatus hyb_decode_logits(HypModel model, HypKvState kv, HypStepResult out_result,
+                            void* host_logits);
+
+/*
+ * Decode with the next input token supplied by the caller instead of the last
+ * sampled one (teacher forcing; used to measure per-step agreement without
+ * divergence cascades).
+ */
+HypStatus hyb_decode_forced(HypModel model, HypKvState kv, uint32_t token, HypStepResult out_result,
+                            void* host_logits);
+
+/*
+ * Test hook: the next decode call on this thread throws once on the host right
+ * after its first forward has been enqueued, like the reference's post-append
+ * fault (native/hyperion_mlx/src/test_fault.cc:1-24). The call returns
+ * INTERNAL and the KV state is poisoned. No device fault is involved.
+ */
+HypStatus hyb_test_arm_post_append_fault(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* HYPERION_B200_H */
