@@ -1,0 +1,466 @@
+#!/usr/bin/env python3
+"""Benchmark of the Hyperion hot path on B200 (one JSON line on rank 0).
+
+Default workload (the metric's configuration): the batch-1
+affine Q4/g64 qmv sweep over the Gemma-12B layer shapes, in the proportions one
+decode token uses them: 48 layers x {q 3840x4096, k 3840x2048, v 3840x2048,
+o 4096x3840, gate 3840x15360, up 3840x15360, down 15360x3840} + the tied lm_head
+3840x262144. Every projection has its own weights (6.62 GB per step, far above
+the 126 MB L2, so nothing is re-read from L2 between steps). One step = the 337
+qmv launches of one token, captured in a CUDA graph; value = algorithmic bytes /
+time (GB/s). Per-shape figures are timed separately over >= 48 distinct copies.
+
+`--workload decode` times the engine's full 12B-shaped decode (config 3) through
+hyp_decode_block after a 4096-token prefill: tokens/s.
+
+`--impl reference` times the CPU restatement of the same qmv (the reference's
+own path is MLX, unavailable here) on the host cores.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+REPO = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, REPO)
+
+PROJ = [("q", 3840, 4096), ("k", 3840, 2048), ("v", 3840, 2048), ("o", 4096, 3840),
+        ("gate", 3840, 15360), ("up", 3840, 15360), ("down", 15360, 3840)]
+LM_HEAD = ("lm_head", 3840, 262144)
+N_LAYERS = 48
+METRIC = "Q4/g64 qmv HBM GB/s (% of peak); 12B-shaped decode tok/s at 1/2/4/8 GPUs"
+
+
+def qmv_bytes(K: int, N: int) -> int:
+    """Algorithmic bytes of one batch-1 qmv: nibbles + bf16 scale/bias + x + y."""
+    return K * N // 2 + 4 * N * K // 64 + 2 * K + 2 * N
+
+
+def peaks():
+    p = os.path.join(REPO, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            d = json.load(f)
+        return d.get("hbm_gbs", 6650.0), d.get("bf16_tflops", 1590.0), "measured"
+    return 6650.0, 1590.0, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clock/throttle samples during the timed region."""
+
+    def __init__(self, gpu_index: int):
+        self.idx = gpu_index
+        self.proc = None
+        self.out = None
+
+    def __enter__(self):
+        q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
+             "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+             "clocks_event_reasons.sw_power_cap")
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.idx), f"--query-gpu={q}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except Exception:
+            self.proc = None
+        return self
+
+    def __exit__(self, *a):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.out, _ = self.proc.communicate(timeout=5)
+            except Exception:
+                self.proc.kill()
+                self.out = ""
+
+    def summary(self):
+        if not self.out:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.out.strip().splitlines():
+            parts = [x.strip() for x in line.split(",")]
+            if len(parts) < 8:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx = float(parts[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, parts[4:8]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx,
+                "samples": len(sm), "reasons": sorted(reasons)}
+
+
+def dist_setup(n_gpus):
+    import torch
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != n_gpus:
+        raise SystemExit(f"--gpus {n_gpus} but WORLD_SIZE={world}")
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local))
+    else:
+        torch.cuda.set_device(0)
+    return rank, world, local
+
+
+def max_over_ranks(x: float, world: int) -> float:
+    if world == 1:
+        return x
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+
+
+# ------------------------------------------------------------------ CPU baseline (oracle)
+def cpu_qmv_baseline(budget_s: float = 10.0):
+    """The oracle's multithreaded qmv over the six cfg-1 shapes, looped for ~budget_s."""
+    import numpy as np
+    from oracle import gemma_oracle as go
+    from hyperion_b200.synth import f32_to_bf16_bits
+    rng = np.random.default_rng(0)
+    shapes = [(3840, 4096), (3840, 2048), (4096, 3840), (3840, 15360), (15360, 3840), (3840, 262144)]
+    data = []
+    for K, N in shapes:
+        w = rng.integers(0, 2 ** 32, size=(N, K // 8), dtype=np.uint32)
+        s = f32_to_bf16_bits(np.abs(rng.standard_normal((N, K // 64), dtype=np.float32)) * 0.02)
+        b = f32_to_bf16_bits(-8 * (s.astype(np.uint32) << 16).view(np.float32))
+        x = f32_to_bf16_bits(rng.standard_normal(K, dtype=np.float32))
+        data.append((K, N, x, w, s, b))
+    threads = go.lib().orc_max_threads()
+    for K, N, x, w, s, b in data:  # warm-up pass
+        go.qmv_fast(x, w, s, b, threads)
+    total_bytes, t0, passes = 0, time.perf_counter(), 0
+    while True:
+        for K, N, x, w, s, b in data:
+            go.qmv_fast(x, w, s, b, threads)
+            total_bytes += qmv_bytes(K, N)
+        passes += 1
+        if time.perf_counter() - t0 >= budget_s:
+            break
+    el = time.perf_counter() - t0
+    return {"value": round(total_bytes / el / 1e9, 2), "unit": "GB/s", "cores": threads, "kind": "port",
+            "sample": f"{passes} passes over the six cfg-1 qmv shapes (655 MB each), {el:.1f} s, "
+                      f"oracle/hyp_oracle.c orc_qmv_fast, OpenMP {threads} threads"}
+
+
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    import numpy as np
+    from oracle import gemma_oracle as go
+    from hyperion_b200.synth import f32_to_bf16_bits
+    rng = np.random.default_rng(0)
+    shapes = [(3840, 4096), (3840, 2048), (4096, 3840), (3840, 15360), (15360, 3840), (3840, 262144)]
+    data = []
+    for K, N in shapes:
+        w = rng.integers(0, 2 ** 32, size=(N, K // 8), dtype=np.uint32)
+        s = f32_to_bf16_bits(np.abs(rng.standard_normal((N, K // 64), dtype=np.float32)) * 0.02)
+        b = f32_to_bf16_bits(-8 * (s.astype(np.uint32) << 16).view(np.float32))
+        x = f32_to_bf16_bits(rng.standard_normal(K, dtype=np.float32))
+        data.append((K, N, x, w, s, b))
+    threads = go.lib().orc_max_threads()
+    step_bytes = sum(qmv_bytes(K, N) for K, N, *_ in data)
+
+    def step():
+        for K, N, x, w, s, b in data:
+            go.qmv_fast(x, w, s, b, threads)
+
+    for _ in range(args.warmup):
+        step()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        step()
+    el = time.perf_counter() - t0
+    v = step_bytes * args.steps / el / 1e9
+    line = {"impl": "reference", "metric": METRIC, "value": round(v, 2), "unit": "GB/s", "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(el / args.steps * 1e3, 3),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "u4/bf16->f32",
+            "data": "synthetic",
+            "config": {"workload": "cfg1 qmv sweep: the six Gemma-12B qmv shapes once per step (655 MB)",
+                       "l2": "inputs larger than L2"},
+            "cpu_baseline": {"value": round(v, 2), "unit": "GB/s", "cores": threads, "kind": "port",
+                             "sample": f"{args.steps} steps of the six cfg-1 shapes, orc_qmv_fast "
+                                       f"(the reference's MLX CPU path is not installable here)"},
+            "e2e": {"value": round(v, 2), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+# ------------------------------------------------------------------ qmv sweep (ours)
+def make_q4(N, K, gen, device):
+    import torch
+    w = torch.randint(-2 ** 31, 2 ** 31 - 1, (N, K // 8), dtype=torch.int32, device=device, generator=gen)
+    s = (torch.randn((N, K // 64), device=device, generator=gen) * 0.02).abs().to(torch.bfloat16)
+    b = (-8.0 * s.float()).to(torch.bfloat16)
+    return w, s, b
+
+
+def run_qmv(args, rank, world, local):
+    import torch
+    import ctypes
+    import hyperion_b200 as hb
+    from hyperion_b200 import ops
+    dev = torch.device("cuda", local)
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(1234 + rank)
+    # weights: 48 layers x 7 projections + lm_head, all distinct
+    layers = []
+    for _ in range(N_LAYERS):
+        lay = []
+        for name, K, N in PROJ:
+            w, s, b = make_q4(N, K, gen, dev)
+            x = torch.randn(K, device=dev, generator=gen).to(torch.bfloat16)
+            y = torch.empty(N, dtype=torch.bfloat16, device=dev)
+            lay.append((name, K, N, w, s, b, x, y))
+        layers.append(lay)
+    K, N = LM_HEAD[1], LM_HEAD[2]
+    lw, ls, lb = make_q4(N, K, gen, dev)
+    lx = torch.randn(K, device=dev, generator=gen).to(torch.bfloat16)
+    ly = torch.empty(N, dtype=torch.bfloat16, device=dev)
+    items = [it for lay in layers for it in lay] + [("lm_head", K, N, lw, ls, lb, lx, ly)]
+    step_bytes = sum(qmv_bytes(it[1], it[2]) for it in items)
+    launches = len(items)
+
+    stream = torch.cuda.Stream(device=dev)
+
+    def launch_all(x_override=None):
+        for it in items:
+            name, K_, N_, w, s, b, x, y = it
+            ops.quantized_matmul(x.view(1, K_), w, s, b, out=y.view(1, N_))
+
+    torch.cuda.synchronize()
+    with torch.cuda.stream(stream):
+        launch_all()  # sets kernel attributes outside capture
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        launch_all()
+    # ---- device-resident timing (graph replays go to the current stream)
+    with torch.cuda.stream(stream):
+        for _ in range(args.warmup):
+            graph.replay()
+    torch.cuda.synchronize()
+    barrier(world)
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk, torch.cuda.stream(stream):
+        torch.cuda.synchronize()
+        barrier(world)
+        ev0.record(stream)
+        for _ in range(args.steps):
+            graph.replay()
+        ev1.record(stream)
+        torch.cuda.synchronize()
+    ms = ev0.elapsed_time(ev1) / args.steps
+    ms_max = max_over_ranks(ms, world)
+    value = step_bytes * world / (ms_max * 1e-3) / 1e9
+
+    # ---- per-shape kernel timing (each shape over its distinct copies, graph of back-to-back launches)
+    per_shape = []
+    shape_time = {}
+    for name, K_, N_ in PROJ + [LM_HEAD]:
+        sel = [it for it in items if it[0] == name]
+        reps = max(1, 48 // len(sel))
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=stream):
+            for _ in range(reps):
+                for it in sel:
+                    ops.quantized_matmul(it[6].view(1, K_), it[3], it[4], it[5], out=it[7].view(1, N_))
+        with torch.cuda.stream(stream):
+            for _ in range(3):
+                g.replay()
+            torch.cuda.synchronize()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            R = 5
+            for _ in range(R):
+                g.replay()
+            e1.record(stream)
+            torch.cuda.synchronize()
+        per_launch_us = e0.elapsed_time(e1) * 1e3 / (R * reps * len(sel))
+        gbs = qmv_bytes(K_, N_) / (per_launch_us * 1e-6) / 1e9
+        shape_time[name] = per_launch_us
+        per_shape.append({"shape": f"{name} K={K_} N={N_}", "us": round(per_launch_us, 2),
+                          "GB/s": round(gbs, 1)})
+        del g
+    # mix-weighted kernel achieved bandwidth (kernel time only, no inter-launch gaps)
+    kern_us = sum(shape_time[it[0]] for it in items)
+    achieved = step_bytes / (kern_us * 1e-6) / 1e9
+
+    # ---- e2e: the C-ABI call per projection with host activations/results
+    hx = torch.empty(sum(it[1] for it in items), dtype=torch.bfloat16).pin_memory()
+    hy = torch.empty(sum(it[2] for it in items), dtype=torch.bfloat16).pin_memory()
+    dx = torch.empty_like(hx, device=dev)
+    dy = torch.empty_like(hy, device=dev)
+    hx.copy_(torch.randn(hx.numel()).to(torch.bfloat16))
+    offs_x, offs_y, ox, oy = [], [], 0, 0
+    for it in items:
+        offs_x.append(ox)
+        offs_y.append(oy)
+        ox += it[1]
+        oy += it[2]
+    L = hb.lib()
+    s_ptr = ctypes.c_void_p(stream.cuda_stream)
+
+    def e2e_step():
+        dx.copy_(hx, non_blocking=True)
+        for i, it in enumerate(items):
+            _, K_, N_, w, s, b, _, _ = it
+            L.hyb_quantized_matmul(ctypes.c_void_p(dx.data_ptr() + 2 * offs_x[i]), ctypes.c_void_p(w.data_ptr()),
+                                   ctypes.c_void_p(s.data_ptr()), ctypes.c_void_p(b.data_ptr()),
+                                   ctypes.c_void_p(dy.data_ptr() + 2 * offs_y[i]), 1, K_, N_, 64, 4, s_ptr)
+        hy.copy_(dy, non_blocking=True)
+
+    with torch.cuda.stream(stream):
+        for _ in range(args.warmup):
+            e2e_step()
+        torch.cuda.synchronize()
+        barrier(world)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(args.steps):
+            e2e_step()
+        e1.record(stream)
+        torch.cuda.synchronize()
+    e2e_ms = max_over_ranks(e0.elapsed_time(e1) / args.steps, world)
+    e2e_val = step_bytes * world / (e2e_ms * 1e-3) / 1e9
+
+    if rank != 0:
+        return
+    hbm, _, src = peaks()
+    traffic = None
+    tp = os.path.join(REPO, "profiles", "qmv_traffic.json")
+    if os.path.exists(tp):
+        with open(tp) as f:
+            traffic = json.load(f).get("dram_bytes_per_launch_mix")
+    line = {
+        "metric": METRIC, "value": round(value, 1), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(ms_max, 4), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "u4/bf16->f32", "data": "synthetic",
+        "config": {"workload": "cfg1 qmv sweep in 12B decode-token proportions: 48 x {q,k,v,o,gate,up,down} "
+                               "+ lm_head, distinct weights (6.62 GB/step)",
+                   "l2": "inputs larger than L2 (no reuse across steps)",
+                   "step_bytes": step_bytes, "parallelism": f"replicas x{world}"},
+        "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s",
+                     "frac": round(achieved / hbm, 4), "traffic": traffic, "peak_source": src,
+                     "kernel": "qmv_kernel (mix-weighted over the step's 337 launches)"},
+        "per_shape": per_shape,
+        "gpu_launches": launches * args.steps,
+        "e2e": {"value": round(e2e_val, 1), "unit": "GB/s",
+                "h2d_bytes_per_step": int(hx.numel() * 2), "d2h_bytes_per_step": int(hy.numel() * 2),
+                "path": "hyb_quantized_matmul per projection via ctypes, host x/y copied each step"},
+        "clocks": clk.summary(),
+    }
+    if world == 1 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_qmv_baseline(args.cpu_seconds)
+    print(json.dumps(line), flush=True)
+
+
+# ------------------------------------------------------------------ 12B decode (ours)
+def run_decode(args, rank, world, local):
+    import torch
+    import hyperion_b200 as hb
+    from hyperion_b200.synth import config3
+    geo = config3()
+    eng = hb.Engine(geo, synthetic_seed=1 + rank)
+    kv = eng.new_kv()
+    ctx = args.ctx
+    prompt = [int(t) for t in torch.randint(0, geo.vocab_size, (ctx,), generator=torch.Generator().manual_seed(5))]
+    t0 = time.perf_counter()
+    kv.prefill(prompt)
+    prefill_s = time.perf_counter() - t0
+    stream = torch.cuda.ExternalStream(eng.stream())
+    for _ in range(args.warmup):
+        kv.decode(1)
+    barrier(world)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        torch.cuda.synchronize()
+        e0.record(stream)
+        for _ in range(args.steps):
+            kv.decode(1)
+        e1.record(stream)
+        torch.cuda.synchronize()
+    ms = max_over_ranks(e0.elapsed_time(e1) / args.steps, world)
+    tok_s = world / (ms * 1e-3)
+    if rank != 0:
+        return
+    w_bytes = 48 * sum(qmv_bytes(K, N) for _, K, N in PROJ) + qmv_bytes(3840, 262144)
+    kv_bytes = 0
+    for i, kind in enumerate(geo.layer_types):
+        n = min(geo.sliding_window, ctx + args.warmup) if kind == 0 else ctx + args.warmup
+        kv_bytes += 2 * n * geo.n_kv(i) * geo.head_dim(i) * 2
+    hbm, _, src = peaks()
+    bytes_tok = w_bytes + kv_bytes
+    line = {"metric": METRIC, "value": round(tok_s, 2), "unit": "tok/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "u4/bf16->f32", "data": "synthetic",
+            "config": {"workload": f"cfg3 12B-shaped decode, ctx {ctx}, batch 1", "prefill_s": round(prefill_s, 3),
+                       "l2": "inputs larger than L2"},
+            "roofline": {"bound": "hbm", "achieved": round(bytes_tok / (ms * 1e-3) / 1e9, 1), "peak": hbm,
+                         "unit": "GB/s", "frac": round(bytes_tok / (ms * 1e-3) / 1e9 / hbm, 4), "traffic": None,
+                         "peak_source": src, "kernel": "whole decode step (weights + KV bytes per token)"},
+            "gpu_launches": None,
+            "e2e": {"value": round(tok_s, 2), "unit": "tok/s", "h2d_bytes_per_step": 4, "d2h_bytes_per_step": 64,
+                    "path": "hyp_decode_block(n_tokens=1) via ctypes"},
+            "clocks": clk.summary()}
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--workload", default="qmv", choices=["qmv", "decode"])
+    ap.add_argument("--ctx", type=int, default=4096)
+    ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        run_reference(args)
+        return
+    from hyperion_b200.build import LIB
+    if not os.path.exists(LIB):
+        raise SystemExit("libhyperion_mlx.so is not built (python -m hyperion_b200.build)")
+    rank, world, local = dist_setup(args.gpus)
+    try:
+        if args.workload == "qmv":
+            run_qmv(args, rank, world, local)
+        else:
+            run_decode(args, rank, world, local)
+    finally:
+        if world > 1:
+            import torch.distributed as dist
+            barrier(world)
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

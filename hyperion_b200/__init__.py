@@ -101,8 +101,9 @@ ABI_FUNCTIONS = [
     "hyp_step_result_free", "hyp_step_result_fields",
 ]
 EXT_FUNCTIONS = [
-    "hyb_build_info", "hyb_quantized_matmul", "hyb_sdpa_decode_scratch_bytes", "hyb_sdpa_decode",
-    "hyb_sdpa_prefill", "hyb_rms_norm", "hyb_qkv_post", "hyb_model_load_synthetic", "hyb_model_stream",
+    "hyb_build_info", "hyb_quantized_matmul", "hyb_qmv_fused", "hyb_sdpa_decode_scratch_bytes", "hyb_sdpa_decode",
+    "hyb_sdpa_prefill", "hyb_rms_norm", "hyb_qkv_post", "hyb_model_load_synthetic",
+    "hyb_model_set_attention_rounding", "hyb_model_stream",
     "hyb_kv_copy_layer", "hyb_kv_cursor", "hyb_prefill_logits", "hyb_decode_logits", "hyb_decode_forced",
     "hyb_test_arm_post_append_fault",
 ]
@@ -138,6 +139,7 @@ def lib() -> ctypes.CDLL:
         "hyp_step_result_fields": [P, ctypes.POINTER(HypStepResultFields)],
         "hyb_build_info": [c.c_char_p, c.c_size_t],
         "hyb_quantized_matmul": [P, P, P, P, P, c.c_int64, c.c_int64, c.c_int64, c.c_int32, c.c_int32, P],
+        "hyb_qmv_fused": [P, P, P, P, P, c.c_int64, c.c_int64, c.c_int32, c.c_int32, P, P, P, P, P, c.c_float, P],
         "hyb_sdpa_decode": [P, P, P, P, c.c_int32, c.c_int32, c.c_int32, c.c_int32, c.c_int32, c.c_int32,
                             c.c_float, c.c_float, c.c_int32, P, c.c_size_t, P],
         "hyb_sdpa_prefill": [P, P, P, P, c.c_int32, c.c_int32, c.c_int32, c.c_int32, c.c_int32, c.c_int32,
@@ -146,6 +148,7 @@ def lib() -> ctypes.CDLL:
         "hyb_qkv_post": [P, c.c_int32, c.c_int32, c.c_int32, c.c_int32, c.c_int32, c.c_int32, P, P, P,
                          c.c_int32, c.c_float, P, P, P, P, P, c.c_int32, c.c_int32, P],
         "hyb_model_load_synthetic": [P, ctypes.POINTER(HypGeometryParams), c.c_uint64],
+        "hyb_model_set_attention_rounding": [P, c.c_int32],
         "hyb_model_stream": [P, ctypes.POINTER(P)],
         "hyb_kv_copy_layer": [P, P, c.c_uint32, c.c_int32, P, ctypes.POINTER(c.c_uint32)],
         "hyb_kv_cursor": [P, ctypes.POINTER(c.c_uint32), ctypes.POINTER(c.c_uint32)],
@@ -248,6 +251,9 @@ class Engine:
         s = ctypes.c_void_p()
         check(lib().hyb_model_stream(self._model, ctypes.byref(s)))
         return s.value or 0
+
+    def set_attention_rounding(self, mode: int) -> None:
+        check(lib().hyb_model_set_attention_rounding(self._model, mode))
 
     def new_kv(self) -> "KvState":
         return KvState(self)

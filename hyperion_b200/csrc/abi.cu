@@ -602,6 +602,15 @@ HypStatus hyb_model_stream(HypModel model, void** out_stream) {
     return ok();
 }
 
+HypStatus hyb_model_set_attention_rounding(HypModel model, int32_t mode) {
+    HypStatus st = validate_model(model);
+    if (st != HYP_STATUS_OK) return st;
+    if (!model->loaded) return fail(HYP_STATUS_INVALID_ARGUMENT, "model is not loaded");
+    if (mode != 0 && mode != 1) return fail(HYP_STATUS_INVALID_ARGUMENT, "attention rounding mode must be 0 or 1");
+    model->model->set_attention_rounding(mode);
+    return ok();
+}
+
 HypStatus hyb_kv_cursor(HypKvState kv, uint32_t* offset, uint32_t* last_token) {
     if (kv == nullptr || kv->magic != kKvStateMagic) return fail(HYP_STATUS_INVALID_ARGUMENT, "kvstate handle is invalid");
     if (offset) *offset = kv->kv->offset;

@@ -503,6 +503,7 @@ void Model::forward_chunk(KvState& kv, int L, uint32_t offset) {
         ap.hd = hd;
         ap.q_pos0 = static_cast<int>(offset);
         ap.scale = 1.0f;
+        ap.rounding = attn_rounding_;
         const size_t row = static_cast<size_t>(nkv) * hd;
         if (W.kind == LayerKind::Sliding) {
             LocalCache& c = kv.local[li++];
@@ -689,6 +690,7 @@ void Model::decode_layers(KvState& kv) {
         ap.n_kv = W.nkv;
         ap.hd = W.hd;
         ap.last_pos = static_cast<int>(pos);
+        ap.rounding = attn_rounding_;
         ap.scratch = ws_.attn_scratch.p;
         ap.scratch_bytes = ws_.attn_scratch_bytes;
         if (W.kind == LayerKind::Sliding) {

@@ -131,6 +131,12 @@ class Model {
     // One decode step at kv.offset from kv.last_token.
     StepOut decode_step(KvState& kv, std::vector<uint16_t>* logits_out);
 
+    // Attention rounding: 0 = MLX CPU-stream semantics (bf16 scores and
+    // probabilities, the default), 1 = fp32 scores/probabilities (MLX's fused
+    // Metal decode kernel semantics).
+    void set_attention_rounding(int mode) { attn_rounding_ = mode; }
+    int attention_rounding() const { return attn_rounding_; }
+
     uint64_t local_kv_bytes(const KvState& kv) const;
     uint64_t global_kv_bytes(const KvState& kv) const;
 
@@ -160,6 +166,7 @@ class Model {
     DevPtr<bf16> final_norm_;
     DevPtr<float> inv_freq_local_, inv_freq_global_;
     bf16 embed_scale_{};
+    int attn_rounding_ = 0;
     Workspace ws_;
 };
 

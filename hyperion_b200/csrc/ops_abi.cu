@@ -59,6 +59,40 @@ HypStatus hyb_quantized_matmul(const void* x, const uint32_t* w, const void* sca
     });
 }
 
+HypStatus hyb_qmv_fused(const void* x, const uint32_t* w, const void* scales, const void* biases, void* y,
+                        int64_t K, int64_t N, int32_t prologue, int32_t epilogue, const void* norm_w,
+                        const void* resid, const void* post_w, const void* scalar, void* h_out, float eps,
+                        void* stream) {
+    if (!x || !w || !scales || !biases || !y) return hyb::abi_fail(HYP_STATUS_INVALID_ARGUMENT, "null pointer argument");
+    if (K <= 0 || K % 64 != 0 || N <= 0 || K > (1 << 20) || N > (1 << 30))
+        return hyb::abi_fail(HYP_STATUS_INVALID_ARGUMENT, "qmv_fused: bad shape");
+    if (prologue < 0 || prologue > 2 || epilogue < 0 || epilogue > 1)
+        return hyb::abi_fail(HYP_STATUS_INVALID_ARGUMENT, "qmv_fused: unknown prologue/epilogue");
+    if (prologue >= 1 && !norm_w) return hyb::abi_fail(HYP_STATUS_INVALID_ARGUMENT, "qmv_fused: norm_w is required");
+    if (prologue == 2 && (!resid || !post_w)) return hyb::abi_fail(HYP_STATUS_INVALID_ARGUMENT, "qmv_fused: resid and post_w are required");
+    if (epilogue == 1 && N % 32 != 0) return hyb::abi_fail(HYP_STATUS_INVALID_ARGUMENT, "qmv_fused: GeGLU rows must be a multiple of 32");
+    if (prologue != 0 && K * 4 > 96 * 1024) return hyb::abi_fail(HYP_STATUS_UNSUPPORTED, "qmv_fused: K too large for a norm prologue");
+    return run([&] {
+        hyb::QmvParams p;
+        p.x = static_cast<const hyb::bf16*>(x);
+        p.w = w;
+        p.s = static_cast<const hyb::bf16*>(scales);
+        p.b = static_cast<const hyb::bf16*>(biases);
+        p.y = static_cast<hyb::bf16*>(y);
+        p.K = static_cast<int>(K);
+        p.N = static_cast<int>(N);
+        p.prologue = static_cast<hyb::QmvPrologue>(prologue);
+        p.epilogue = static_cast<hyb::QmvEpilogue>(epilogue);
+        p.norm_w = static_cast<const hyb::bf16*>(norm_w);
+        p.resid = static_cast<const hyb::bf16*>(resid);
+        p.post_w = static_cast<const hyb::bf16*>(post_w);
+        p.scalar = static_cast<const hyb::bf16*>(scalar);
+        p.h_out = static_cast<hyb::bf16*>(h_out);
+        p.eps = eps;
+        hyb::launch_qmv(p, as_stream(stream), false);
+    });
+}
+
 size_t hyb_sdpa_decode_scratch_bytes(int32_t n_heads, int32_t n_kv, int32_t head_dim, int32_t max_keys) {
     if (n_heads <= 0 || n_kv <= 0 || head_dim <= 0 || max_keys <= 0) return 0;
     return hyb::decode_attn_scratch_bytes(n_heads, n_kv, head_dim, max_keys);

@@ -201,7 +201,9 @@ void launch_quantized_matmul(const bf16* x, const uint32_t* w, const bf16* s, co
         p.y = y;
         p.K = K;
         p.N = N;
-        launch_qmv(p, stream, false);
+        // Programmatic dependent launch: the kernel reads only weights before
+        // griddepcontrol.wait, so its first loads may overlap the previous kernel.
+        launch_qmv(p, stream, true);
     } else {
         launch_qmm(x, w, s, b, y, M, K, N, stream);
     }

@@ -163,7 +163,7 @@ __global__ void __launch_bounds__(kThreads, 1) qmv_kernel(const QmvParams p) {
                 if (p.scalar) hv = rbf(hv * sc);
                 xf[k] = hv;
                 ss2 += hv * hv;
-                if (blockIdx.x == 0) p.h_out[k] = f2bf(hv);
+                if (blockIdx.x == 0 && p.h_out) p.h_out[k] = f2bf(hv);
             }
             tot = block_sum(ss2, tmp);
             inv = 1.0f / sqrtf(tot / static_cast<float>(K) + p.eps);

@@ -33,6 +33,19 @@ def quantized_matmul(x: torch.Tensor, w: torch.Tensor, scales: torch.Tensor, bia
     return out
 
 
+def qmv_fused(x, w, scales, biases, prologue=0, epilogue=0, norm_w=None, resid=None, post_w=None, scalar=None,
+              h_out=None, eps=1e-6, out=None, stream=None):
+    """Batch-1 qmv with the decode engine's fused norm prologue / GeGLU epilogue."""
+    K = x.numel()
+    N = w.shape[0]
+    if out is None:
+        out = torch.empty(N // 2 if epilogue == 1 else N, dtype=torch.bfloat16, device=x.device)
+    opt = lambda t: _p(t) if t is not None else None
+    check(lib().hyb_qmv_fused(_p(x), _p(w), _p(scales), _p(biases), _p(out), K, N, prologue, epilogue,
+                              opt(norm_w), opt(resid), opt(post_w), opt(scalar), opt(h_out), eps, _stream(stream)))
+    return out
+
+
 class DecodeScratch:
     """Device workspace for hyb_sdpa_decode (zeroed once)."""
 

@@ -56,6 +56,24 @@ HypStatus hyb_quantized_matmul(const void* x, const uint32_t* w, const void* sca
  *   scratch: device workspace of hyb_sdpa_decode_scratch_bytes() bytes, zeroed
  *   once before first use; the call leaves it ready for the next call.
  */
+/*
+ * The batch-1 qmv with the decode engine's fused prologue / epilogue (the
+ * reference computes these as separate MLX ops: forward.cc:25-27 rms_norm,
+ * :510-542 residual adds and layer_scalar, :324-343 GeGLU).
+ *   prologue 0: x used as is; 1: x <- rms_norm(x, norm_w);
+ *            2: h = bf16(resid + rms_norm(x, post_w)) [* scalar if non-NULL],
+ *               h written to h_out (may be NULL), then x <- rms_norm(h, norm_w).
+ *   epilogue 0: y[n] = bf16(x . w_hat[n]);
+ *            1: rows are gate/up interleaved by 16-row tiles (tile 2t = gate rows
+ *               16t..16t+15, tile 2t+1 = the matching up rows);
+ *               y[n] = bf16(gelu_tanh(gate[n]) * up[n]) for n < N/2.
+ *   x, resid, h_out, norm_w, post_w: bf16 [K]; scalar: bf16 [1].
+ */
+HypStatus hyb_qmv_fused(const void* x, const uint32_t* w, const void* scales, const void* biases,
+                        void* y, int64_t K, int64_t N, int32_t prologue, int32_t epilogue,
+                        const void* norm_w, const void* resid, const void* post_w,
+                        const void* scalar, void* h_out, float eps, void* stream);
+
 size_t hyb_sdpa_decode_scratch_bytes(int32_t n_heads, int32_t n_kv, int32_t head_dim, int32_t max_keys);
 HypStatus hyb_sdpa_decode(const void* q, const void* k_cache, const void* v_cache, void* out,
                           int32_t n_heads, int32_t n_kv, int32_t head_dim, int32_t capacity,
@@ -105,6 +123,13 @@ HypStatus hyb_qkv_post(const void* qkv, int32_t L, int32_t ld, int32_t n_heads, 
  * bf16(1 + N(0, 0.02)). Same validation and errors as hyp_model_load.
  */
 HypStatus hyb_model_load_synthetic(HypModel model, const HypGeometryParams* geometry, uint64_t seed);
+
+/*
+ * Attention rounding of a loaded model: 0 (default) rounds scores and softmax
+ * probabilities to bf16 as MLX's CPU-stream SDPA does (the semantics the parity
+ * oracle follows); 1 keeps them in fp32 as MLX's fused Metal decode kernel does.
+ */
+HypStatus hyb_model_set_attention_rounding(HypModel model, int32_t mode);
 
 /* The CUDA stream the model's kernels run on (for event timing). */
 HypStatus hyb_model_stream(HypModel model, void** out_stream);
