@@ -244,13 +244,16 @@ def run_qmv(args, rank, world, local):
     items = [it for lay in layers for it in lay] + [("lm_head", K, N, lw, ls, lb, lx, ly)]
     step_bytes = sum(qmv_bytes(it[1], it[2]) for it in items)
     launches = len(items)
+    # the decode engine's resident layout: every matrix repacked once (not timed)
+    packs = [ops.qmv_pack(it[3], it[4], it[5]) for it in items]
+    torch.cuda.synchronize()
 
     stream = torch.cuda.Stream(device=dev)
 
-    def launch_all(x_override=None):
-        for it in items:
+    def launch_all():
+        for it, pk in zip(items, packs):
             name, K_, N_, w, s, b, x, y = it
-            ops.quantized_matmul(x.view(1, K_), w, s, b, out=y.view(1, N_))
+            ops.qmv_packed(x, pk, K_, N_, out=y)
 
     torch.cuda.synchronize()
     with torch.cuda.stream(stream):
@@ -281,14 +284,17 @@ def run_qmv(args, rank, world, local):
     # ---- per-shape kernel timing (each shape over its distinct copies, graph of back-to-back launches)
     per_shape = []
     shape_time = {}
-    for name, K_, N_ in PROJ + [LM_HEAD]:
-        sel = [it for it in items if it[0] == name]
+    for (name, K_, N_), layout in [(sh, lay) for sh in PROJ + [LM_HEAD] for lay in ("packed", "mlx")]:
+        sel = [(it, pk) for it, pk in zip(items, packs) if it[0] == name]
         reps = max(1, 48 // len(sel))
         g = torch.cuda.CUDAGraph()
         with torch.cuda.graph(g, stream=stream):
             for _ in range(reps):
-                for it in sel:
-                    ops.quantized_matmul(it[6].view(1, K_), it[3], it[4], it[5], out=it[7].view(1, N_))
+                for it, pk in sel:
+                    if layout == "packed":
+                        ops.qmv_packed(it[6], pk, K_, N_, out=it[7])
+                    else:
+                        ops.quantized_matmul(it[6].view(1, K_), it[3], it[4], it[5], out=it[7].view(1, N_))
         with torch.cuda.stream(stream):
             for _ in range(3):
                 g.replay()
@@ -302,9 +308,10 @@ def run_qmv(args, rank, world, local):
             torch.cuda.synchronize()
         per_launch_us = e0.elapsed_time(e1) * 1e3 / (R * reps * len(sel))
         gbs = qmv_bytes(K_, N_) / (per_launch_us * 1e-6) / 1e9
-        shape_time[name] = per_launch_us
-        per_shape.append({"shape": f"{name} K={K_} N={N_}", "us": round(per_launch_us, 2),
-                          "GB/s": round(gbs, 1)})
+        if layout == "packed":
+            shape_time[name] = per_launch_us
+        per_shape.append({"shape": f"{name} K={K_} N={N_}", "layout": layout, "us": round(per_launch_us, 2),
+                          "GB/s": round(gbs, 1), "frac": round(gbs / peaks()[0], 3)})
         del g
     # mix-weighted kernel achieved bandwidth (kernel time only, no inter-launch gaps)
     kern_us = sum(shape_time[it[0]] for it in items)
@@ -329,9 +336,9 @@ def run_qmv(args, rank, world, local):
         dx.copy_(hx, non_blocking=True)
         for i, it in enumerate(items):
             _, K_, N_, w, s, b, _, _ = it
-            L.hyb_quantized_matmul(ctypes.c_void_p(dx.data_ptr() + 2 * offs_x[i]), ctypes.c_void_p(w.data_ptr()),
-                                   ctypes.c_void_p(s.data_ptr()), ctypes.c_void_p(b.data_ptr()),
-                                   ctypes.c_void_p(dy.data_ptr() + 2 * offs_y[i]), 1, K_, N_, 64, 4, s_ptr)
+            L.hyb_qmv_packed(ctypes.c_void_p(dx.data_ptr() + 2 * offs_x[i]), ctypes.c_void_p(packs[i].data_ptr()),
+                             ctypes.c_void_p(dy.data_ptr() + 2 * offs_y[i]), K_, N_, 0, 0, None, None, None, None,
+                             None, 1e-6, s_ptr)
         hy.copy_(dy, non_blocking=True)
 
     with torch.cuda.stream(stream):
@@ -366,17 +373,63 @@ def run_qmv(args, rank, world, local):
                    "step_bytes": step_bytes, "parallelism": f"replicas x{world}"},
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s",
                      "frac": round(achieved / hbm, 4), "traffic": traffic, "peak_source": src,
-                     "kernel": "qmv_kernel (mix-weighted over the step's 337 launches)"},
+                     "kernel": "qmv_packed_kernel (mix-weighted over the step's 337 launches)"},
         "per_shape": per_shape,
         "gpu_launches": launches * args.steps,
         "e2e": {"value": round(e2e_val, 1), "unit": "GB/s",
                 "h2d_bytes_per_step": int(hx.numel() * 2), "d2h_bytes_per_step": int(hy.numel() * 2),
-                "path": "hyb_quantized_matmul per projection via ctypes, host x/y copied each step"},
+                "path": "hyb_qmv_packed per projection via ctypes, host x/y copied each step"},
         "clocks": clk.summary(),
     }
     if world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_qmv_baseline(args.cpu_seconds)
     print(json.dumps(line), flush=True)
+
+
+# ------------------------------------------------------------------ single qmv shape (profiling)
+def run_qmv_shape(args, rank, world, local):
+    """One cfg-1 shape over enough distinct copies to exceed 2x L2 (the workload the
+    committed ncu summaries under profiles/ capture)."""
+    import torch
+    from hyperion_b200 import ops
+    K, N = (int(v) for v in args.shape.split(","))
+    dev = torch.device("cuda", local)
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(99)
+    nbytes = qmv_bytes(K, N)
+    copies = max(1, -(-2 * 126 * 2 ** 20 // nbytes))
+    bufs = []
+    for _ in range(copies):
+        w, s, b = make_q4(N, K, gen, dev)
+        pk = ops.qmv_pack(w, s, b) if args.layout == "packed" else None
+        if pk is not None:
+            del w, s, b
+            w = s = b = None
+        bufs.append((w, s, b, pk, torch.randn(1, K, device=dev, generator=gen).to(torch.bfloat16),
+                     torch.empty(1, N, dtype=torch.bfloat16, device=dev)))
+
+    def one(w, s, b, pk, x, y):
+        if pk is not None:
+            ops.qmv_packed(x, pk, K, N, out=y)
+        else:
+            ops.quantized_matmul(x, w, s, b, out=y)
+
+    for bf in bufs:  # warm-up launches (also what ncu's -s skips)
+        one(*bf)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    reps = max(1, args.steps)
+    e0.record()
+    for _ in range(reps):
+        for bf in bufs:
+            one(*bf)
+    e1.record()
+    torch.cuda.synchronize()
+    us = e0.elapsed_time(e1) * 1e3 / (reps * copies)
+    if rank == 0:
+        print(json.dumps({"workload": f"qmv K={K} N={N} ({args.layout} layout)", "copies": copies,
+                          "us_per_launch": round(us, 2),
+                          "GB/s": round(nbytes / (us * 1e-6) / 1e9, 1), "bytes_per_launch": nbytes}), flush=True)
 
 
 # ------------------------------------------------------------------ 12B decode (ours)
@@ -436,7 +489,9 @@ def main():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="qmv", choices=["qmv", "decode"])
+    ap.add_argument("--workload", default="qmv", choices=["qmv", "decode", "qmv-shape"])
+    ap.add_argument("--shape", default="3840,262144", help="K,N for --workload qmv-shape")
+    ap.add_argument("--layout", default="packed", choices=["packed", "mlx"], help="weights for qmv-shape")
     ap.add_argument("--ctx", type=int, default=4096)
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -453,6 +508,8 @@ def main():
     try:
         if args.workload == "qmv":
             run_qmv(args, rank, world, local)
+        elif args.workload == "qmv-shape":
+            run_qmv_shape(args, rank, world, local)
         else:
             run_decode(args, rank, world, local)
     finally:

@@ -101,7 +101,8 @@ ABI_FUNCTIONS = [
     "hyp_step_result_free", "hyp_step_result_fields",
 ]
 EXT_FUNCTIONS = [
-    "hyb_build_info", "hyb_quantized_matmul", "hyb_qmv_fused", "hyb_sdpa_decode_scratch_bytes", "hyb_sdpa_decode",
+    "hyb_build_info", "hyb_quantized_matmul", "hyb_qmv_fused", "hyb_qmv_packed_bytes", "hyb_qmv_pack",
+    "hyb_qmv_packed", "hyb_sdpa_decode_scratch_bytes", "hyb_sdpa_decode",
     "hyb_sdpa_prefill", "hyb_rms_norm", "hyb_qkv_post", "hyb_model_load_synthetic",
     "hyb_model_set_attention_rounding", "hyb_model_stream",
     "hyb_kv_copy_layer", "hyb_kv_cursor", "hyb_prefill_logits", "hyb_decode_logits", "hyb_decode_forced",
@@ -140,6 +141,8 @@ def lib() -> ctypes.CDLL:
         "hyb_build_info": [c.c_char_p, c.c_size_t],
         "hyb_quantized_matmul": [P, P, P, P, P, c.c_int64, c.c_int64, c.c_int64, c.c_int32, c.c_int32, P],
         "hyb_qmv_fused": [P, P, P, P, P, c.c_int64, c.c_int64, c.c_int32, c.c_int32, P, P, P, P, P, c.c_float, P],
+        "hyb_qmv_pack": [P, P, P, c.c_int64, c.c_int64, P, P],
+        "hyb_qmv_packed": [P, P, P, c.c_int64, c.c_int64, c.c_int32, c.c_int32, P, P, P, P, P, c.c_float, P],
         "hyb_sdpa_decode": [P, P, P, P, c.c_int32, c.c_int32, c.c_int32, c.c_int32, c.c_int32, c.c_int32,
                             c.c_float, c.c_float, c.c_int32, P, c.c_size_t, P],
         "hyb_sdpa_prefill": [P, P, P, P, c.c_int32, c.c_int32, c.c_int32, c.c_int32, c.c_int32, c.c_int32,
@@ -163,6 +166,8 @@ def lib() -> ctypes.CDLL:
         fn.restype = S
     L.hyb_sdpa_decode_scratch_bytes.argtypes = [c.c_int32, c.c_int32, c.c_int32, c.c_int32]
     L.hyb_sdpa_decode_scratch_bytes.restype = c.c_size_t
+    L.hyb_qmv_packed_bytes.argtypes = [c.c_int64, c.c_int64]
+    L.hyb_qmv_packed_bytes.restype = c.c_size_t
     _lib = L
     return L
 

@@ -209,6 +209,21 @@ void Model::init_common(const Geometry& g) {
     }
 }
 
+void Model::pack_all() {
+    auto pack = [&](QLin& q) {
+        q.packed.reset(qmv_packed_bytes(q.K, q.N));
+        launch_qmv_pack(q.w.p, q.s.p, q.b.p, q.K, q.N, q.packed.p, stream_);
+    };
+    for (auto& L : layers_) {
+        pack(L.qkv);
+        pack(L.o);
+        pack(L.gateup);
+        pack(L.down);
+    }
+    pack(embed_);
+    HYB_CUDA(cudaStreamSynchronize(stream_));
+}
+
 void Model::load_synthetic(const Geometry& g, uint64_t seed) {
     init_common(g);
     const int H = static_cast<int>(g.hidden), I = static_cast<int>(g.intermediate);
@@ -229,6 +244,7 @@ void Model::load_synthetic(const Geometry& g, uint64_t seed) {
         synth_norm(L.scalar, 1, ++tag, stream_);
     }
     HYB_CUDA(cudaStreamSynchronize(stream_));
+    pack_all();
     loaded_ = true;
 }
 
@@ -347,6 +363,7 @@ void Model::load_dir(const Geometry& g, const std::string& dir) {
             HYB_CUDA(cudaMemcpy(L.scalar.p, t.data, 2, cudaMemcpyHostToDevice));
         }
     }
+    pack_all();
     loaded_ = true;
 }
 
@@ -565,6 +582,7 @@ StepOut Model::epilogue(const bf16* final_row, bool fused_prologue, const bf16* 
     const Geometry& g = geo_;
     QmvParams p;
     p.w = embed_.w.p;
+    p.packed = embed_.packed.p;
     p.s = embed_.s.p;
     p.b = embed_.b.p;
     p.y = ws_.logits.p;
@@ -648,6 +666,7 @@ void Model::decode_layers(KvState& kv) {
         // post-MLP residual/scalar) fused into its prologue
         QmvParams p;
         p.w = W.qkv.w.p;
+        p.packed = W.qkv.packed.p;
         p.s = W.qkv.s.p;
         p.b = W.qkv.b.p;
         p.y = ws_.qkv.p;
@@ -720,17 +739,19 @@ void Model::decode_layers(KvState& kv) {
         launch_decode_attn(ap, st);
         QmvParams po;
         po.w = W.o.w.p;
+        po.packed = W.o.packed.p;
         po.s = W.o.s.p;
         po.b = W.o.b.p;
         po.x = ws_.attn.p;
         po.y = ws_.o.p;
         po.K = W.o.K;
         po.N = H;
-        launch_qmv(po, st, false);
+        launch_qmv(po, st, true);
         // gate/up with the post-attention residual + pre-MLP norm in the prologue
         // and GeGLU in the epilogue
         QmvParams pg;
         pg.w = W.gateup.w.p;
+        pg.packed = W.gateup.packed.p;
         pg.s = W.gateup.s.p;
         pg.b = W.gateup.b.p;
         pg.x = ws_.o.p;
@@ -748,6 +769,7 @@ void Model::decode_layers(KvState& kv) {
         launch_qmv(pg, st, true);
         QmvParams pd;
         pd.w = W.down.w.p;
+        pd.packed = W.down.packed.p;
         pd.s = W.down.s.p;
         pd.b = W.down.b.p;
         pd.x = ws_.act.p;

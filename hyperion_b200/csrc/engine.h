@@ -54,8 +54,9 @@ struct DevPtr {
 };
 
 struct QLin {
-    DevPtr<uint32_t> w;
+    DevPtr<uint32_t> w;               // MLX layout (prefill GEMM, embedding gather)
     DevPtr<bf16> s, b;
+    DevPtr<unsigned char> packed;     // packed resident layout streamed by the decode qmv
     int N = 0, K = 0;
 };
 
@@ -151,6 +152,7 @@ class Model {
 
   private:
     void init_common(const Geometry& g);
+    void pack_all();  // build the packed decode layout of every projection and the lm_head
     void ensure_workspace(int tokens, uint32_t max_keys);
     void forward_chunk(KvState& kv, int L, uint32_t offset);  // ids already in ws_.ids
     void decode_layers(KvState& kv);

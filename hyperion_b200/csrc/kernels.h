@@ -44,9 +44,17 @@ struct QmvParams {
     const bf16* scalar = nullptr;     // [1] layer_scalar multiplied after the add, or null
     bf16* h_out = nullptr;            // [K] new residual, written by CTA 0
     float eps = 1e-6f;
+    const void* packed = nullptr;     // packed resident layout (launch_qmv_packed); w/s/b unused then
 };
 
 void launch_qmv(const QmvParams& p, cudaStream_t stream, bool pdl = false);
+
+// Packed resident layout for the TMA-streamed qmv (see qmv_packed.cu): bytes for
+// an [N, K] matrix, the repack from the MLX layout, and the kernel itself.
+size_t qmv_packed_bytes(int K, int N);
+void launch_qmv_pack(const uint32_t* w, const bf16* s, const bf16* b, int K, int N, void* packed,
+                     cudaStream_t stream);
+void launch_qmv_packed(const QmvParams& p, cudaStream_t stream, bool pdl = false);
 
 // Prefill GEMM for M >= 2 (tensor cores; fp16 operands, fp32 accumulation).
 void launch_qmm(const bf16* x, const uint32_t* w, const bf16* s, const bf16* b, bf16* y,

@@ -93,6 +93,53 @@ HypStatus hyb_qmv_fused(const void* x, const uint32_t* w, const void* scales, co
     });
 }
 
+size_t hyb_qmv_packed_bytes(int64_t K, int64_t N) {
+    if (K <= 0 || K % 64 != 0 || N <= 0 || K > (1 << 20) || N > (1 << 30)) return 0;
+    return hyb::qmv_packed_bytes(static_cast<int>(K), static_cast<int>(N));
+}
+
+HypStatus hyb_qmv_pack(const uint32_t* w, const void* scales, const void* biases, int64_t K, int64_t N, void* packed,
+                       void* stream) {
+    if (!w || !scales || !biases || !packed) return hyb::abi_fail(HYP_STATUS_INVALID_ARGUMENT, "null pointer argument");
+    if (K <= 0 || K % 64 != 0 || N <= 0 || K > (1 << 20) || N > (1 << 30))
+        return hyb::abi_fail(HYP_STATUS_INVALID_ARGUMENT, "qmv_pack: bad shape");
+    if (!aligned16(w) || !aligned16(packed)) return hyb::abi_fail(HYP_STATUS_INVALID_ARGUMENT, "qmv_pack: w and packed must be 16-byte aligned");
+    return run([&] {
+        hyb::launch_qmv_pack(w, static_cast<const hyb::bf16*>(scales), static_cast<const hyb::bf16*>(biases),
+                             static_cast<int>(K), static_cast<int>(N), packed, as_stream(stream));
+    });
+}
+
+HypStatus hyb_qmv_packed(const void* x, const void* packed, void* y, int64_t K, int64_t N, int32_t prologue,
+                         int32_t epilogue, const void* norm_w, const void* resid, const void* post_w,
+                         const void* scalar, void* h_out, float eps, void* stream) {
+    if (!x || !packed || !y) return hyb::abi_fail(HYP_STATUS_INVALID_ARGUMENT, "null pointer argument");
+    if (K <= 0 || K % 64 != 0 || N <= 0 || K > (1 << 20) || N > (1 << 30))
+        return hyb::abi_fail(HYP_STATUS_INVALID_ARGUMENT, "qmv_packed: bad shape");
+    if (prologue < 0 || prologue > 2 || epilogue < 0 || epilogue > 1)
+        return hyb::abi_fail(HYP_STATUS_INVALID_ARGUMENT, "qmv_packed: unknown prologue/epilogue");
+    if (prologue >= 1 && !norm_w) return hyb::abi_fail(HYP_STATUS_INVALID_ARGUMENT, "qmv_packed: norm_w is required");
+    if (prologue == 2 && (!resid || !post_w)) return hyb::abi_fail(HYP_STATUS_INVALID_ARGUMENT, "qmv_packed: resid and post_w are required");
+    if (epilogue == 1 && N % 32 != 0) return hyb::abi_fail(HYP_STATUS_INVALID_ARGUMENT, "qmv_packed: GeGLU rows must be a multiple of 32");
+    return run([&] {
+        hyb::QmvParams p;
+        p.x = static_cast<const hyb::bf16*>(x);
+        p.packed = packed;
+        p.y = static_cast<hyb::bf16*>(y);
+        p.K = static_cast<int>(K);
+        p.N = static_cast<int>(N);
+        p.prologue = static_cast<hyb::QmvPrologue>(prologue);
+        p.epilogue = static_cast<hyb::QmvEpilogue>(epilogue);
+        p.norm_w = static_cast<const hyb::bf16*>(norm_w);
+        p.resid = static_cast<const hyb::bf16*>(resid);
+        p.post_w = static_cast<const hyb::bf16*>(post_w);
+        p.scalar = static_cast<const hyb::bf16*>(scalar);
+        p.h_out = static_cast<hyb::bf16*>(h_out);
+        p.eps = eps;
+        hyb::launch_qmv_packed(p, as_stream(stream), true);
+    });
+}
+
 size_t hyb_sdpa_decode_scratch_bytes(int32_t n_heads, int32_t n_kv, int32_t head_dim, int32_t max_keys) {
     if (n_heads <= 0 || n_kv <= 0 || head_dim <= 0 || max_keys <= 0) return 0;
     return hyb::decode_attn_scratch_bytes(n_heads, n_kv, head_dim, max_keys);

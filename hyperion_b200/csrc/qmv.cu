@@ -330,6 +330,10 @@ void launch_rt(const QmvParams& p, cudaStream_t stream, bool pdl) {
 }  // namespace
 
 void launch_qmv(const QmvParams& p, cudaStream_t stream, bool pdl) {
+    if (p.packed) {  // packed resident layout: the TMA-streamed kernel
+        launch_qmv_packed(p, stream, pdl);
+        return;
+    }
     if (p.K <= 0 || p.K % 64 != 0 || p.N <= 0) throw ArgError("qmv: K must be a positive multiple of 64");
     if (p.epilogue == QmvEpilogue::kGeglu) {
         if (p.N % 32 != 0) throw ArgError("qmv geglu: interleaved rows must be a multiple of 32");

@@ -1,0 +1,467 @@
+// Batch-1 affine Q4/g64 qmv over the engine's packed resident weight layout,
+// streamed with TMA bulk copies (cp.async.bulk + mbarrier) into per-warp
+// shared-memory rings.
+//
+// Same mathematics and MMA formulation as qmv.cu (codes as bf16 128 + q on the
+// A side, per-unit group-masked activations on the B side, per-group
+// scale/bias fold in fp32); only the data movement differs.
+//
+// Packed layout (built once at load by launch_qmv_pack from the MLX layout
+// [N, K/8] u32 + [N, K/64] bf16 scales/biases):
+//   rows are grouped in 16-row blocks (zero padded), K in 512-wide units of
+//   8 groups (the last unit may hold fewer). For block rb and unit u the item is
+//   one contiguous run of nv * 144 bytes, nv = 8 * ceil(gc / 2) valid lanes:
+//     chunk c (0..7) of every valid lane, then one 16-byte scale/bias record per
+//     lane. Lane (g, t) owns rows g and g + 8 and groups 2t, 2t + 1 of the unit;
+//     chunk c = (row h = c / 4, 16-byte piece c % 4 of its 64-byte segment).
+//     The record holds bf16 {sA(g), sB(g), sA(g+8), sB(g+8), bA(g), bB(g),
+//     bA(g+8), bB(g+8)}. Lane rank = g * tv + t with tv = ceil(gc / 2).
+//   A warp's reads of one chunk index are 32 consecutive 16-byte words, so the
+//   shared-memory reads are conflict-free, and each item is a single bulk copy.
+#include "kernels.h"
+
+#include <algorithm>
+
+namespace hyb {
+
+__device__ int g_qmv_wait_timeouts = 0;  // set if an mbarrier wait gave up (never expected)
+
+namespace {
+
+// Two CTAs per SM (16 warps, <= 128 registers, <= ~113 KB shared memory each) so
+// that latency is hidden across warps and the next kernel's CTAs can become
+// resident during this one's tail (programmatic dependent launch).
+constexpr int kWarps = 8;
+constexpr int kThreads = kWarps * 32;
+constexpr int kStages = 2;
+constexpr int kCtasPerSm = 2;
+constexpr int kItemMax = 32 * 144;  // 4608 bytes
+
+struct PackGeo {
+    int K, N, G, nunits, nrb;
+    int gc_last, tv_last, item_last;  // last unit's group count, valid t count, bytes
+    long long rb_bytes;               // bytes of one 16-row block
+};
+
+__host__ __device__ inline PackGeo pack_geo(int K, int N) {
+    PackGeo p;
+    p.K = K;
+    p.N = N;
+    p.G = K / 64;
+    p.nunits = (p.G + 7) / 8;
+    p.nrb = (N + 15) / 16;
+    p.gc_last = p.G - 8 * (p.nunits - 1);
+    p.tv_last = (p.gc_last + 1) / 2;
+    p.item_last = 8 * p.tv_last * 144;
+    p.rb_bytes = static_cast<long long>(p.nunits - 1) * kItemMax + p.item_last;
+    return p;
+}
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
+}
+
+// Bounded wait on an mbarrier phase: gives up (and records it) instead of hanging.
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t phase) {
+    for (int it = 0; it < (1 << 20); ++it) {
+        uint32_t done;
+        asm volatile(
+            "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+            : "=r"(done)
+            : "r"(bar), "r"(phase)
+            : "memory");
+        if (done) return true;
+    }
+    atomicAdd(&g_qmv_wait_timeouts, 1);
+    return false;
+}
+
+__device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
+        "l"(src), "r"(bytes), "r"(bar)
+        : "memory");
+}
+
+__device__ __forceinline__ void fence_proxy_async() {
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+__device__ __forceinline__ float block_sum(float v, float* tmp) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    v = warp_sum(v);
+    __syncthreads();
+    if (lane == 0) tmp[warp] = v;
+    __syncthreads();
+    float r = (lane < kWarps) ? tmp[lane] : 0.f;
+    return warp_sum(r);
+}
+
+__device__ __forceinline__ float gelu_tanh_bf16ops(float x) {
+    const float kC = 0.044677734375f;  // bf16(0.044715)
+    const float kK = 0.796875f;        // bf16(sqrt(2/pi))
+    float x2 = rbf(x * x);
+    float x3 = rbf(x * x2);
+    float in = rbf(kC * x3);
+    in = rbf(in + x);
+    in = rbf(kK * in);
+    float th = rbf(tanhf(in));
+    float hx = rbf(0.5f * x);
+    float op = rbf(1.0f + th);
+    return rbf(hx * op);
+}
+
+// GEGLU: the interleaved gate/up matrix alternates 16-row gate blocks (even) and the
+// matching up blocks (odd); a CTA processes them as one pair so the epilogue can
+// combine them. BG = row blocks per work group.
+template <bool GEGLU>
+__global__ void __launch_bounds__(kThreads, kCtasPerSm) qmv_packed_kernel(const QmvParams p) {
+    constexpr int BG = GEGLU ? 2 : 1;
+    extern __shared__ __align__(128) unsigned char smem_raw[];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int g = lane >> 2, t = lane & 3;
+    const PackGeo pg = pack_geo(p.K, p.N);
+    const unsigned char* packed = static_cast<const unsigned char*>(p.packed);
+
+    // shared memory: [rings kWarps x kStages x 4608][mbar kWarps x kStages][xp K/2 u32][zero 32]
+    //                [xsum G][red 2 x kWarps x 16][pair 32][tmp 32][xf K (prologue)]
+    unsigned char* ring = smem_raw;
+    uint64_t* bars = reinterpret_cast<uint64_t*>(ring + kWarps * kStages * kItemMax);
+    uint32_t* xp = reinterpret_cast<uint32_t*>(bars + kWarps * kStages);
+    uint32_t* zero_page = xp + p.K / 2;
+    float* xsum = reinterpret_cast<float*>(zero_page + 32);
+    float* red = xsum + ((pg.G + 3) & ~3);
+    float* pairbuf = red + 2 * kWarps * 16;
+    float* tmp = pairbuf + 32;
+    float* xf = tmp + 32;
+
+    unsigned char* my_ring = ring + warp * kStages * kItemMax;
+    const uint32_t my_bar0 = smem_u32(bars + warp * kStages);
+
+    const int n_groups = (pg.nrb + BG - 1) / BG;
+    const int my_units = (warp < pg.nunits) ? (pg.nunits - warp + kWarps - 1) / kWarps : 0;
+    const int my_groups = (static_cast<int>(blockIdx.x) < n_groups)
+                              ? (n_groups - static_cast<int>(blockIdx.x) + static_cast<int>(gridDim.x) - 1) / gridDim.x
+                              : 0;
+    const int per_group = BG * my_units;
+    const int n_items = my_groups * per_group;
+
+    if (lane == 0) {
+        for (int s = 0; s < kStages; ++s) mbar_init(my_bar0 + 8 * s, 1);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    __syncwarp();
+
+    auto issue = [&](int i) {
+        if (lane == 0) {
+            const int grp = static_cast<int>(blockIdx.x) + (i / per_group) * static_cast<int>(gridDim.x);
+            const int rb = grp * BG + (i / my_units) % BG;
+            const int unit = warp + (i % my_units) * kWarps;
+            if (rb < pg.nrb) {
+                const unsigned char* src = packed + rb * pg.rb_bytes + static_cast<long long>(unit) * kItemMax;
+                const uint32_t bytes =
+                    (unit == pg.nunits - 1) ? static_cast<uint32_t>(pg.item_last) : static_cast<uint32_t>(kItemMax);
+                const int s = i % kStages;
+                const uint32_t bar = my_bar0 + 8 * s;
+                mbar_expect_tx(bar, bytes);
+                bulk_g2s(smem_u32(my_ring + s * kItemMax), src, bytes, bar);
+            } else {
+                // a padding block of an odd block count: complete the phase without data
+                asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(my_bar0 + 8 * (i % kStages)) : "memory");
+            }
+        }
+    };
+    // weights do not depend on the previous kernel: start streaming before the PDL wait
+    for (int i = 0; i < kStages - 1 && i < n_items; ++i) issue(i);
+
+    pdl_wait();
+    if (threadIdx.x < 32) zero_page[threadIdx.x] = 0u;
+    const int K = p.K;
+    if (p.prologue == QmvPrologue::kNone) {
+        // One cooperative round trip: 16-byte chunk j of x holds x[8j .. 8j+7], which is
+        // exactly the four permuted pairs xp[4j .. 4j+3] = (x[8j+p], x[8j+p+4]), p < 4.
+        // The 8 chunks of a group sit in 8 consecutive lanes, which reduce its sum.
+        const uint4* xv = reinterpret_cast<const uint4*>(p.x);
+        for (int j0 = 0; j0 < K / 8; j0 += kThreads) {
+            const int j = j0 + static_cast<int>(threadIdx.x);
+            uint4 v = make_uint4(0, 0, 0, 0);
+            if (j < K / 8) v = xv[j];
+            const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+            float part = 0.f;
+#pragma unroll
+            for (int q = 0; q < 4; ++q) part += __uint_as_float(w[q] << 16) + __uint_as_float(w[q] & 0xFFFF0000u);
+            if (j < K / 8) {
+                // pairs: p = 0: (w0.lo, w2.lo), p = 1: (w0.hi, w2.hi), p = 2: (w1.lo, w3.lo), p = 3: (w1.hi, w3.hi)
+                uint4 o;
+                o.x = (w[0] & 0xFFFFu) | (w[2] << 16);
+                o.y = (w[0] >> 16) | (w[2] & 0xFFFF0000u);
+                o.z = (w[1] & 0xFFFFu) | (w[3] << 16);
+                o.w = (w[1] >> 16) | (w[3] & 0xFFFF0000u);
+                *reinterpret_cast<uint4*>(xp + 4 * j) = o;
+            }
+            part += __shfl_xor_sync(0xffffffffu, part, 1);
+            part += __shfl_xor_sync(0xffffffffu, part, 2);
+            part += __shfl_xor_sync(0xffffffffu, part, 4);
+            if (j < K / 8 && (j & 7) == 0) xsum[j >> 3] = part;
+        }
+    } else {
+        float ss = 0.f;
+        for (int k = threadIdx.x; k < K; k += kThreads) {
+            float v = bf2f(p.x[k]);
+            xf[k] = v;
+            ss += v * v;
+        }
+        float tot = block_sum(ss, tmp);
+        float inv = 1.0f / sqrtf(tot / static_cast<float>(K) + p.eps);
+        if (p.prologue == QmvPrologue::kResidNorm) {
+            float ss2 = 0.f;
+            const float sc = p.scalar ? bf2f(p.scalar[0]) : 1.0f;
+            for (int k = threadIdx.x; k < K; k += kThreads) {
+                float nv = rbf(rbf(xf[k] * inv) * bf2f(p.post_w[k]));
+                float hv = rbf(bf2f(p.resid[k]) + nv);
+                if (p.scalar) hv = rbf(hv * sc);
+                xf[k] = hv;
+                ss2 += hv * hv;
+                if (blockIdx.x == 0 && p.h_out) p.h_out[k] = f2bf(hv);
+            }
+            tot = block_sum(ss2, tmp);
+            inv = 1.0f / sqrtf(tot / static_cast<float>(K) + p.eps);
+        }
+        for (int k = threadIdx.x; k < K; k += kThreads) xf[k] = rbf(rbf(xf[k] * inv) * bf2f(p.norm_w[k]));
+        __syncthreads();
+        for (int gr = warp; gr < pg.G; gr += kWarps) {
+            const float* xg = xf + gr * 64;
+            const int i = lane >> 2, pp = lane & 3;
+            float lo = xg[8 * i + pp], hi = xg[8 * i + pp + 4];
+            xp[gr * 32 + lane] = pack_bf2(f2bf(lo), f2bf(hi));
+            float sv = warp_sum(lo + hi);
+            if (lane == 0) xsum[gr] = sv;
+        }
+    }
+    __syncthreads();
+    pdl_launch_dependents();
+
+    uint32_t phase_bits = 0;  // one parity bit per stage
+    int buf = 0, it = 0;
+    for (int gi = 0; gi < my_groups; ++gi) {
+        const int grp = static_cast<int>(blockIdx.x) + gi * static_cast<int>(gridDim.x);
+        for (int j = 0; j < BG; ++j) {
+            const int rb = grp * BG + j;
+            float acc0 = 0.f, acc1 = 0.f;
+            for (int ui = 0; ui < my_units; ++ui, ++it) {
+                const int unit = warp + ui * kWarps;
+                if (it + kStages - 1 < n_items) {
+                    fence_proxy_async();  // earlier generic reads of the reused stage come first
+                    issue(it + kStages - 1);
+                }
+                const int s = it % kStages;
+                const bool ok = mbar_wait(my_bar0 + 8 * s, (phase_bits >> s) & 1u);
+                phase_bits ^= (1u << s);
+                if (!ok || rb >= pg.nrb) continue;
+                const int gc = (unit == pg.nunits - 1) ? pg.gc_last : 8;
+                const int tv = (gc + 1) / 2;
+                const int nv = 8 * tv;
+                const bool valid = t < tv;
+                const int rank = g * tv + t;
+                const unsigned char* st = my_ring + s * kItemMax;
+                uint4 wv[8];
+#pragma unroll
+                for (int c = 0; c < 8; ++c)
+                    wv[c] = valid ? *reinterpret_cast<const uint4*>(st + (c * nv + rank) * 16) : make_uint4(0, 0, 0, 0);
+                const uint4 sb =
+                    valid ? *reinterpret_cast<const uint4*>(st + (8 * nv + rank) * 16) : make_uint4(0, 0, 0, 0);
+                const int gA = unit * 8 + 2 * t;
+                const uint32_t* src0 = (g == 2 * t && gA < pg.G) ? xp + gA * 32 : zero_page;
+                const uint32_t* src1 = (g == 2 * t + 1 && gA + 1 < pg.G) ? xp + (gA + 1) * 32 : zero_page;
+                // four independent accumulator chains (one per nibble pair) shorten the
+                // MMA dependency chain to 8
+                float d[4][4];
+#pragma unroll
+                for (int q = 0; q < 4; ++q) d[q][0] = d[q][1] = d[q][2] = d[q][3] = 0.f;
+#pragma unroll
+                for (int i = 0; i < 8; ++i) {
+                    const uint4 b0v = *reinterpret_cast<const uint4*>(src0 + 4 * i);
+                    const uint4 b1v = *reinterpret_cast<const uint4*>(src1 + 4 * i);
+                    const uint32_t b0s[4] = {b0v.x, b0v.y, b0v.z, b0v.w};
+                    const uint32_t b1s[4] = {b1v.x, b1v.y, b1v.z, b1v.w};
+                    // word i of group A (chunks 0,1 row g; 4,5 row g+8) and group B (2,3 / 6,7)
+                    const uint4 ra0 = wv[i >> 2], ra1 = wv[4 + (i >> 2)];
+                    const uint4 rb0 = wv[2 + (i >> 2)], rb1 = wv[6 + (i >> 2)];
+                    const int cc = i & 3;
+                    const uint32_t xa0 = cc == 0 ? ra0.x : cc == 1 ? ra0.y : cc == 2 ? ra0.z : ra0.w;
+                    const uint32_t xa1 = cc == 0 ? ra1.x : cc == 1 ? ra1.y : cc == 2 ? ra1.z : ra1.w;
+                    const uint32_t xb0 = cc == 0 ? rb0.x : cc == 1 ? rb0.y : cc == 2 ? rb0.z : rb0.w;
+                    const uint32_t xb1 = cc == 0 ? rb1.x : cc == 1 ? rb1.y : cc == 2 ? rb1.z : rb1.w;
+#pragma unroll
+                    for (int pp = 0; pp < 4; ++pp) {
+                        const uint32_t a0 = lop3_and_or(xa0 >> (4 * pp), 0x000F000Fu, 0x43004300u);
+                        const uint32_t a1 = lop3_and_or(xa1 >> (4 * pp), 0x000F000Fu, 0x43004300u);
+                        const uint32_t a2 = lop3_and_or(xb0 >> (4 * pp), 0x000F000Fu, 0x43004300u);
+                        const uint32_t a3 = lop3_and_or(xb1 >> (4 * pp), 0x000F000Fu, 0x43004300u);
+                        mma_bf16_16816(d[pp], a0, a1, a2, a3, b0s[pp], b1s[pp]);
+                    }
+                }
+                float d0[4], d1[4];
+#pragma unroll
+                for (int c = 0; c < 4; ++c) {
+                    d0[c] = d[0][c] + d[2][c];
+                    d1[c] = d[1][c] + d[3][c];
+                }
+                const float xsA = (gA < pg.G) ? xsum[gA] : 0.f;
+                const float xsB = (gA + 1 < pg.G) ? xsum[gA + 1] : 0.f;
+                // record: {sA(g), sB(g), sA(g+8), sB(g+8), bA(g), bB(g), bA(g+8), bB(g+8)}
+                const float sA0 = __uint_as_float(sb.x << 16), sB0 = __uint_as_float(sb.x & 0xFFFF0000u);
+                const float sA1 = __uint_as_float(sb.y << 16), sB1 = __uint_as_float(sb.y & 0xFFFF0000u);
+                const float bA0 = __uint_as_float(sb.z << 16), bB0 = __uint_as_float(sb.z & 0xFFFF0000u);
+                const float bA1 = __uint_as_float(sb.w << 16), bB1 = __uint_as_float(sb.w & 0xFFFF0000u);
+                acc0 = fmaf(sA0, d0[0] + d1[0], acc0);
+                acc0 = fmaf(sB0, d0[1] + d1[1], acc0);
+                acc0 = fmaf(fmaf(-128.f, sA0, bA0), xsA, acc0);
+                acc0 = fmaf(fmaf(-128.f, sB0, bB0), xsB, acc0);
+                acc1 = fmaf(sA1, d0[2] + d1[2], acc1);
+                acc1 = fmaf(sB1, d0[3] + d1[3], acc1);
+                acc1 = fmaf(fmaf(-128.f, sA1, bA1), xsA, acc1);
+                acc1 = fmaf(fmaf(-128.f, sB1, bB1), xsB, acc1);
+            }
+            acc0 += __shfl_xor_sync(0xffffffffu, acc0, 1);
+            acc0 += __shfl_xor_sync(0xffffffffu, acc0, 2);
+            acc1 += __shfl_xor_sync(0xffffffffu, acc1, 1);
+            acc1 += __shfl_xor_sync(0xffffffffu, acc1, 2);
+            if (t == 0) {
+                red[(buf * kWarps + warp) * 16 + g] = acc0;
+                red[(buf * kWarps + warp) * 16 + g + 8] = acc1;
+            }
+            __syncthreads();
+            if (threadIdx.x < 16) {
+                float v = 0.f;
+#pragma unroll
+                for (int w = 0; w < kWarps; ++w) v += red[(buf * kWarps + w) * 16 + threadIdx.x];
+                if (!GEGLU) {
+                    const int row = rb * 16 + threadIdx.x;
+                    if (row < pg.N) p.y[row] = f2bf(v);
+                } else {
+                    pairbuf[j * 16 + threadIdx.x] = v;  // j = 0 gate rows, j = 1 up rows
+                    if (j == 1) {
+                        const float gv = pairbuf[threadIdx.x];
+                        const int row = grp * 16 + threadIdx.x;
+                        if (row < pg.N / 2) p.y[row] = f2bf(gelu_tanh_bf16ops(rbf(gv)) * rbf(v));
+                    }
+                }
+            }
+            buf ^= 1;
+        }
+    }
+}
+
+__global__ void qmv_pack_kernel(const uint32_t* __restrict__ w, const bf16* __restrict__ s,
+                                const bf16* __restrict__ b, int K, int N, unsigned char* __restrict__ out) {
+    const PackGeo pg = pack_geo(K, N);
+    // one thread per (row block, unit, rank): writes its 8 weight chunks and its record
+    const long long total = static_cast<long long>(pg.nrb) * pg.nunits * 32;
+    for (long long idx = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; idx < total;
+         idx += static_cast<long long>(gridDim.x) * blockDim.x) {
+        const int L = static_cast<int>(idx % 32);
+        const long long ru = idx / 32;
+        const int unit = static_cast<int>(ru % pg.nunits);
+        const int rb = static_cast<int>(ru / pg.nunits);
+        const int gc = (unit == pg.nunits - 1) ? pg.gc_last : 8;
+        const int tv = (gc + 1) / 2;
+        const int nv = 8 * tv;
+        const int g = L / 4, t = L % 4;
+        if (t >= tv) continue;
+        const int rank = g * tv + t;
+        unsigned char* item = out + rb * pg.rb_bytes + static_cast<long long>(unit) * kItemMax;
+        const int gA = unit * 8 + 2 * t, gB = gA + 1;
+        const int K8 = K / 8, G = pg.G;
+        for (int c = 0; c < 8; ++c) {
+            const int h = c / 4, q = c % 4;
+            const int row = rb * 16 + g + 8 * h;
+            const int grp = (q < 2) ? gA : gB;
+            uint4 v = make_uint4(0, 0, 0, 0);
+            if (row < N && grp < G) v = *reinterpret_cast<const uint4*>(w + static_cast<size_t>(row) * K8 + grp * 8 + 4 * (q & 1));
+            *reinterpret_cast<uint4*>(item + (c * nv + rank) * 16) = v;
+        }
+        uint16_t rec[8];
+        for (int h = 0; h < 2; ++h) {
+            const int row = rb * 16 + g + 8 * h;
+            const bool vr = row < N;
+            const uint16_t* sr = reinterpret_cast<const uint16_t*>(s) + static_cast<size_t>(row) * G;
+            const uint16_t* br = reinterpret_cast<const uint16_t*>(b) + static_cast<size_t>(row) * G;
+            rec[2 * h + 0] = (vr && gA < G) ? sr[gA] : 0;
+            rec[2 * h + 1] = (vr && gB < G) ? sr[gB] : 0;
+            rec[4 + 2 * h + 0] = (vr && gA < G) ? br[gA] : 0;
+            rec[4 + 2 * h + 1] = (vr && gB < G) ? br[gB] : 0;
+        }
+        *reinterpret_cast<uint4*>(item + (8 * nv + rank) * 16) = *reinterpret_cast<uint4*>(rec);
+    }
+}
+
+size_t packed_smem_bytes(int K, bool prologue) {
+    const int G = K / 64;
+    size_t b = static_cast<size_t>(kWarps) * kStages * kItemMax + kWarps * kStages * 8 +
+               static_cast<size_t>(K / 2) * 4 + 32 * 4 + static_cast<size_t>((G + 3) & ~3) * 4 +
+               (2 * kWarps * 16 + 32 + 32) * 4;  // red, pair, tmp
+    if (prologue) b += static_cast<size_t>(K) * 4;
+    return b;
+}
+
+}  // namespace
+
+size_t qmv_packed_bytes(int K, int N) {
+    const PackGeo pg = pack_geo(K, N);
+    return static_cast<size_t>(pg.rb_bytes) * pg.nrb;
+}
+
+void launch_qmv_pack(const uint32_t* w, const bf16* s, const bf16* b, int K, int N, void* packed,
+                     cudaStream_t stream) {
+    if (K <= 0 || K % 64 != 0 || N <= 0) throw ArgError("qmv_pack: K must be a positive multiple of 64");
+    const PackGeo pg = pack_geo(K, N);
+    const long long total = static_cast<long long>(pg.nrb) * pg.nunits * 32;
+    const int grid = static_cast<int>(std::min<long long>((total + 255) / 256, 65535));
+    qmv_pack_kernel<<<grid, 256, 0, stream>>>(w, s, b, K, N, static_cast<unsigned char*>(packed));
+    HYB_LAUNCH_CHECK("qmv_pack_kernel");
+}
+
+void launch_qmv_packed(const QmvParams& p, cudaStream_t stream, bool pdl) {
+    if (p.K <= 0 || p.K % 64 != 0 || p.N <= 0) throw ArgError("qmv: K must be a positive multiple of 64");
+    if (!p.packed) throw ArgError("qmv_packed: packed weights are required");
+    if ((reinterpret_cast<uintptr_t>(p.packed) & 15u) != 0) throw ArgError("qmv_packed: packed weights must be 16-byte aligned");
+    const bool pro = p.prologue != QmvPrologue::kNone;
+    const size_t smem = packed_smem_bytes(p.K, pro);
+    if (smem > 227 * 1024) throw ArgError("qmv_packed: K too large for the shared-memory plan");
+    int dev = 0;
+    HYB_CUDA(cudaGetDevice(&dev));
+    static int attr_dev = -1;
+    if (attr_dev != dev) {
+        HYB_CUDA(cudaFuncSetAttribute(qmv_packed_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024));
+        HYB_CUDA(cudaFuncSetAttribute(qmv_packed_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024));
+        attr_dev = dev;
+    }
+    const PackGeo pg = pack_geo(p.K, p.N);
+    const bool geglu = p.epilogue == QmvEpilogue::kGeglu;
+    if (geglu && p.N % 32 != 0) throw ArgError("qmv geglu: interleaved rows must be a multiple of 32");
+    const int groups = geglu ? (pg.nrb + 1) / 2 : pg.nrb;
+    const int grid = std::max(1, std::min(groups, kCtasPerSm * num_sms()));
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    if (geglu) HYB_CUDA(cudaLaunchKernelEx(&cfg, qmv_packed_kernel<true>, p));
+    else HYB_CUDA(cudaLaunchKernelEx(&cfg, qmv_packed_kernel<false>, p));
+}
+
+}  // namespace hyb

@@ -46,6 +46,26 @@ def qmv_fused(x, w, scales, biases, prologue=0, epilogue=0, norm_w=None, resid=N
     return out
 
 
+def qmv_pack(w, scales, biases, stream=None) -> torch.Tensor:
+    """Repack MLX-layout Q4/g64 weights into the decode engine's packed layout (uint8 tensor)."""
+    N, K8 = w.shape
+    K = K8 * 8
+    out = torch.empty(lib().hyb_qmv_packed_bytes(K, N), dtype=torch.uint8, device=w.device)
+    check(lib().hyb_qmv_pack(_p(w), _p(scales), _p(biases), K, N, _p(out), _stream(stream)))
+    return out
+
+
+def qmv_packed(x, packed, K, N, prologue=0, epilogue=0, norm_w=None, resid=None, post_w=None, scalar=None,
+               h_out=None, eps=1e-6, out=None, stream=None):
+    """Batch-1 qmv over packed weights (TMA-streamed kernel), same options as qmv_fused."""
+    if out is None:
+        out = torch.empty(N // 2 if epilogue == 1 else N, dtype=torch.bfloat16, device=x.device)
+    opt = lambda t: _p(t) if t is not None else None
+    check(lib().hyb_qmv_packed(_p(x), _p(packed), _p(out), K, N, prologue, epilogue, opt(norm_w), opt(resid),
+                               opt(post_w), opt(scalar), opt(h_out), eps, _stream(stream)))
+    return out
+
+
 class DecodeScratch:
     """Device workspace for hyb_sdpa_decode (zeroed once)."""
 

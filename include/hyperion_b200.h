@@ -74,6 +74,27 @@ HypStatus hyb_qmv_fused(const void* x, const uint32_t* w, const void* scales, co
                         const void* norm_w, const void* resid, const void* post_w,
                         const void* scalar, void* h_out, float eps, void* stream);
 
+/*
+ * Packed resident weight layout of the decode engine (no reference counterpart:
+ * a load-time transform of the same MLX affine Q4/g64 tensors, like the
+ * reference loader turning checkpoint tensors into its MLX arrays). Each 16-row x
+ * 512-code block becomes one contiguous record in the order the qmv kernel's
+ * tensor-core lanes consume it, with its scales and biases appended, so the
+ * kernel streams every block with a single TMA bulk copy.
+ *   hyb_qmv_packed_bytes: size of the packed form of an [N, K] matrix.
+ *   hyb_qmv_pack: repack w/scales/biases (MLX layout) into `packed` (device,
+ *   16-byte aligned). The MLX tensors may be freed afterwards.
+ *   hyb_qmv_packed: the batch-1 qmv (with the hyb_qmv_fused prologue/epilogue
+ *   options) reading the packed form; same results as hyb_qmv_fused.
+ */
+size_t hyb_qmv_packed_bytes(int64_t K, int64_t N);
+HypStatus hyb_qmv_pack(const uint32_t* w, const void* scales, const void* biases, int64_t K,
+                       int64_t N, void* packed, void* stream);
+HypStatus hyb_qmv_packed(const void* x, const void* packed, void* y, int64_t K, int64_t N,
+                         int32_t prologue, int32_t epilogue, const void* norm_w,
+                         const void* resid, const void* post_w, const void* scalar,
+                         void* h_out, float eps, void* stream);
+
 size_t hyb_sdpa_decode_scratch_bytes(int32_t n_heads, int32_t n_kv, int32_t head_dim, int32_t max_keys);
 HypStatus hyb_sdpa_decode(const void* q, const void* k_cache, const void* v_cache, void* out,
                           int32_t n_heads, int32_t n_kv, int32_t head_dim, int32_t capacity,

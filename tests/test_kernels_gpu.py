@@ -223,3 +223,50 @@ def test_qmv_fused_prologue_epilogue(built_lib, oracle_lib, K, N, prologue, epil
         want = go.bf(go.fl(go.gelu_tanh(g)) * go.fl(u)).reshape(-1)
     assert rel_l2(got, want) <= REL_L2_QMM
     assert (got == want).mean() >= 0.98
+
+
+@pytest.mark.parametrize("K,N", CFG1_SHAPES + [(64, 8), (128, 40), (576, 33), (192, 4096), (1024, 17)])
+def test_qmv_packed_layout(built_lib, oracle_lib, K, N):
+    """The TMA-streamed qmv over the packed resident layout (the decode engine's path)."""
+    from hyperion_b200 import ops
+    from oracle import gemma_oracle as go
+    import torch
+    rng = np.random.default_rng(K * 3 + N)
+    w, s, b = random_q4(rng, N, K)
+    x = f32_to_bf16_bits(rng.standard_normal((1, K), dtype=np.float32))
+    packed = ops.qmv_pack(dev(w), dev(s), dev(b))
+    y = host(ops.qmv_packed(dev(x).view(-1), packed, K, N))
+    torch.cuda.synchronize()
+    rows = np.arange(N) if N <= 20000 else np.sort(np.random.default_rng(9).choice(N, 8192, replace=False))
+    want = go.qmm(x, w[rows], s[rows], b[rows]).reshape(-1)
+    got = y[rows]
+    # a few dozen outputs make the rel-L2 of one-ulp flips noisy: small outputs get 1e-3
+    assert rel_l2(got, want) <= (REL_L2_QMM if N >= 256 else 1e-3)
+    assert within_one_ulp(got, want) >= 0.999
+    # the same sums as the MLX-layout kernel, up to fp32 summation order
+    y2 = host(ops.quantized_matmul(dev(x), dev(w), dev(s), dev(b))).reshape(-1)
+    assert within_one_ulp(y, y2) >= 0.999
+
+
+@pytest.mark.parametrize("K,N,prologue,epilogue,with_scalar", [
+    (256, 2048, 2, 1, False), (3840, 8192, 2, 0, True), (3840, 30720, 2, 1, False), (128, 64, 1, 1, True)])
+def test_qmv_packed_fused(built_lib, oracle_lib, K, N, prologue, epilogue, with_scalar):
+    """Packed path with the decode engine's fused prologues/epilogues vs the MLX-layout fused kernel."""
+    from hyperion_b200 import ops
+    import torch
+    rng = np.random.default_rng(K + 2 * N)
+    w, s, b = random_q4(rng, N, K)
+    x = f32_to_bf16_bits(rng.standard_normal(K, dtype=np.float32) * 2)
+    resid = f32_to_bf16_bits(rng.standard_normal(K, dtype=np.float32) * 4)
+    nw = f32_to_bf16_bits(1 + 0.02 * rng.standard_normal(K, dtype=np.float32))
+    pw = f32_to_bf16_bits(1 + 0.02 * rng.standard_normal(K, dtype=np.float32))
+    sc = f32_to_bf16_bits(np.asarray([1.015625], dtype=np.float32))
+    kw = dict(prologue=prologue, epilogue=epilogue, norm_w=dev(nw), resid=dev(resid) if prologue == 2 else None,
+              post_w=dev(pw) if prologue == 2 else None, scalar=dev(sc) if with_scalar else None)
+    h1 = torch.zeros(K, dtype=torch.bfloat16, device="cuda")
+    h2 = torch.zeros(K, dtype=torch.bfloat16, device="cuda")
+    ref = host(ops.qmv_fused(dev(x), dev(w), dev(s), dev(b), h_out=h1 if prologue == 2 else None, **kw))
+    packed = ops.qmv_pack(dev(w), dev(s), dev(b))
+    got = host(ops.qmv_packed(dev(x), packed, K, N, h_out=h2 if prologue == 2 else None, **kw))
+    assert within_one_ulp(got, ref) >= 0.999 and rel_l2(got, ref) <= REL_L2_QMM
+    assert np.array_equal(host(h1), host(h2))
