@@ -213,7 +213,9 @@ __global__ void gather_ring_kernel(const bf16* __restrict__ cache, int cap, int 
 }
 
 // ------------------------------------------------------------------ softcap + top-k
-constexpr int kTopK = 8;
+// The greedy epilogue needs the winner and the runner-up (near-tie flag); the
+// sampled epilogue works on the full host copy of the logits.
+constexpr int kTopK = 2;
 constexpr int kTkThreads = 256;
 
 // Insert (v, i) into a descending list; ties keep the smaller index first.
@@ -278,19 +280,42 @@ __global__ void softcap_topk_stage1(bf16* logits, int N, float cap, float* part_
     }
 }
 
+// Stage 2: one block merges the per-block candidates (strided scan + shared-memory tree).
 __global__ void softcap_topk_stage2(const float* part_val, const int* part_idx, int nparts, uint32_t* out_idx,
                                     float* out_val) {
-    if (threadIdx.x != 0) return;
     float vals[kTopK];
     int idx[kTopK];
+#pragma unroll
     for (int i = 0; i < kTopK; ++i) {
         vals[i] = -FLT_MAX;
         idx[i] = INT32_MAX;
     }
-    for (int p = 0; p < nparts * kTopK; ++p) topk_insert(vals, idx, part_val[p], part_idx[p]);
+    for (int p = threadIdx.x; p < nparts * kTopK; p += blockDim.x) topk_insert(vals, idx, part_val[p], part_idx[p]);
+    __shared__ float sv[kTkThreads * kTopK];
+    __shared__ int si[kTkThreads * kTopK];
+#pragma unroll
     for (int i = 0; i < kTopK; ++i) {
-        out_idx[i] = static_cast<uint32_t>(idx[i]);
-        out_val[i] = vals[i];
+        sv[threadIdx.x * kTopK + i] = vals[i];
+        si[threadIdx.x * kTopK + i] = idx[i];
+    }
+    __syncthreads();
+    for (int stride = kTkThreads / 2; stride > 0; stride >>= 1) {
+        if (threadIdx.x < stride) {
+            const int o = (threadIdx.x + stride) * kTopK;
+            for (int i = 0; i < kTopK; ++i) topk_insert(vals, idx, sv[o + i], si[o + i]);
+#pragma unroll
+            for (int i = 0; i < kTopK; ++i) {
+                sv[threadIdx.x * kTopK + i] = vals[i];
+                si[threadIdx.x * kTopK + i] = idx[i];
+            }
+        }
+        __syncthreads();
+    }
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < kTopK; ++i) {
+            out_idx[i] = static_cast<uint32_t>(idx[i]);
+            out_val[i] = vals[i];
+        }
     }
 }
 
@@ -357,7 +382,7 @@ void launch_softcap_topk(bf16* logits, int N, float cap, float* scratch, int scr
     int* pi = reinterpret_cast<int*>(scratch + nb * kTopK);
     softcap_topk_stage1<<<nb, kTkThreads, 0, stream>>>(logits, N, cap, pv, pi);
     HYB_LAUNCH_CHECK("softcap_topk_stage1");
-    softcap_topk_stage2<<<1, 32, 0, stream>>>(pv, pi, nb, out_idx, out_val);
+    softcap_topk_stage2<<<1, kTkThreads, 0, stream>>>(pv, pi, nb, out_idx, out_val);
     HYB_LAUNCH_CHECK("softcap_topk_stage2");
 }
 

@@ -613,7 +613,7 @@ StepOut Model::epilogue(const bf16* final_row, bool fused_prologue, const bf16* 
     }
     HYB_CUDA(cudaStreamSynchronize(stream_));
     StepOut out;
-    const int n = static_cast<int>(std::min<uint32_t>(8, g.vocab));
+    const int n = static_cast<int>(std::min<uint32_t>(2, g.vocab));  // device top-2: winner + runner-up
     for (int i = 0; i < n; ++i) {
         out.topk_idx[i] = ws_.h_topk_idx[i];
         out.topk_val[i] = ws_.h_topk_val[i];

@@ -36,6 +36,7 @@ constexpr int kThreads = kWarps * 32;
 constexpr int kStages = 2;
 constexpr int kCtasPerSm = 2;
 constexpr int kItemMax = 32 * 144;  // 4608 bytes
+constexpr int kMaxPrologueK = 8192; // norm prologues hold K/8 16-byte chunks in registers
 
 struct PackGeo {
     int K, N, G, nunits, nrb;
@@ -141,7 +142,6 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) qmv_packed_kernel(const 
     float* red = xsum + ((pg.G + 3) & ~3);
     float* pairbuf = red + 2 * kWarps * 16;
     float* tmp = pairbuf + 32;
-    float* xf = tmp + 32;
 
     unsigned char* my_ring = ring + warp * kStages * kItemMax;
     const uint32_t my_bar0 = smem_u32(bars + warp * kStages);
@@ -213,37 +213,85 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) qmv_packed_kernel(const 
             if (j < K / 8 && (j & 7) == 0) xsum[j >> 3] = part;
         }
     } else {
+        // Norm prologues in one round trip: every thread loads its 16-byte chunks of
+        // x (and resid, post_w, norm_w) with independent vector loads into registers,
+        // then the reductions and the permuted-pair writes work from registers.
+        constexpr int kMaxC = kMaxPrologueK / 8 / kThreads;
+        const int nch = K / 8;
+        const uint4* x4 = reinterpret_cast<const uint4*>(p.x);
+        const uint4* n4 = reinterpret_cast<const uint4*>(p.norm_w);
+        const bool resid = p.prologue == QmvPrologue::kResidNorm;
+        uint4 xv[kMaxC], nv4[kMaxC], rv[kMaxC], pv[kMaxC];
+#pragma unroll
+        for (int c = 0; c < kMaxC; ++c) {
+            const int j = static_cast<int>(threadIdx.x) + c * kThreads;
+            const uint4 z = make_uint4(0, 0, 0, 0);
+            xv[c] = j < nch ? x4[j] : z;
+            nv4[c] = j < nch ? n4[j] : z;
+            rv[c] = (resid && j < nch) ? reinterpret_cast<const uint4*>(p.resid)[j] : z;
+            pv[c] = (resid && j < nch) ? reinterpret_cast<const uint4*>(p.post_w)[j] : z;
+        }
+        auto lo = [](uint32_t w) { return __uint_as_float(w << 16); };
+        auto hi = [](uint32_t w) { return __uint_as_float(w & 0xFFFF0000u); };
         float ss = 0.f;
-        for (int k = threadIdx.x; k < K; k += kThreads) {
-            float v = bf2f(p.x[k]);
-            xf[k] = v;
-            ss += v * v;
+#pragma unroll
+        for (int c = 0; c < kMaxC; ++c) {
+            const uint32_t w[4] = {xv[c].x, xv[c].y, xv[c].z, xv[c].w};
+#pragma unroll
+            for (int q = 0; q < 4; ++q) ss += lo(w[q]) * lo(w[q]) + hi(w[q]) * hi(w[q]);
         }
-        float tot = block_sum(ss, tmp);
-        float inv = 1.0f / sqrtf(tot / static_cast<float>(K) + p.eps);
-        if (p.prologue == QmvPrologue::kResidNorm) {
-            float ss2 = 0.f;
+        float inv = 1.0f / sqrtf(block_sum(ss, tmp) / static_cast<float>(K) + p.eps);
+        if (resid) {
             const float sc = p.scalar ? bf2f(p.scalar[0]) : 1.0f;
-            for (int k = threadIdx.x; k < K; k += kThreads) {
-                float nv = rbf(rbf(xf[k] * inv) * bf2f(p.post_w[k]));
-                float hv = rbf(bf2f(p.resid[k]) + nv);
-                if (p.scalar) hv = rbf(hv * sc);
-                xf[k] = hv;
-                ss2 += hv * hv;
-                if (blockIdx.x == 0 && p.h_out) p.h_out[k] = f2bf(hv);
+            float ss2 = 0.f;
+#pragma unroll
+            for (int c = 0; c < kMaxC; ++c) {
+                uint32_t w[4] = {xv[c].x, xv[c].y, xv[c].z, xv[c].w};
+                const uint32_t r[4] = {rv[c].x, rv[c].y, rv[c].z, rv[c].w};
+                const uint32_t pw[4] = {pv[c].x, pv[c].y, pv[c].z, pv[c].w};
+#pragma unroll
+                for (int q = 0; q < 4; ++q) {
+                    float h0 = rbf(lo(r[q]) + rbf(rbf(lo(w[q]) * inv) * lo(pw[q])));
+                    float h1 = rbf(hi(r[q]) + rbf(rbf(hi(w[q]) * inv) * hi(pw[q])));
+                    if (p.scalar) {
+                        h0 = rbf(h0 * sc);
+                        h1 = rbf(h1 * sc);
+                    }
+                    ss2 += h0 * h0 + h1 * h1;
+                    w[q] = pack_bf2(f2bf(h0), f2bf(h1));
+                }
+                xv[c] = make_uint4(w[0], w[1], w[2], w[3]);
+                const int j = static_cast<int>(threadIdx.x) + c * kThreads;
+                if (blockIdx.x == 0 && p.h_out && j < nch) reinterpret_cast<uint4*>(p.h_out)[j] = xv[c];
             }
-            tot = block_sum(ss2, tmp);
-            inv = 1.0f / sqrtf(tot / static_cast<float>(K) + p.eps);
+            inv = 1.0f / sqrtf(block_sum(ss2, tmp) / static_cast<float>(K) + p.eps);
         }
-        for (int k = threadIdx.x; k < K; k += kThreads) xf[k] = rbf(rbf(xf[k] * inv) * bf2f(p.norm_w[k]));
-        __syncthreads();
-        for (int gr = warp; gr < pg.G; gr += kWarps) {
-            const float* xg = xf + gr * 64;
-            const int i = lane >> 2, pp = lane & 3;
-            float lo = xg[8 * i + pp], hi = xg[8 * i + pp + 4];
-            xp[gr * 32 + lane] = pack_bf2(f2bf(lo), f2bf(hi));
-            float sv = warp_sum(lo + hi);
-            if (lane == 0) xsum[gr] = sv;
+#pragma unroll
+        for (int c = 0; c < kMaxC; ++c) {
+            const int j = static_cast<int>(threadIdx.x) + c * kThreads;
+            const uint32_t w[4] = {xv[c].x, xv[c].y, xv[c].z, xv[c].w};
+            const uint32_t nw[4] = {nv4[c].x, nv4[c].y, nv4[c].z, nv4[c].w};
+            uint32_t o[4];
+            float part = 0.f;
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+                const float y0 = rbf(rbf(lo(w[q]) * inv) * lo(nw[q]));
+                const float y1 = rbf(rbf(hi(w[q]) * inv) * hi(nw[q]));
+                part += y0 + y1;
+                o[q] = pack_bf2(f2bf(y0), f2bf(y1));
+            }
+            if (j < nch) {
+                uint4 pr;  // permuted pairs (x[8j+p], x[8j+p+4])
+                pr.x = (o[0] & 0xFFFFu) | (o[2] << 16);
+                pr.y = (o[0] >> 16) | (o[2] & 0xFFFF0000u);
+                pr.z = (o[1] & 0xFFFFu) | (o[3] << 16);
+                pr.w = (o[1] >> 16) | (o[3] & 0xFFFF0000u);
+                *reinterpret_cast<uint4*>(xp + 4 * j) = pr;
+            }
+            part += __shfl_xor_sync(0xffffffffu, part, 1);
+            part += __shfl_xor_sync(0xffffffffu, part, 2);
+            part += __shfl_xor_sync(0xffffffffu, part, 4);
+            if (j < nch && (j & 7) == 0) xsum[j >> 3] = part;
         }
     }
     __syncthreads();
@@ -409,7 +457,7 @@ size_t packed_smem_bytes(int K, bool prologue) {
     size_t b = static_cast<size_t>(kWarps) * kStages * kItemMax + kWarps * kStages * 8 +
                static_cast<size_t>(K / 2) * 4 + 32 * 4 + static_cast<size_t>((G + 3) & ~3) * 4 +
                (2 * kWarps * 16 + 32 + 32) * 4;  // red, pair, tmp
-    if (prologue) b += static_cast<size_t>(K) * 4;
+    (void)prologue;  // the norm prologues work in registers
     return b;
 }
 
@@ -435,6 +483,8 @@ void launch_qmv_packed(const QmvParams& p, cudaStream_t stream, bool pdl) {
     if (!p.packed) throw ArgError("qmv_packed: packed weights are required");
     if ((reinterpret_cast<uintptr_t>(p.packed) & 15u) != 0) throw ArgError("qmv_packed: packed weights must be 16-byte aligned");
     const bool pro = p.prologue != QmvPrologue::kNone;
+    if (pro && p.K > kMaxPrologueK) throw ArgError("qmv_packed: norm prologues support K <= 8192");
+    if (reinterpret_cast<uintptr_t>(p.x) & 15u) throw ArgError("qmv_packed: x must be 16-byte aligned");
     const size_t smem = packed_smem_bytes(p.K, pro);
     if (smem > 227 * 1024) throw ArgError("qmv_packed: K too large for the shared-memory plan");
     int dev = 0;
