@@ -29,8 +29,15 @@
 
 #include <algorithm>
 #include <cfloat>
+#include <mutex>
 
 namespace hyb {
+
+// Fixed scratch for hyb_sdpa_decode_noalloc (see launch_decode_attn_noalloc below).
+// Every GPU that loads this library holds these bytes until the process exits.
+constexpr size_t kNoAllocScratchBytes = size_t(8) << 20;  // 8 MiB
+static __device__ __align__(256) unsigned char g_decode_noalloc_scratch[kNoAllocScratchBytes];
+
 namespace {
 
 constexpr int kDecThreads = 256;
@@ -516,6 +523,40 @@ void launch_decode_attn(const DecodeAttnParams& p, cudaStream_t stream) {
         case 512: launch_decode_rep<16>(p, sc, stream); break;
         default: throw ArgError("decode attention: head_dim must be 64, 128, 256 or 512");
     }
+}
+
+// Device address of g_decode_noalloc_scratch on the current device. Host code only
+// sees a host-side stand-in for the symbol, so the device address is looked up
+// once per device with cudaGetSymbolAddress (with that device current) and cached.
+static void* noalloc_scratch_on_current_device() {
+    static std::mutex mu;
+    static void* addr[64] = {};
+    int dev = 0;
+    HYB_CUDA(cudaGetDevice(&dev));
+    if (dev < 0 || dev >= 64) throw ArgError("sdpa_decode_noalloc: device index out of range");
+    std::lock_guard<std::mutex> lock(mu);
+    if (addr[dev] == nullptr) {
+        void* p = nullptr;
+        HYB_CUDA(cudaGetSymbolAddress(&p, g_decode_noalloc_scratch));
+        addr[dev] = p;
+    }
+    return addr[dev];
+}
+
+size_t decode_attn_noalloc_limit_bytes() { return kNoAllocScratchBytes; }
+
+void launch_decode_attn_noalloc(DecodeAttnParams p, cudaStream_t stream) {
+    const size_t need = decode_attn_scratch_bytes(p.n_heads, p.n_kv, p.hd, p.n_keys);
+    if (need > kNoAllocScratchBytes)
+        throw ArgError("sdpa_decode_noalloc: this call needs " + std::to_string(need) +
+                       " bytes of scratch, above the fixed 8 MiB (8388608-byte) device buffer");
+    void* scratch = noalloc_scratch_on_current_device();
+    // The buffer keeps whatever the previous call left; the per-KV-head completion
+    // counters must start at zero, so clear them for this call (no allocation).
+    HYB_CUDA(cudaMemsetAsync(scratch, 0, align256(sizeof(unsigned) * p.n_kv), stream));
+    p.scratch = scratch;
+    p.scratch_bytes = kNoAllocScratchBytes;
+    launch_decode_attn(p, stream);
 }
 
 void launch_prefill_attn(const PrefillAttnParams& p, cudaStream_t stream) {

@@ -136,6 +136,10 @@ struct DecodeAttnParams {
 };
 size_t decode_attn_scratch_bytes(int n_heads, int n_kv, int hd, int max_keys);
 void launch_decode_attn(const DecodeAttnParams& p, cudaStream_t stream);
+// The same attention with its scratch in a fixed file-scope device buffer
+// (p.scratch / p.scratch_bytes are ignored); throws ArgError above the limit.
+void launch_decode_attn_noalloc(DecodeAttnParams p, cudaStream_t stream);
+size_t decode_attn_noalloc_limit_bytes();
 
 // Prefill: q [Lq, H, hd] at positions q_pos0 + i; k/v [Lk, Hkv, hd] at k_pos0 + j.
 struct PrefillAttnParams {

@@ -177,6 +177,36 @@ HypStatus hyb_sdpa_decode(const void* q, const void* k_cache, const void* v_cach
     });
 }
 
+HypStatus hyb_sdpa_decode_noalloc(const void* q, const void* k_cache, const void* v_cache, void* out,
+                                  int32_t n_heads, int32_t n_kv, int32_t head_dim, int32_t capacity,
+                                  int32_t last_pos, int32_t n_keys, float scale, float softcap, int32_t rounding,
+                                  void* stream) {
+    if (!q || !k_cache || !v_cache || !out) return hyb::abi_fail(HYP_STATUS_INVALID_ARGUMENT, "null pointer argument");
+    if (n_heads <= 0 || n_kv <= 0 || n_heads % n_kv != 0 || n_keys <= 0 || capacity <= 0 || last_pos < n_keys - 1)
+        return hyb::abi_fail(HYP_STATUS_INVALID_ARGUMENT, "sdpa_decode_noalloc: bad shape");
+    if (n_keys > capacity)
+        return hyb::abi_fail(HYP_STATUS_INVALID_ARGUMENT, "sdpa_decode_noalloc: n_keys exceeds the cache capacity");
+    if (head_dim != 64 && head_dim != 128 && head_dim != 256 && head_dim != 512)
+        return hyb::abi_fail(HYP_STATUS_UNSUPPORTED, "sdpa_decode_noalloc: head_dim must be 64, 128, 256 or 512");
+    return run([&] {
+        hyb::DecodeAttnParams p;
+        p.q = static_cast<const hyb::bf16*>(q);
+        p.k_cache = static_cast<const hyb::bf16*>(k_cache);
+        p.v_cache = static_cast<const hyb::bf16*>(v_cache);
+        p.out = static_cast<hyb::bf16*>(out);
+        p.n_heads = n_heads;
+        p.n_kv = n_kv;
+        p.hd = head_dim;
+        p.cap = capacity;
+        p.last_pos = last_pos;
+        p.n_keys = n_keys;
+        p.scale = scale;
+        p.softcap = softcap;
+        p.rounding = rounding;
+        hyb::launch_decode_attn_noalloc(p, as_stream(stream));
+    });
+}
+
 HypStatus hyb_sdpa_prefill(const void* q, const void* k, const void* v, void* out, int32_t Lq, int32_t Lk,
                            int32_t n_heads, int32_t n_kv, int32_t head_dim, int32_t q_pos0, int32_t k_pos0,
                            int32_t window, float scale, float softcap, int32_t rounding, void* stream) {

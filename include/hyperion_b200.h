@@ -102,6 +102,30 @@ HypStatus hyb_sdpa_decode(const void* q, const void* k_cache, const void* v_cach
                           int32_t rounding, void* scratch, size_t scratch_bytes, void* stream);
 
 /*
+ * hyb_sdpa_decode without caller-provided scratch. This entry point has no
+ * counterpart in the reference; it exists for callers that cannot call
+ * cudaMalloc: a host runtime that hands the whole device to its own memory pool
+ * and gives plugins no allocator, or a per-token loop that cannot afford the
+ * device-wide synchronization a cudaMalloc may cause. It allocates nothing: its
+ * scratch is a fixed 8 MiB (8388608-byte) array in device memory that every GPU
+ * which loads this library holds until the process exits.
+ *   Arguments, semantics and results are those of hyb_sdpa_decode.
+ *   Limit: a call whose hyb_sdpa_decode_scratch_bytes(n_heads, n_kv, head_dim,
+ *   n_keys) exceeds 8 MiB returns INVALID_ARGUMENT with a message naming the
+ *   bytes it would need (e.g. 16 heads, 8 KV heads, head_dim 256 fit up to
+ *   ~114k keys; the kernel itself accepts at most 32768).
+ *   The first call on a device looks up the array's device address with that
+ *   device current and caches it; make that first call before any stream capture.
+ *   All calls share the one array: it keeps the previous call's contents (each
+ *   call clears the parts that must start at zero), and calls that overlap on the
+ *   GPU (different streams, other threads) race with each other.
+ */
+HypStatus hyb_sdpa_decode_noalloc(const void* q, const void* k_cache, const void* v_cache, void* out,
+                                  int32_t n_heads, int32_t n_kv, int32_t head_dim, int32_t capacity,
+                                  int32_t last_pos, int32_t n_keys, float scale, float softcap,
+                                  int32_t rounding, void* stream);
+
+/*
  * Multi-token causal attention with an optional sliding window, the prefill case
  * of the same op with the mask of build_mask (forward.cc:345-374).
  *   q: bf16 [Lq, n_heads, head_dim] at absolute positions q_pos0 + i;
