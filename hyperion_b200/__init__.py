@@ -103,6 +103,7 @@ ABI_FUNCTIONS = [
 EXT_FUNCTIONS = [
     "hyb_build_info", "hyb_quantized_matmul", "hyb_qmv_fused", "hyb_qmv_packed_bytes", "hyb_qmv_pack",
     "hyb_qmv_packed", "hyb_sdpa_decode_scratch_bytes", "hyb_sdpa_decode", "hyb_sdpa_decode_noalloc",
+    "hyb_sdpa_decode_fused", "hyb_wait_timeouts",
     "hyb_sdpa_prefill", "hyb_rms_norm", "hyb_qkv_post", "hyb_model_load_synthetic",
     "hyb_model_set_attention_rounding", "hyb_model_stream",
     "hyb_kv_copy_layer", "hyb_kv_cursor", "hyb_prefill_logits", "hyb_decode_logits", "hyb_decode_forced",
@@ -145,6 +146,9 @@ def lib() -> ctypes.CDLL:
         "hyb_qmv_packed": [P, P, P, c.c_int64, c.c_int64, c.c_int32, c.c_int32, P, P, P, P, P, c.c_float, P],
         "hyb_sdpa_decode": [P, P, P, P, c.c_int32, c.c_int32, c.c_int32, c.c_int32, c.c_int32, c.c_int32,
                             c.c_float, c.c_float, c.c_int32, P, c.c_size_t, P],
+        "hyb_sdpa_decode_fused": [P, c.c_int32, P, P, P, c.c_float, P, P, c.c_int32, c.c_int32, c.c_int32,
+                                  c.c_int32, c.c_int32, c.c_int32, c.c_float, c.c_float, c.c_int32, P, P],
+        "hyb_wait_timeouts": [c.POINTER(c.c_int64)],
         "hyb_sdpa_decode_noalloc": [P, P, P, P, c.c_int32, c.c_int32, c.c_int32, c.c_int32, c.c_int32,
                                     c.c_int32, c.c_float, c.c_float, c.c_int32, P],
         "hyb_sdpa_prefill": [P, P, P, P, c.c_int32, c.c_int32, c.c_int32, c.c_int32, c.c_int32, c.c_int32,

@@ -688,55 +688,75 @@ void Model::decode_layers(KvState& kv) {
             resid = ws_.h_a.p;
         }
         launch_qmv(p, st, true);
-        QkvPostParams qp;
-        qp.qkv = ws_.qkv.p;
-        qp.L = 1;
-        qp.ld = qkv_rows;
-        qp.n_heads = nh;
-        qp.n_kv = W.nkv;
-        qp.hd = W.hd;
-        qp.v_from_k = W.v_rows == 0;
-        qp.q_norm = W.q_norm.p;
-        qp.k_norm = W.k_norm.p;
-        qp.inv_freq = W.inv_freq;
-        qp.pos0 = static_cast<int>(pos);
-        qp.eps = g.eps;
-        qp.q_out = ws_.q.p;
-        DecodeAttnParams ap;
-        ap.q = ws_.q.p;
-        ap.out = ws_.attn.p;
+        // QK-norm + RoPE + cache append + attention in one cluster kernel
+        DecodeFusedParams ap;
+        ap.qkv = ws_.qkv.p;
+        ap.v_from_k = W.v_rows == 0;
+        ap.q_norm = W.q_norm.p;
+        ap.k_norm = W.k_norm.p;
+        ap.inv_freq = W.inv_freq;
+        ap.eps = g.eps;
+        ap.pos = static_cast<int>(pos);
         ap.n_heads = nh;
         ap.n_kv = W.nkv;
         ap.hd = W.hd;
-        ap.last_pos = static_cast<int>(pos);
         ap.rounding = attn_rounding_;
-        ap.scratch = ws_.attn_scratch.p;
-        ap.scratch_bytes = ws_.attn_scratch_bytes;
+        ap.out = ws_.attn.p;
         if (W.kind == LayerKind::Sliding) {
             LocalCache& c = kv.local[li++];
-            qp.k_cache = c.k.p;
-            qp.v_cache = c.v.p;
-            qp.cache_cap = static_cast<int>(c.cap);
-            launch_qkv_post(qp, st);
-            c.committed = pos + 1;
             ap.k_cache = c.k.p;
             ap.v_cache = c.v.p;
             ap.cap = static_cast<int>(c.cap);
             ap.n_keys = static_cast<int>(std::min(g.window, pos + 1));  // forward.cc:55-57
+            c.committed = pos + 1;
         } else {
             GlobalCache& c = kv.global[gi++];
             if (c.capacity < pos + 1) throw std::runtime_error("global cache not reserved");
-            qp.k_cache = c.k.p;
-            qp.v_cache = c.v.p;
-            qp.cache_cap = static_cast<int>(c.capacity);
-            launch_qkv_post(qp, st);
-            c.committed = pos + 1;
             ap.k_cache = c.k.p;
             ap.v_cache = c.v.p;
             ap.cap = static_cast<int>(c.capacity);
             ap.n_keys = static_cast<int>(pos + 1);
+            c.committed = pos + 1;
         }
-        launch_decode_attn(ap, st);
+        if (decode_attn_fused_fits(nh, W.nkv, W.hd, ap.n_keys)) {
+            launch_decode_attn_fused(ap, st, true);
+        } else {
+            // contexts whose scores outgrow one cluster's shared memory: separate
+            // norm/RoPE/append kernel, then split-K attention over global scratch
+            QkvPostParams qp;
+            qp.qkv = ws_.qkv.p;
+            qp.L = 1;
+            qp.ld = qkv_rows;
+            qp.n_heads = nh;
+            qp.n_kv = W.nkv;
+            qp.hd = W.hd;
+            qp.v_from_k = ap.v_from_k;
+            qp.q_norm = W.q_norm.p;
+            qp.k_norm = W.k_norm.p;
+            qp.inv_freq = W.inv_freq;
+            qp.pos0 = ap.pos;
+            qp.eps = g.eps;
+            qp.q_out = ws_.q.p;
+            qp.k_cache = ap.k_cache;
+            qp.v_cache = ap.v_cache;
+            qp.cache_cap = ap.cap;
+            launch_qkv_post(qp, st);
+            DecodeAttnParams dp;
+            dp.q = ws_.q.p;
+            dp.k_cache = ap.k_cache;
+            dp.v_cache = ap.v_cache;
+            dp.out = ws_.attn.p;
+            dp.n_heads = nh;
+            dp.n_kv = W.nkv;
+            dp.hd = W.hd;
+            dp.cap = ap.cap;
+            dp.last_pos = ap.pos;
+            dp.n_keys = ap.n_keys;
+            dp.rounding = attn_rounding_;
+            dp.scratch = ws_.attn_scratch.p;
+            dp.scratch_bytes = ws_.attn_scratch_bytes;
+            launch_decode_attn(dp, st);
+        }
         QmvParams po;
         po.w = W.o.w.p;
         po.packed = W.o.packed.p;

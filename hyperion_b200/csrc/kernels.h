@@ -141,6 +141,38 @@ void launch_decode_attn(const DecodeAttnParams& p, cudaStream_t stream);
 void launch_decode_attn_noalloc(DecodeAttnParams p, cudaStream_t stream);
 size_t decode_attn_noalloc_limit_bytes();
 
+// Fused single-token decode attention (attention_fused.cu): from the raw projection
+// row qkv (q | k | v, or q | k with v_from_k) it normalises and rotates q and the new
+// k, normalises the new v, appends k/v at slot pos % cap, and attends over the
+// n_keys positions pos - n_keys + 1 .. pos. One thread-block cluster per KV head.
+struct DecodeFusedParams {
+    const bf16* qkv = nullptr;
+    bool v_from_k = false;
+    const bf16* q_norm = nullptr;
+    const bf16* k_norm = nullptr;
+    const float* inv_freq = nullptr;
+    float eps = 1e-6f;
+    bf16* k_cache = nullptr;  // [cap, n_kv, hd]
+    bf16* v_cache = nullptr;
+    int cap = 0;
+    int pos = 0;
+    int n_keys = 0;
+    int n_heads = 0, n_kv = 0, hd = 0;
+    float scale = 1.0f;
+    float softcap = 0.0f;
+    int rounding = 0;
+    bf16* out = nullptr;      // [n_heads, hd]
+};
+void launch_decode_attn_fused(const DecodeFusedParams& p, cudaStream_t stream, bool pdl = false);
+// Whether the fused kernel's shared-memory plan holds n_keys scores (else use the
+// split-K path above).
+bool decode_attn_fused_fits(int n_heads, int n_kv, int hd, int n_keys);
+
+// Bounded mbarrier waits that gave up on the current device (never expected):
+// qmv_packed.cu and attention_fused.cu each keep a counter.
+int64_t read_qmv_wait_timeouts();
+int64_t read_attn_wait_timeouts();
+
 // Prefill: q [Lq, H, hd] at positions q_pos0 + i; k/v [Lk, Hkv, hd] at k_pos0 + j.
 struct PrefillAttnParams {
     const bf16* q = nullptr;

@@ -207,6 +207,40 @@ HypStatus hyb_sdpa_decode_noalloc(const void* q, const void* k_cache, const void
     });
 }
 
+HypStatus hyb_sdpa_decode_fused(const void* qkv, int32_t v_from_k, const void* q_norm, const void* k_norm,
+                                const float* inv_freq, float eps, void* k_cache, void* v_cache, int32_t capacity,
+                                int32_t pos, int32_t n_keys, int32_t n_heads, int32_t n_kv, int32_t head_dim,
+                                float scale, float softcap, int32_t rounding, void* out, void* stream) {
+    if (!qkv || !q_norm || !k_norm || !inv_freq || !k_cache || !v_cache || !out)
+        return hyb::abi_fail(HYP_STATUS_INVALID_ARGUMENT, "null pointer argument");
+    if (n_heads <= 0 || n_kv <= 0 || n_heads % n_kv != 0 || n_keys <= 0 || capacity < n_keys || pos < n_keys - 1)
+        return hyb::abi_fail(HYP_STATUS_INVALID_ARGUMENT, "sdpa_decode_fused: bad shape");
+    if (head_dim != 64 && head_dim != 128 && head_dim != 256)
+        return hyb::abi_fail(HYP_STATUS_UNSUPPORTED, "sdpa_decode_fused: head_dim must be 64, 128 or 256");
+    return run([&] {
+        hyb::DecodeFusedParams p;
+        p.qkv = static_cast<const hyb::bf16*>(qkv);
+        p.v_from_k = v_from_k != 0;
+        p.q_norm = static_cast<const hyb::bf16*>(q_norm);
+        p.k_norm = static_cast<const hyb::bf16*>(k_norm);
+        p.inv_freq = inv_freq;
+        p.eps = eps;
+        p.k_cache = static_cast<hyb::bf16*>(k_cache);
+        p.v_cache = static_cast<hyb::bf16*>(v_cache);
+        p.cap = capacity;
+        p.pos = pos;
+        p.n_keys = n_keys;
+        p.n_heads = n_heads;
+        p.n_kv = n_kv;
+        p.hd = head_dim;
+        p.scale = scale;
+        p.softcap = softcap;
+        p.rounding = rounding;
+        p.out = static_cast<hyb::bf16*>(out);
+        hyb::launch_decode_attn_fused(p, as_stream(stream), false);
+    });
+}
+
 HypStatus hyb_sdpa_prefill(const void* q, const void* k, const void* v, void* out, int32_t Lq, int32_t Lk,
                            int32_t n_heads, int32_t n_kv, int32_t head_dim, int32_t q_pos0, int32_t k_pos0,
                            int32_t window, float scale, float softcap, int32_t rounding, void* stream) {
@@ -280,6 +314,11 @@ HypStatus hyb_qkv_post(const void* qkv, int32_t L, int32_t ld, int32_t n_heads, 
         p.cache_first = cache_first;
         hyb::launch_qkv_post(p, as_stream(stream));
     });
+}
+
+HypStatus hyb_wait_timeouts(int64_t* count) {
+    if (!count) return hyb::abi_fail(HYP_STATUS_INVALID_ARGUMENT, "count is null");
+    return run([&] { *count = hyb::read_qmv_wait_timeouts() + hyb::read_attn_wait_timeouts(); });
 }
 
 }  // extern "C"

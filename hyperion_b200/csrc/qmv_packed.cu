@@ -19,6 +19,7 @@
 //   A warp's reads of one chunk index are 32 consecutive 16-byte words, so the
 //   shared-memory reads are conflict-free, and each item is a single bulk copy.
 #include "kernels.h"
+#include "tma.cuh"
 
 #include <algorithm>
 
@@ -58,42 +59,11 @@ __host__ __device__ inline PackGeo pack_geo(int K, int N) {
     return p;
 }
 
-__device__ __forceinline__ uint32_t smem_u32(const void* p) {
-    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
-}
-
-__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
-    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
-}
-
-__device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
-    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
-}
-
 // Bounded wait on an mbarrier phase: gives up (and records it) instead of hanging.
 __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t phase) {
-    for (int it = 0; it < (1 << 20); ++it) {
-        uint32_t done;
-        asm volatile(
-            "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
-            : "=r"(done)
-            : "r"(bar), "r"(phase)
-            : "memory");
-        if (done) return true;
-    }
+    if (mbar_wait_bounded(bar, phase)) return true;
     atomicAdd(&g_qmv_wait_timeouts, 1);
     return false;
-}
-
-__device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
-    asm volatile(
-        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
-        "l"(src), "r"(bytes), "r"(bar)
-        : "memory");
-}
-
-__device__ __forceinline__ void fence_proxy_async() {
-    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
 
 __device__ __forceinline__ float block_sum(float v, float* tmp) {
@@ -156,7 +126,7 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) qmv_packed_kernel(const 
 
     if (lane == 0) {
         for (int s = 0; s < kStages; ++s) mbar_init(my_bar0 + 8 * s, 1);
-        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        mbar_init_fence();
     }
     __syncwarp();
 
@@ -175,7 +145,7 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) qmv_packed_kernel(const 
                 bulk_g2s(smem_u32(my_ring + s * kItemMax), src, bytes, bar);
             } else {
                 // a padding block of an odd block count: complete the phase without data
-                asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(my_bar0 + 8 * (i % kStages)) : "memory");
+                mbar_arrive(my_bar0 + 8 * (i % kStages));
             }
         }
     };
@@ -512,6 +482,12 @@ void launch_qmv_packed(const QmvParams& p, cudaStream_t stream, bool pdl) {
     cfg.numAttrs = pdl ? 1 : 0;
     if (geglu) HYB_CUDA(cudaLaunchKernelEx(&cfg, qmv_packed_kernel<true>, p));
     else HYB_CUDA(cudaLaunchKernelEx(&cfg, qmv_packed_kernel<false>, p));
+}
+
+int64_t read_qmv_wait_timeouts() {
+    int a = 0;
+    HYB_CUDA(cudaMemcpyFromSymbol(&a, g_qmv_wait_timeouts, sizeof(int)));
+    return a;
 }
 
 }  // namespace hyb

@@ -1,0 +1,61 @@
+// Bulk-copy (non-tensor TMA) and mbarrier helpers shared by the streaming kernels.
+//
+// Every wait is bounded: a wait that gives up returns false and the caller
+// records it in its translation unit's timeout counter (read back on the host by
+// hyb_wait_timeouts), so a copy that never lands cannot hang the GPU.
+#pragma once
+
+#include <cstdint>
+
+namespace hyb {
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void mbar_init_fence() {
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+// One arrival that also adds `bytes` to the phase's expected transaction count.
+__device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+
+// Bounded wait for the phase of parity `phase` to complete (2^20 try_wait polls).
+__device__ __forceinline__ bool mbar_wait_bounded(uint32_t bar, uint32_t phase) {
+    for (int it = 0; it < (1 << 20); ++it) {
+        uint32_t done;
+        asm volatile(
+            "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+            : "=r"(done)
+            : "r"(bar), "r"(phase)
+            : "memory");
+        if (done) return true;
+    }
+    return false;
+}
+
+// Global -> this CTA's shared memory, completion counted on `bar` in bytes.
+// Both addresses 16-byte aligned, bytes a multiple of 16.
+__device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
+        "l"(src), "r"(bytes), "r"(bar)
+        : "memory");
+}
+
+// Orders earlier generic-proxy accesses of shared memory before later bulk copies into it.
+__device__ __forceinline__ void fence_proxy_async() {
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+}  // namespace hyb

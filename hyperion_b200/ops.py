@@ -86,6 +86,18 @@ def sdpa_decode(q, k_cache, v_cache, last_pos: int, n_keys: int, scratch: Decode
     return out
 
 
+def sdpa_decode_fused(qkv, v_from_k, q_norm, k_norm, inv_freq, k_cache, v_cache, pos, n_keys, n_heads, eps=1e-6,
+                      scale=1.0, softcap=0.0, rounding=0, out=None, stream=None):
+    """Fused decode step: norms + RoPE + cache append + attention (cluster kernel)."""
+    cap, nkv, hd = k_cache.shape
+    if out is None:
+        out = torch.empty((n_heads, hd), dtype=torch.bfloat16, device=qkv.device)
+    check(lib().hyb_sdpa_decode_fused(_p(qkv), int(v_from_k), _p(q_norm), _p(k_norm), _p(inv_freq), eps,
+                                      _p(k_cache), _p(v_cache), cap, pos, n_keys, n_heads, nkv, hd, scale, softcap,
+                                      rounding, _p(out), _stream(stream)))
+    return out
+
+
 def sdpa_prefill(q, k, v, q_pos0: int, k_pos0: int, window: int, scale=1.0, softcap=0.0, rounding=0,
                  out=None, stream=None):
     Lq, H, hd = q.shape

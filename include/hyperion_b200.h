@@ -126,6 +126,38 @@ HypStatus hyb_sdpa_decode_noalloc(const void* q, const void* k_cache, const void
                                   int32_t rounding, void* stream);
 
 /*
+ * The decode engine's fused single-token attention step, replacing for q_len == 1
+ * the sequence q/k/v norms + RoPE + cache append + cache read + SDPA of
+ * ForwardPass::attention (native/hyperion_mlx/src/forward.cc:394-504).
+ *   qkv: bf16 raw projection row of the token: q (n_heads * head_dim), k (n_kv *
+ *   head_dim), then v (n_kv * head_dim) unless v_from_k (global K=V layers: v is
+ *   the weightless norm of the k columns). q and k are RMS-normalised with
+ *   q_norm / k_norm [head_dim] and rotated at position pos with inv_freq
+ *   [head_dim/2]; the new k and v are written to k_cache / v_cache
+ *   [capacity, n_kv, head_dim] at slot pos % capacity; the query attends to the
+ *   n_keys positions pos - n_keys + 1 .. pos. out: bf16 [n_heads, head_dim].
+ *   Same score/probability rounding modes as hyb_sdpa_decode; no scratch. The
+ *   n_keys scores live in the cluster's shared memory (about 200K keys for
+ *   head_dim 256 and 2 query heads per KV head); longer contexts return
+ *   INVALID_ARGUMENT (the engine then uses hyb_qkv_post + hyb_sdpa_decode).
+ */
+HypStatus hyb_sdpa_decode_fused(const void* qkv, int32_t v_from_k, const void* q_norm,
+                                const void* k_norm, const float* inv_freq, float eps,
+                                void* k_cache, void* v_cache, int32_t capacity, int32_t pos,
+                                int32_t n_keys, int32_t n_heads, int32_t n_kv, int32_t head_dim,
+                                float scale, float softcap, int32_t rounding, void* out,
+                                void* stream);
+
+/*
+ * Count of bounded shared-memory waits (mbarrier, bulk-copy completion) that gave
+ * up on the current device since the library was loaded, summed over the
+ * streaming qmv and the fused decode attention. A wait that gives up leaves that
+ * launch's output undefined but never hangs the GPU; the count is expected to stay
+ * 0. No reference counterpart (the reference's kernels are MLX's).
+ */
+HypStatus hyb_wait_timeouts(int64_t* count);
+
+/*
  * Multi-token causal attention with an optional sliding window, the prefill case
  * of the same op with the mask of build_mask (forward.cc:345-374).
  *   q: bf16 [Lq, n_heads, head_dim] at absolute positions q_pos0 + i;

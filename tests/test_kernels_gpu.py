@@ -270,3 +270,54 @@ def test_qmv_packed_fused(built_lib, oracle_lib, K, N, prologue, epilogue, with_
     got = host(ops.qmv_packed(dev(x), packed, K, N, h_out=h2 if prologue == 2 else None, **kw))
     assert within_one_ulp(got, ref) >= 0.999 and rel_l2(got, ref) <= REL_L2_QMM
     assert np.array_equal(host(h1), host(h2))
+
+
+@pytest.mark.parametrize("H,Hkv,hd,cap,pos,n_keys,v_from_k,proportional", [
+    (16, 8, 256, 1032, 2999, 1024, False, False),   # cfg3 sliding, wrapped ring (8-CTA clusters)
+    (16, 8, 256, 4352, 4099, 4100, True, True),     # cfg3 global
+    (32, 16, 128, 1032, 700, 701, False, False),    # cfg4 sliding before the window fills
+    (4, 2, 64, 136, 33, 34, False, False),          # cfg0 sliding (single-CTA cluster)
+    (4, 1, 128, 512, 300, 301, True, True),         # tiny-fixture global, GQA 4
+    (8, 1, 64, 16, 40, 8, False, False),            # window 8, GQA 8
+    (16, 8, 256, 16384, 16383, 16384, True, True),  # cfg3 global at 16K (many stage reuses)
+    (8, 8, 128, 300, 299, 300, False, False),       # GQA 1
+])
+def test_sdpa_decode_fused(built_lib, oracle_lib, H, Hkv, hd, cap, pos, n_keys, v_from_k, proportional):
+    """QK-norm + RoPE + cache append + attention in one cluster kernel vs the oracle's op sequence."""
+    from hyperion_b200 import ops
+    from oracle import gemma_oracle as go
+    import torch
+    rng = np.random.default_rng(H + hd + pos)
+    ld = (H + (1 if v_from_k else 2) * Hkv) * hd
+    qkv = f32_to_bf16_bits(rng.standard_normal(ld, dtype=np.float32) * 3)
+    qn = f32_to_bf16_bits(1 + 0.02 * rng.standard_normal(hd, dtype=np.float32))
+    kn = f32_to_bf16_bits(1 + 0.02 * rng.standard_normal(hd, dtype=np.float32))
+    inv = go.rope_inv_freq(hd, 1e6 if proportional else 1e4, proportional, 0.25)
+    kc = f32_to_bf16_bits(rng.standard_normal((cap, Hkv, hd), dtype=np.float32))
+    vc = f32_to_bf16_bits(rng.standard_normal((cap, Hkv, hd), dtype=np.float32))
+    dk, dv = dev(kc), dev(vc)
+    out = host(ops.sdpa_decode_fused(dev(qkv), v_from_k, dev(qn), dev(kn), dev(inv), dk, dv, pos, n_keys, H))
+    torch.cuda.synchronize()
+    q = go.rope(go.rms_norm(qkv[:H * hd].reshape(1, H, hd), qn, 1e-6), pos, inv)
+    kraw = qkv[H * hd:(H + Hkv) * hd].reshape(1, Hkv, hd)
+    k = go.rope(go.rms_norm(kraw, kn, 1e-6), pos, inv)
+    v = go.rms_norm(kraw if v_from_k else qkv[(H + Hkv) * hd:].reshape(1, Hkv, hd), None, 1e-6)
+    kc[pos % cap], vc[pos % cap] = k[0], v[0]
+    assert max_ulp(host(dk)[pos % cap], k[0]) <= 1 and max_ulp(host(dv)[pos % cap], v[0]) <= 1
+    ps = np.arange(pos - n_keys + 1, pos + 1)
+    want = go.sdpa(q, kc[ps % cap], vc[ps % cap], pos, pos - n_keys + 1, 0).reshape(H, hd)
+    assert rel_l2(out, want) <= REL_L2_BF16
+
+
+def test_sdpa_decode_fused_rejects_oversized_context(built_lib):
+    """Scores that outgrow the cluster's shared memory are refused, not truncated."""
+    import torch
+    from hyperion_b200 import HypError, ops
+    H, Hkv, hd, n = 8, 1, 128, 50000
+    kc = torch.zeros((n, Hkv, hd), dtype=torch.bfloat16, device="cuda")
+    vc = torch.zeros_like(kc)
+    qkv = torch.zeros((H + 2 * Hkv) * hd, dtype=torch.bfloat16, device="cuda")
+    nw = torch.ones(hd, dtype=torch.bfloat16, device="cuda")
+    inv = torch.ones(hd // 2, dtype=torch.float32, device="cuda")
+    with pytest.raises(HypError, match="too many keys"):
+        ops.sdpa_decode_fused(qkv, False, nw, nw, inv, kc, vc, n - 1, n, H)
