@@ -6,25 +6,32 @@
 // RoPE, :459-468 cache append, :474-495 cache read, :498-504 SDPA).
 //
 // Each cluster of CS CTAs (CS <= 8, portable) owns one KV head and its REP query
-// heads; CTA rank c owns a contiguous slice of the n_keys cache positions and
-// each of its 8 warps a contiguous sub-slice. A warp streams its K rows and then
-// its V rows through its own ring of 2 KB shared-memory stages with bulk copies
-// (one cp.async.bulk per cache row, so ring wrap-around of the cache costs
-// nothing; up to 16 KB in flight per warp). Warps never wait for each other while
-// streaming. The first stages are issued before the programmatic-dependent-launch
-// wait: cache rows of earlier positions never depend on the previous kernel.
+// heads; CTA rank c owns a contiguous slice of the n_keys cache positions. The
+// slice's K rows and then its V rows stream through a ring of shared-memory tiles
+// of 64 consecutive cache slots of this KV head: HD/64 tensor-map TMA boxes of
+// [64 slots][64 dims] with the 128-byte swizzle, so the tensor-core fragment loads
+// (ldmatrix) are free of bank conflicts. Tiles are cut at the ring's wrap-around so
+// their slots are contiguous. Each tile has a "full" barrier (bytes landed) and an
+// "empty" barrier (all 8 warps done); warp (t mod 8) refills the stage of tile t,
+// so no warp waits for another except through data. The first tiles are issued
+// before the programmatic-dependent-launch wait: cache rows of earlier positions
+// never depend on the previous kernel.
 //   phase 0  every CTA normalises and rotates its REP query heads from the raw
 //            projection row; the CTA owning the newest position also normalises /
-//            rotates the new K, normalises the new V, appends both to the cache
-//            slot pos % cap and keeps them in shared memory (that row is never
-//            bulk-copied);
-//   phase 1  scores s = bf16(q . k * scale) into shared memory; per-CTA max and
-//            sum of exp, pushed into every CTA of the cluster (remote stores);
-//   cluster barrier; each CTA forms the row's (M, L) from the pushed pairs in
-//            rank order;
-//   phase 2  p = bf16(exp(s - M) / L) in place, P V per warp, summed over warps;
-//            the CTA pushes each output element's partial to the CTA that owns
-//            that element's slice;
+//            rotates the new K, normalises the new V and appends both to the cache
+//            slot pos % cap (the tile copy of that slot is patched from shared
+//            memory, never trusted);
+//   phase 1  S = Q K^T with mma.sync m16n8k16 (bf16 in, fp32 accumulate; heads are
+//            the M rows, zero padded to 16): warp w owns keys 8w..8w+7 of every
+//            tile; s = bf16(s * scale) into shared memory; each warp reduces
+//            (max, sum of exp) over its own keys; the CTA's pair is pushed into every
+//            CTA of the cluster (remote stores);
+//   cluster barrier; each warp forms the row's (M, L) from the pushed pairs in rank
+//            order and turns its own scores into p = bf16(exp(s - M) / L);
+//   phase 2  O = P V with mma.sync: warp w owns head_dim columns [w HD/8, (w+1) HD/8)
+//            over all keys (bf16 p is exact in rounding mode 0; mode 1 adds the
+//            bf16 residual p - bf16(p) as a second product); each output element's
+//            CTA partial is pushed to the CTA owning that element's slice;
 //   cluster barrier; each CTA sums the pushed partials of its slice in rank order
 //            (deterministic) and writes bf16.
 // Only remote stores cross CTAs (no remote loads wait on latency). The cluster
@@ -32,8 +39,11 @@
 #include "kernels.h"
 #include "tma.cuh"
 
+#include <cudaTypedefs.h>
+
 #include <algorithm>
 #include <cfloat>
+#include <string>
 
 namespace hyb {
 
@@ -44,8 +54,9 @@ namespace {
 constexpr int kThreads = 256;
 constexpr int kWarps = kThreads / 32;
 constexpr int kMaxCluster = 8;
-constexpr int kStageBytes = 2048;
-constexpr int kMaxStages = 8;  // per warp
+constexpr int kTileKeys = 64;       // cache slots per tile (8 per warp)
+constexpr int kRingBytes = 131072;  // tile bytes in flight per CTA
+constexpr int kMaxStages = 8;
 constexpr size_t kSmemLimit = 227 * 1024;
 
 __device__ __forceinline__ void cluster_arrive_relaxed() {
@@ -91,55 +102,6 @@ __device__ __forceinline__ float score_round(float dot, float scale, float cap, 
     return s;
 }
 
-template <int PER>
-__device__ __forceinline__ void load_row(const bf16* p, float (&o)[PER]) {
-    if constexpr (PER == 2) {
-        uint32_t v = *reinterpret_cast<const uint32_t*>(p);
-        o[0] = __uint_as_float(v << 16);
-        o[1] = __uint_as_float(v & 0xFFFF0000u);
-    } else if constexpr (PER == 4) {
-        uint2 v = *reinterpret_cast<const uint2*>(p);
-        o[0] = __uint_as_float(v.x << 16);
-        o[1] = __uint_as_float(v.x & 0xFFFF0000u);
-        o[2] = __uint_as_float(v.y << 16);
-        o[3] = __uint_as_float(v.y & 0xFFFF0000u);
-    } else {
-#pragma unroll
-        for (int c = 0; c < PER / 8; ++c) {
-            uint4 v = *reinterpret_cast<const uint4*>(p + 8 * c);
-            const uint32_t w[4] = {v.x, v.y, v.z, v.w};
-#pragma unroll
-            for (int i = 0; i < 4; ++i) {
-                o[8 * c + 2 * i] = __uint_as_float(w[i] << 16);
-                o[8 * c + 2 * i + 1] = __uint_as_float(w[i] & 0xFFFF0000u);
-            }
-        }
-    }
-}
-
-// Sum each of the V per-lane values over the warp. Reduce-scatter by halves
-// (log2 V exchange steps), then a plain butterfly over the remaining lane bits:
-// V - 1 + log2(32 / V) shuffles instead of 5 V. Afterwards v[0] of lane l holds
-// the total of value index (l / (32 / V)).
-template <int V>
-__device__ __forceinline__ float warp_reduce_scatter(float (&v)[V]) {
-    const int lane = threadIdx.x & 31;
-    static_assert(V >= 1 && V <= 32 && (V & (V - 1)) == 0, "V must be a power of two <= 32");
-#pragma unroll
-    for (int half = V / 2, off = 16; half >= 1; half /= 2, off /= 2) {
-        const bool upper = (lane & off) != 0;
-#pragma unroll
-        for (int i = 0; i < half; ++i) {
-            const float send = upper ? v[i] : v[i + half];
-            const float keep = upper ? v[i + half] : v[i];
-            v[i] = keep + __shfl_xor_sync(0xffffffffu, send, off);
-        }
-    }
-#pragma unroll
-    for (int off = 16 / V; off >= 1; off /= 2) v[0] += __shfl_xor_sync(0xffffffffu, v[0], off);
-    return v[0];
-}
-
 // Normalise one head row of the raw projection (optionally rotate) into `dst`
 // (floats holding bf16-rounded values). One warp; elements e = lane + 32 i.
 template <int PER>
@@ -182,18 +144,16 @@ __device__ void norm_rope_row(const bf16* src, const bf16* nw, const float* inv_
     }
 }
 
-// Shared-memory plan (bytes): rings, mbarriers, then the float arrays below.
+// Shared-memory plan (bytes from a 1024-byte aligned base): tiles, barriers, floats.
 struct FusedLayout {
-    int stages;
-    size_t rings, bars, q_s, knew, vnew, wred, ml, allml, stat, o_w, recv, s_sc, total;
+    size_t full, empty, q_s, knew, vnew, wml, allml, recv, s_sc, total;
 };
 
 __host__ __device__ inline FusedLayout fused_layout(int hd, int rep, int chunk, int stages) {
     FusedLayout L;
-    L.stages = stages;
-    L.rings = 0;
-    L.bars = static_cast<size_t>(kWarps) * stages * kStageBytes;
-    size_t f = L.bars + 8 * kWarps * kMaxStages;  // float cursor in bytes
+    L.full = static_cast<size_t>(stages) * kTileKeys * hd * 2;
+    L.empty = L.full + 8 * kMaxStages;
+    size_t f = L.empty + 8 * kMaxStages;
     auto take = [&](size_t floats) {
         const size_t at = f;
         f += 4 * ((floats + 1) & ~static_cast<size_t>(1));  // keep 8-byte alignment
@@ -203,40 +163,62 @@ __host__ __device__ inline FusedLayout fused_layout(int hd, int rep, int chunk, 
     L.q_s = take(E);
     L.knew = take(hd);
     L.vnew = take(hd);
-    L.wred = take(static_cast<size_t>(kWarps) * rep);
-    L.ml = take(2 * rep);
+    L.wml = take(2 * static_cast<size_t>(kWarps) * rep);
     L.allml = take(2 * static_cast<size_t>(kMaxCluster) * rep);
-    L.stat = take(2 * rep);
-    L.o_w = take(static_cast<size_t>(kWarps) * E);
     L.recv = take(E + kMaxCluster);
     L.s_sc = take(static_cast<size_t>(rep) * chunk);
     L.total = f;
     return L;
 }
 
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+                 : "r"(addr));
+}
+__device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+                 : "r"(addr));
+}
+__device__ __forceinline__ void ldsm_x2_t(uint32_t addr, uint32_t& r0, uint32_t& r1) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x2.trans.shared.b16 {%0,%1}, [%2];" : "=r"(r0), "=r"(r1) : "r"(addr));
+}
+
+// Byte offset of 16-byte chunk c (8 bf16 of head_dim) of tile row r. A tile is
+// HD/64 sub-tiles of [64 rows][128 bytes], each written by one TMA box with the
+// 128-byte swizzle: chunk c' of row r sits at chunk c' ^ (r mod 8).
+__device__ __forceinline__ uint32_t tile_off(int r, int c) {
+    return static_cast<uint32_t>((c >> 3) * (kTileKeys * 128) + r * 128 + (((c & 7) ^ (r & 7)) << 4));
+}
+
 template <int PER, int REP>
 __global__ void __launch_bounds__(kThreads) decode_attn_fused_kernel(const DecodeFusedParams p, int chunk,
-                                                                     int stages) {
+                                                                     int stages,
+                                                                     const __grid_constant__ CUtensorMap tmk,
+                                                                     const __grid_constant__ CUtensorMap tmv) {
     constexpr int HD = PER * 32;
     constexpr int E = REP * HD;
-    constexpr int ROWB = HD * 2;               // bytes of one cache row
-    constexpr int RS = kStageBytes / ROWB;     // rows per stage: 4 / 8 / 16
-    constexpr int U = 4;                       // keys per score batch
-    extern __shared__ __align__(128) unsigned char smem_raw[];
+    constexpr int T = kTileKeys;            // keys per tile
+    constexpr int TILE = T * HD * 2;        // bytes per tile
+    constexpr int SUB = HD / 64;            // 128-byte sub-tiles (TMA boxes) per tile
+    constexpr int KSTEPS = HD / 16;         // MMA k-steps over head_dim
+    constexpr int NTW = HD / 64;            // 8-wide output column tiles per warp in P V
+    static_assert(T == 8 * kWarps, "each warp owns 8 keys of a tile");
+    extern __shared__ unsigned char smem_dyn[];
+    unsigned char* smem_raw = smem_dyn + ((1024 - (smem_u32(smem_dyn) & 1023)) & 1023);  // 1024-aligned
     const FusedLayout lay = fused_layout(HD, REP, chunk, stages);
-    uint64_t* bars = reinterpret_cast<uint64_t*>(smem_raw + lay.bars);
+    unsigned char* tiles = smem_raw;                                  // [stages][TILE], swizzled
     float* q_s = reinterpret_cast<float*>(smem_raw + lay.q_s);      // [REP][HD]
     float* knew = reinterpret_cast<float*>(smem_raw + lay.knew);    // [HD]
     float* vnew = reinterpret_cast<float*>(smem_raw + lay.vnew);    // [HD]
-    float* wred = reinterpret_cast<float*>(smem_raw + lay.wred);    // [kWarps][REP]
-    float* ml = reinterpret_cast<float*>(smem_raw + lay.ml);        // [REP][2] this CTA's (max, sum)
+    float* wml = reinterpret_cast<float*>(smem_raw + lay.wml);      // [kWarps][REP][2] per-warp (max, sum)
     float* allml = reinterpret_cast<float*>(smem_raw + lay.allml);  // [CS][REP][2] pushed by every CTA
-    float* stat = reinterpret_cast<float*>(smem_raw + lay.stat);    // [REP][2] (M, 1/L) of the row
-    float* o_w = reinterpret_cast<float*>(smem_raw + lay.o_w);      // [kWarps][E]
     float* recv = reinterpret_cast<float*>(smem_raw + lay.recv);    // [CS][per_cta] pushed partials
     float* s_sc = reinterpret_cast<float*>(smem_raw + lay.s_sc);    // [REP][chunk]
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int g = lane >> 2, t4 = lane & 3;  // MMA fragment coordinates
     const int hk = blockIdx.y;
     const int CS = gridDim.x;
     const uint32_t rank = cluster_rank();
@@ -244,42 +226,48 @@ __global__ void __launch_bounds__(kThreads) decode_attn_fused_kernel(const Decod
     const int j1 = min(p.n_keys, j0 + chunk);
     const int n = max(0, j1 - j0);
     const bool owns_newest = (j1 == p.n_keys) && n > 0;
+    const int newest = p.n_keys - 1;
     const int first_pos = p.pos - p.n_keys + 1;
-    // this warp's keys [wb, we) and its items: K stages then V stages
-    const int kw = (n + kWarps - 1) / kWarps;
-    const int wb = j0 + min(n, warp * kw), we = j0 + min(n, warp * kw + kw);
-    const int nb = (we - wb + RS - 1) / RS;
-    const int items = 2 * nb;
-    unsigned char* ring = smem_raw + static_cast<size_t>(warp) * stages * kStageBytes;
-    const uint32_t bar0 = smem_u32(bars + warp * kMaxStages);
+    // tiles: segment A = keys before the ring wraps to slot 0, segment B = the rest
+    const int s_first = (first_pos + j0) % p.cap;
+    const int lenA = min(n, p.cap - s_first);
+    const int ntA = (lenA + T - 1) / T;
+    const int nt = ntA + (n - lenA + T - 1) / T;  // K tiles (and V tiles) of this CTA
+    const int items = 2 * nt;                     // item t < nt: K tile t; t >= nt: V tile t - nt
+    // tile t: keys [x, y) and the first slot z of its box
+    auto tile_keys = [=](int t) {
+        if (t < ntA) return make_int3(j0 + t * T, min(j0 + lenA, j0 + t * T + T), s_first + t * T);
+        const int jb = j0 + lenA + (t - ntA) * T;
+        return make_int3(jb, min(j1, jb + T), (t - ntA) * T);
+    };
+    const uint32_t tiles_u32 = smem_u32(tiles);
+    const uint32_t full0 = smem_u32(smem_raw + lay.full), empty0 = smem_u32(smem_raw + lay.empty);
 
     cluster_arrive_relaxed();  // matched by the wait before the first remote store
-    if (lane == 0) {
-        for (int s = 0; s < stages; ++s) mbar_init(bar0 + 8 * s, 1);
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < stages; ++s) {
+            mbar_init(full0 + 8 * s, 1);
+            mbar_init(empty0 + 8 * s, kWarps);
+        }
         mbar_init_fence();
     }
-    __syncwarp();
+    __syncthreads();
 
-    // Item i < nb: K rows of stage-batch i; i >= nb: V rows of batch i - nb.
-    // Called by the whole warp; lane r copies row r of the batch.
-    auto issue = [&](int i) {
-        const bool isv = i >= nb;
-        const int b = isv ? i - nb : i;
-        const int rb = wb + b * RS, re = min(we, rb + RS);
-        const bool has_new = owns_newest && re == p.n_keys;
-        const int s = i % stages;
-        const uint32_t bar = bar0 + 8 * s;
-        if (lane == 0) mbar_expect_tx(bar, static_cast<uint32_t>(re - rb - (has_new ? 1 : 0)) * ROWB);
-        __syncwarp();
-        const int j = rb + lane;
-        if (j < re && !(has_new && j == p.n_keys - 1)) {
-            const int slot = (first_pos + j) % p.cap;
-            const bf16* base = isv ? p.v_cache : p.k_cache;
-            bulk_g2s(smem_u32(ring + s * kStageBytes) + lane * ROWB,
-                     base + (static_cast<size_t>(slot) * p.n_kv + hk) * HD, ROWB, bar);
-        }
+    // Load item `it` into stage it % stages (one thread): SUB boxes of 64 slots x 64
+    // dims. Rows past the tile's keys (other slots, or zero fill past cap) are never
+    // used, and the newest slot, written by this kernel, is patched from registers.
+    auto issue = [&](int it) {
+        const bool isv = it >= nt;
+        const int3 tk = tile_keys(isv ? it - nt : it);
+        const int s = it % stages;
+        const uint32_t fb = full0 + 8 * s;
+        mbar_expect_tx(fb, TILE);
+#pragma unroll
+        for (int sub = 0; sub < SUB; ++sub)
+            tma_load_3d(tiles_u32 + s * TILE + sub * (T * 128), isv ? &tmv : &tmk, 64 * sub, hk, tk.z, fb);
     };
-    for (int i = 0; i < stages && i < items; ++i) issue(i);
+    if (threadIdx.x == 0)
+        for (int it = 0; it < stages && it < items; ++it) issue(it);
 
     pdl_wait();
     // ---- phase 0: query heads of this KV head, and the new token's K/V
@@ -300,167 +288,209 @@ __global__ void __launch_bounds__(kThreads) decode_attn_fused_kernel(const Decod
     }
     __syncthreads();
 
-    uint32_t phase_bits = 0;  // one parity bit per stage
     bool waits_ok = true;
-    auto wait_item = [&](int i) {
-        const int s = i % stages;
-        if (!mbar_wait_bounded(bar0 + 8 * s, (phase_bits >> s) & 1u)) waits_ok = false;
-        phase_bits ^= 1u << s;
-        return static_cast<const unsigned char*>(ring + s * kStageBytes);
+    auto wait_full = [&](int it) {
+        const int s = it % stages;
+        if (!mbar_wait_bounded(full0 + 8 * s, static_cast<uint32_t>(it / stages) & 1u)) waits_ok = false;
+        return tiles_u32 + static_cast<uint32_t>(s * TILE);
     };
-    auto release_item = [&](int i) {
-        if (i + stages < items) {
-            fence_proxy_async();  // this lane's reads of the stage precede the next copy into it
-            __syncwarp();
-            issue(i + stages);
+    // This warp is done with item `it`; warp (it mod 8) refills the stage once all are.
+    auto release = [&](int it) {
+        const int s = it % stages;
+        __syncwarp();
+        if (lane == 0) mbar_arrive(empty0 + 8 * s);
+        if (it + stages < items && warp == it % kWarps && lane == 0) {
+            if (!mbar_wait_bounded(empty0 + 8 * s, static_cast<uint32_t>(it / stages) & 1u)) waits_ok = false;
+            issue(it + stages);
         }
     };
+    // Overwrite columns [c0, c1) (16-byte chunks) of tile row r with `src` (floats
+    // holding bf16 values): the newest slot, whose cache row this kernel just wrote.
+    auto patch_row = [&](uint32_t tile, int r, const float* src, int c0, int c1) {
+        for (int c = c0 + lane; c < c1; c += 32) {
+            const float* v = src + 8 * c;
+            uint4 w;
+            w.x = pack_bf2(f2bf(v[0]), f2bf(v[1]));
+            w.y = pack_bf2(f2bf(v[2]), f2bf(v[3]));
+            w.z = pack_bf2(f2bf(v[4]), f2bf(v[5]));
+            w.w = pack_bf2(f2bf(v[6]), f2bf(v[7]));
+            asm volatile("st.shared.v4.u32 [%0], {%1,%2,%3,%4};" ::"r"(tile + tile_off(r, c)), "r"(w.x), "r"(w.y),
+                         "r"(w.z), "r"(w.w)
+                         : "memory");
+        }
+        fence_proxy_async();  // the stage is refilled by TMA later
+        __syncwarp();
+    };
+    // key index (relative to j0) of this warp's i-th key, or -1 past its tile's keys
+    auto my_key = [=](int i) {
+        const int3 tk = tile_keys(i >> 3);
+        const int j = tk.x + 8 * warp + (i & 7);
+        return j < tk.y ? j - j0 : -1;
+    };
+    const int my_count = nt * 8;
 
-    // ---- phase 1: scores of this warp's keys
+    // ---- phase 1: scores S = Q K^T on tensor cores; this warp owns keys 8w..8w+7 of each tile
     {
-        float q[REP][PER];
+        uint32_t qa[KSTEPS][2];  // A fragments of Q (rows = heads; rows >= REP are zero)
 #pragma unroll
-        for (int r = 0; r < REP; ++r)
-#pragma unroll
-            for (int e = 0; e < PER; ++e) q[r][e] = q_s[r * HD + lane * PER + e];
-        for (int b = 0; b < nb; ++b) {
-            const unsigned char* st = wait_item(b);
-            const int rb = wb + b * RS;
-#pragma unroll
-            for (int u0 = 0; u0 < RS; u0 += U) {
-                float d[U * REP];
-#pragma unroll
-                for (int u = 0; u < U; ++u) {
-                    const int j = rb + u0 + u;
-                    float kv[PER];
-                    if (owns_newest && j == p.n_keys - 1) {
-#pragma unroll
-                        for (int e = 0; e < PER; ++e) kv[e] = knew[lane * PER + e];
-                    } else {
-                        // rows past this warp's keys hold stale bytes; their scores are discarded
-                        load_row<PER>(reinterpret_cast<const bf16*>(st + (u0 + u) * ROWB) + lane * PER, kv);
-                    }
-#pragma unroll
-                    for (int h = 0; h < REP; ++h) {
-                        float acc = 0.f;
-#pragma unroll
-                        for (int e = 0; e < PER; ++e) acc = fmaf(q[h][e], kv[e], acc);
-                        d[u * REP + h] = acc;
-                    }
-                }
-                const float tot = warp_reduce_scatter<U * REP>(d);
-                constexpr int LPV = 32 / (U * REP);  // lanes per value after the reduce-scatter
-                if (lane % LPV == 0) {
-                    const int idx = lane / LPV;
-                    const int j = rb + u0 + idx / REP;
-                    if (j < we) s_sc[(idx % REP) * chunk + (j - j0)] = score_round(tot, p.scale, p.softcap, p.rounding);
-                }
+        for (int kk = 0; kk < KSTEPS; ++kk) {
+            if (g < REP) {
+                const float* qr = q_s + g * HD + 16 * kk + 2 * t4;
+                qa[kk][0] = pack_bf2(f2bf(qr[0]), f2bf(qr[1]));
+                qa[kk][1] = pack_bf2(f2bf(qr[8]), f2bf(qr[9]));
+            } else {
+                qa[kk][0] = qa[kk][1] = 0u;
             }
-            release_item(b);
+        }
+        for (int it = 0; it < nt; ++it) {
+            const uint32_t tile = wait_full(it);
+            const int3 tk = tile_keys(it);
+            const int kb = tk.x, ke = tk.y;
+            if (owns_newest && newest >= kb + 8 * warp && newest < kb + 8 * warp + 8 && newest < ke)
+                patch_row(tile, newest - kb, knew, 0, HD / 8);
+            float acc[4] = {0.f, 0.f, 0.f, 0.f};
+            const int lr = 8 * warp + (lane & 7);  // this lane's ldmatrix row
+#pragma unroll
+            for (int k2 = 0; k2 < KSTEPS / 2; ++k2) {
+                uint32_t b0, b1, b2, b3;
+                ldsm_x4(tile + tile_off(lr, 4 * k2 + (lane >> 3)), b0, b1, b2, b3);
+                mma_bf16_16816(acc, qa[2 * k2][0], 0u, qa[2 * k2][1], 0u, b0, b1);
+                mma_bf16_16816(acc, qa[2 * k2 + 1][0], 0u, qa[2 * k2 + 1][1], 0u, b2, b3);
+            }
+            if (g < REP) {
+                const int j = kb + 8 * warp + 2 * t4;
+                if (j < ke) s_sc[g * chunk + (j - j0)] = score_round(acc[0], p.scale, p.softcap, p.rounding);
+                if (j + 1 < ke) s_sc[g * chunk + (j + 1 - j0)] = score_round(acc[1], p.scale, p.softcap, p.rounding);
+            }
+            release(it);
         }
     }
-    __syncthreads();
-    // ---- per-head max and sum of exp over this CTA's keys
+    // ---- this warp's (max, sum of exp) per head over its own keys
 #pragma unroll
-    for (int r = 0; r < REP; ++r) {
+    for (int h = 0; h < REP; ++h) {
         float m = -FLT_MAX;
-        for (int i = threadIdx.x; i < n; i += kThreads) m = fmaxf(m, s_sc[r * chunk + i]);
+        for (int i = lane; i < my_count; i += 32) {
+            const int k = my_key(i);
+            if (k >= 0) m = fmaxf(m, s_sc[h * chunk + k]);
+        }
         m = warp_max(m);
-        if (lane == 0) wred[warp * REP + r] = m;
-    }
-    __syncthreads();
-    if (threadIdx.x < REP) {
-        float m = -FLT_MAX;
-        for (int w = 0; w < kWarps; ++w) m = fmaxf(m, wred[w * REP + threadIdx.x]);
-        ml[2 * threadIdx.x] = m;
-    }
-    __syncthreads();
-#pragma unroll
-    for (int r = 0; r < REP; ++r) {
-        const float m = ml[2 * r];
         float l = 0.f;
-        for (int i = threadIdx.x; i < n; i += kThreads) l += expf(s_sc[r * chunk + i] - m);
+        for (int i = lane; i < my_count; i += 32) {
+            const int k = my_key(i);
+            if (k >= 0) l += expf(s_sc[h * chunk + k] - m);
+        }
         l = warp_sum(l);
-        if (lane == 0) wred[warp * REP + r] = l;
-    }
-    __syncthreads();
-    if (threadIdx.x < REP) {
-        float l = 0.f;
-        for (int w = 0; w < kWarps; ++w) l += wred[w * REP + threadIdx.x];
-        ml[2 * threadIdx.x + 1] = l;
+        if (lane == 0) {
+            wml[(warp * REP + h) * 2] = m;
+            wml[(warp * REP + h) * 2 + 1] = l;
+        }
     }
     __syncthreads();
     // every CTA of the cluster has started: its shared memory may now be written
     cluster_wait();
     if (static_cast<int>(threadIdx.x) < CS * REP) {
-        const int c = threadIdx.x / REP, r = threadIdx.x % REP;
-        dsmem_st2(dsmem_addr(&allml[(rank * REP + r) * 2], c), ml[2 * r], ml[2 * r + 1]);
+        const int c = threadIdx.x / REP, h = threadIdx.x % REP;
+        float M = -FLT_MAX;
+        for (int w = 0; w < kWarps; ++w)
+            if (wml[(w * REP + h) * 2 + 1] > 0.f) M = fmaxf(M, wml[(w * REP + h) * 2]);
+        float L = 0.f;
+        for (int w = 0; w < kWarps; ++w) {
+            const float lw = wml[(w * REP + h) * 2 + 1];
+            if (lw > 0.f) L += lw * expf(wml[(w * REP + h) * 2] - M);
+        }
+        dsmem_st2(dsmem_addr(&allml[(rank * REP + h) * 2], c), M, L);
     }
     cluster_sync();
-    if (threadIdx.x < REP) {
-        const int r = threadIdx.x;
-        float M = -FLT_MAX;
-        for (int c = 0; c < CS; ++c) M = fmaxf(M, allml[(c * REP + r) * 2]);
-        float L = 0.f;
-        for (int c = 0; c < CS; ++c) {
-            const float lc = allml[(c * REP + r) * 2 + 1];
-            if (lc > 0.f) L += lc * expf(allml[(c * REP + r) * 2] - M);
-        }
-        stat[2 * r] = M;
-        stat[2 * r + 1] = 1.0f / L;
-    }
-    __syncthreads();
-    // probabilities in place: p = exp(s - M) / L, bf16-rounded unless rounding mode 1
-    for (int i = threadIdx.x; i < REP * n; i += kThreads) {
-        const int r = i / n, k = i - r * n;
-        const float e = expf(s_sc[r * chunk + k] - stat[2 * r]) * stat[2 * r + 1];
-        s_sc[r * chunk + k] = (p.rounding == 0) ? rbf(e) : e;
-    }
-    __syncthreads();
-    // ---- phase 2: P V over this warp's keys
+    // ---- row statistics (lane h < REP), then p in place over this warp's keys
     {
-        float acc[REP][PER];
+        float Ml = 0.f, iLl = 0.f;
+        if (lane < REP) {
+            float M = -FLT_MAX;
+            for (int c = 0; c < CS; ++c) M = fmaxf(M, allml[(c * REP + lane) * 2]);
+            float L = 0.f;
+            for (int c = 0; c < CS; ++c) {
+                const float lc = allml[(c * REP + lane) * 2 + 1];
+                if (lc > 0.f) L += lc * expf(allml[(c * REP + lane) * 2] - M);
+            }
+            Ml = M;
+            iLl = 1.0f / L;
+        }
 #pragma unroll
-        for (int r = 0; r < REP; ++r)
-#pragma unroll
-            for (int e = 0; e < PER; ++e) acc[r][e] = 0.f;
-        for (int b = 0; b < nb; ++b) {
-            const unsigned char* st = wait_item(nb + b);
-            const int rb = wb + b * RS;
-            const int rows = min(RS, we - rb);
-#pragma unroll 4
-            for (int u = 0; u < rows; ++u) {
-                const int j = rb + u;
-                float vv[PER];
-                if (owns_newest && j == p.n_keys - 1) {
-#pragma unroll
-                    for (int e = 0; e < PER; ++e) vv[e] = vnew[lane * PER + e];
-                } else {
-                    load_row<PER>(reinterpret_cast<const bf16*>(st + u * ROWB) + lane * PER, vv);
-                }
-#pragma unroll
-                for (int h = 0; h < REP; ++h) {
-                    const float pr = s_sc[h * chunk + (j - j0)];
-#pragma unroll
-                    for (int e = 0; e < PER; ++e) acc[h][e] = fmaf(pr, vv[e], acc[h][e]);
+        for (int h = 0; h < REP; ++h) {
+            const float M = __shfl_sync(0xffffffffu, Ml, h), iL = __shfl_sync(0xffffffffu, iLl, h);
+            for (int i = lane; i < my_count; i += 32) {
+                const int k = my_key(i);
+                if (k >= 0) {
+                    const float e = expf(s_sc[h * chunk + k] - M) * iL;
+                    s_sc[h * chunk + k] = (p.rounding == 0) ? rbf(e) : e;
                 }
             }
-            release_item(nb + b);
         }
-#pragma unroll
-        for (int r = 0; r < REP; ++r)
-#pragma unroll
-            for (int e = 0; e < PER; ++e) o_w[warp * E + r * HD + lane * PER + e] = acc[r][e];
     }
-    __syncthreads();
-    // ---- sum over warps, push each element's partial to the CTA owning its slice
-    const int per_cta = (E + CS - 1) / CS;
-    for (int i = threadIdx.x; i < E; i += kThreads) {
-        float v = 0.f;
+    __syncthreads();  // P V reads every warp's probabilities
+    // ---- phase 2: O = P V on tensor cores; this warp owns head_dim columns [w HD/8, (w+1) HD/8)
+    float o[NTW][4];
 #pragma unroll
-        for (int w = 0; w < kWarps; ++w) v += o_w[w * E + i];
-        const int owner = i / per_cta;
-        dsmem_st(dsmem_addr(&recv[rank * per_cta + (i - owner * per_cta)], owner), v);
+    for (int nn = 0; nn < NTW; ++nn) o[nn][0] = o[nn][1] = o[nn][2] = o[nn][3] = 0.f;
+    for (int it = nt; it < items; ++it) {
+        const uint32_t tile = wait_full(it);
+        const int3 tk = tile_keys(it - nt);
+        const int kb = tk.x, ke = tk.y;
+        if (owns_newest && newest >= kb && newest < ke)
+            patch_row(tile, newest - kb, vnew, warp * NTW, warp * NTW + NTW);
+#pragma unroll
+        for (int kk = 0; kk < T / 16; ++kk) {
+            // A fragment: p[head g][keys kb + 16 kk + {2t, 2t+1, 2t+8, 2t+9}], zero past the tile's keys
+            float pv[4] = {0.f, 0.f, 0.f, 0.f};
+            if (g < REP) {
+                const int jj = kb + 16 * kk + 2 * t4;
+                const float* pr = s_sc + g * chunk - j0;
+                if (jj < ke) pv[0] = pr[jj];
+                if (jj + 1 < ke) pv[1] = pr[jj + 1];
+                if (jj + 8 < ke) pv[2] = pr[jj + 8];
+                if (jj + 9 < ke) pv[3] = pr[jj + 9];
+            }
+            const bf16 h0 = f2bf(pv[0]), h1 = f2bf(pv[1]), h2 = f2bf(pv[2]), h3 = f2bf(pv[3]);
+            const uint32_t a0 = pack_bf2(h0, h1), a2 = pack_bf2(h2, h3);
+            uint32_t l0 = 0u, l2 = 0u;  // rounding mode 1: fp32 p = hi + lo in two bf16 products
+            if (p.rounding != 0) {
+                l0 = pack_bf2(f2bf(pv[0] - bf2f(h0)), f2bf(pv[1] - bf2f(h1)));
+                l2 = pack_bf2(f2bf(pv[2] - bf2f(h2)), f2bf(pv[3] - bf2f(h3)));
+            }
+            const int lr = 16 * kk + 8 * ((lane >> 3) & 1) + (lane & 7);  // this lane's ldmatrix row (key)
+            if constexpr (NTW == 1) {
+                uint32_t b0, b1;
+                ldsm_x2_t(tile + tile_off(lr, warp), b0, b1);
+                mma_bf16_16816(o[0], a0, 0u, a2, 0u, b0, b1);
+                if (p.rounding != 0) mma_bf16_16816(o[0], l0, 0u, l2, 0u, b0, b1);
+            } else {
+#pragma unroll
+                for (int nn = 0; nn < NTW; nn += 2) {
+                    uint32_t b0, b1, b2, b3;
+                    ldsm_x4_t(tile + tile_off(lr, warp * NTW + nn + (lane >> 4)), b0, b1, b2, b3);
+                    mma_bf16_16816(o[nn], a0, 0u, a2, 0u, b0, b1);
+                    mma_bf16_16816(o[nn + 1], a0, 0u, a2, 0u, b2, b3);
+                    if (p.rounding != 0) {
+                        mma_bf16_16816(o[nn], l0, 0u, l2, 0u, b0, b1);
+                        mma_bf16_16816(o[nn + 1], l0, 0u, l2, 0u, b2, b3);
+                    }
+                }
+            }
+        }
+        release(it);
+    }
+    // ---- push each output element's CTA partial to the CTA owning its slice
+    const int per_cta = (E + CS - 1) / CS;
+    if (g < REP) {
+#pragma unroll
+        for (int nn = 0; nn < NTW; ++nn) {
+#pragma unroll
+            for (int q = 0; q < 2; ++q) {
+                const int i = g * HD + (warp * NTW + nn) * 8 + 2 * t4 + q;
+                const int owner = i / per_cta;
+                dsmem_st(dsmem_addr(&recv[rank * per_cta + (i - owner * per_cta)], owner), o[nn][q]);
+            }
+        }
     }
     cluster_sync();
     // ---- this CTA's slice, summed in rank order
@@ -471,10 +501,11 @@ __global__ void __launch_bounds__(kThreads) decode_attn_fused_kernel(const Decod
         p.out[static_cast<size_t>(hk * REP) * HD + i] = f2bf(v);
     }
     pdl_launch_dependents();
-    if (!waits_ok && lane == 0) {
+    if (__syncthreads_or(!waits_ok) && threadIdx.x == 0) {
         atomicAdd(&g_attn_wait_timeouts, 1);
         // copies that never signalled may still land: wait (bounded) before the CTA exits
-        for (int s = 0; s < stages; ++s) mbar_wait_bounded(bar0 + 8 * s, ((phase_bits >> s) & 1u) ^ 1u);
+        for (int s = 0; s < stages && s < items; ++s)
+            mbar_wait_bounded(full0 + 8 * s, static_cast<uint32_t>((items - 1 - s) / stages) & 1u);
     }
 }
 
@@ -488,10 +519,12 @@ FusedPlan plan_fused(int hd, int rep, int n_keys) {
     f.cs = std::min(kMaxCluster, std::max(1, (n_keys + 127) / 128));
     f.chunk = (n_keys + f.cs - 1) / f.cs;
     f.cs = (n_keys + f.chunk - 1) / f.chunk;
-    for (int s = kMaxStages; s >= 1; s /= 2) {
-        const FusedLayout L = fused_layout(hd, rep, f.chunk, s);
+    const int tile = kTileKeys * hd * 2;
+    // up to 128 KB of tiles in flight; +1 for a possible split at the ring wrap
+    const int items = 2 * ((f.chunk + kTileKeys - 1) / kTileKeys + 1);
+    for (int s = std::min({kMaxStages, items, kRingBytes / tile}); s >= 1; --s) {
         f.stages = s;
-        f.smem = L.total;
+        f.smem = fused_layout(hd, rep, f.chunk, s).total + 1024;  // + alignment slack
         if (f.smem <= kSmemLimit) return f;
     }
     f.stages = 0;
@@ -524,7 +557,12 @@ void launch_fused_t(const DecodeFusedParams& p, cudaStream_t stream, bool pdl) {
     attr[1].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = pdl ? 2 : 1;
-    HYB_CUDA(cudaLaunchKernelEx(&cfg, kern, p, f.chunk, f.stages));
+    CUtensorMap tk, tv;
+    if (p.tmap_k) tk = *p.tmap_k;
+    else encode_kv_tensor_map(&tk, p.k_cache, p.cap, p.n_kv, p.hd);
+    if (p.tmap_v) tv = *p.tmap_v;
+    else encode_kv_tensor_map(&tv, p.v_cache, p.cap, p.n_kv, p.hd);
+    HYB_CUDA(cudaLaunchKernelEx(&cfg, kern, p, f.chunk, f.stages, tk, tv));
 }
 
 template <int PER>
@@ -539,6 +577,28 @@ void launch_fused_rep(const DecodeFusedParams& p, cudaStream_t stream, bool pdl)
 }
 
 }  // namespace
+
+void encode_kv_tensor_map(CUtensorMap* map, const bf16* cache, int cap, int n_kv, int hd) {
+    if ((reinterpret_cast<uintptr_t>(cache) & 15) || cap <= 0 || n_kv <= 0 || (hd != 64 && hd != 128 && hd != 256))
+        throw ArgError("decode attention: bad K/V cache for a tensor map");
+    const cuuint64_t dims[3] = {static_cast<cuuint64_t>(hd), static_cast<cuuint64_t>(n_kv), static_cast<cuuint64_t>(cap)};
+    const cuuint64_t strides[2] = {static_cast<cuuint64_t>(hd) * 2, static_cast<cuuint64_t>(n_kv) * hd * 2};
+    const cuuint32_t box[3] = {64, 1, static_cast<cuuint32_t>(kTileKeys)};  // 128-byte rows, swizzled
+    const cuuint32_t estr[3] = {1, 1, 1};
+    // through the runtime's driver entry point, so the library loads without libcuda
+    static PFN_cuTensorMapEncodeTiled_v12000 encode = nullptr;
+    if (!encode) {
+        void* fn = nullptr;
+        cudaDriverEntryPointQueryResult q = cudaDriverEntryPointSymbolNotFound;
+        HYB_CUDA(cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q));
+        if (q != cudaDriverEntryPointSuccess || !fn) throw CudaError("cuTensorMapEncodeTiled is not available");
+        encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+    }
+    const CUresult r = encode(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<bf16*>(cache), dims, strides, box,
+                              estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) throw CudaError("cuTensorMapEncodeTiled failed with CUresult " + std::to_string(static_cast<int>(r)));
+}
 
 bool decode_attn_fused_fits(int n_heads, int n_kv, int hd, int n_keys) {
     if (n_kv <= 0 || n_heads % n_kv != 0 || (hd != 64 && hd != 128 && hd != 256) || n_keys <= 0) return false;

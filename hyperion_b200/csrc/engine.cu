@@ -381,6 +381,8 @@ std::unique_ptr<KvState> Model::new_kv() const {
             c.v.reset(n);
             HYB_CUDA(cudaMemsetAsync(c.k.p, 0, n * 2, stream_));
             HYB_CUDA(cudaMemsetAsync(c.v.p, 0, n * 2, stream_));
+            encode_kv_tensor_map(&c.tk, c.k.p, static_cast<int>(c.cap), c.nkv, c.hd);
+            encode_kv_tensor_map(&c.tv, c.v.p, static_cast<int>(c.cap), c.nkv, c.hd);
             kv->local.push_back(std::move(c));
         } else {
             GlobalCache c;
@@ -411,6 +413,8 @@ void Model::reserve(KvState& kv, uint32_t n_tokens) const {
         c.k = std::move(nk);
         c.v = std::move(nv);
         c.capacity = static_cast<uint32_t>(need);
+        encode_kv_tensor_map(&c.tk, c.k.p, static_cast<int>(c.capacity), c.nkv, c.hd);
+        encode_kv_tensor_map(&c.tv, c.v.p, static_cast<int>(c.capacity), c.nkv, c.hd);
     }
 }
 
@@ -707,6 +711,8 @@ void Model::decode_layers(KvState& kv) {
             ap.k_cache = c.k.p;
             ap.v_cache = c.v.p;
             ap.cap = static_cast<int>(c.cap);
+            ap.tmap_k = &c.tk;
+            ap.tmap_v = &c.tv;
             ap.n_keys = static_cast<int>(std::min(g.window, pos + 1));  // forward.cc:55-57
             c.committed = pos + 1;
         } else {
@@ -715,6 +721,8 @@ void Model::decode_layers(KvState& kv) {
             ap.k_cache = c.k.p;
             ap.v_cache = c.v.p;
             ap.cap = static_cast<int>(c.capacity);
+            ap.tmap_k = &c.tk;
+            ap.tmap_v = &c.tv;
             ap.n_keys = static_cast<int>(pos + 1);
             c.committed = pos + 1;
         }

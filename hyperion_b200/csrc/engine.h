@@ -73,12 +73,14 @@ struct LocalCache {
     DevPtr<bf16> k, v;
     uint32_t cap = 0, committed = 0;
     int nkv = 0, hd = 0;
+    CUtensorMap tk{}, tv{};  // decode-attention tile maps of k / v (encode_kv_tensor_map)
 };
 
 struct GlobalCache {
     DevPtr<bf16> k, v;
     uint32_t capacity = 0, committed = 0;
     int nkv = 0, hd = 0;
+    CUtensorMap tk{}, tv{};  // re-encoded whenever the buffers grow
 };
 
 struct KvState {

@@ -162,7 +162,15 @@ struct DecodeFusedParams {
     float softcap = 0.0f;
     int rounding = 0;
     bf16* out = nullptr;      // [n_heads, hd]
+    // Optional pre-encoded tensor maps of k_cache / v_cache (encode_kv_tensor_map);
+    // encoded per launch when null.
+    const CUtensorMap* tmap_k = nullptr;
+    const CUtensorMap* tmap_v = nullptr;
 };
+// 3-D tensor map over a [cap, n_kv, hd] bf16 cache whose box is 64 consecutive
+// slots x 64 dims of one KV head, 128-byte swizzled (the fused decode attention's
+// tile is hd/64 such boxes).
+void encode_kv_tensor_map(CUtensorMap* map, const bf16* cache, int cap, int n_kv, int hd);
 void launch_decode_attn_fused(const DecodeFusedParams& p, cudaStream_t stream, bool pdl = false);
 // Whether the fused kernel's shared-memory plan holds n_keys scores (else use the
 // split-K path above).
