@@ -15,7 +15,8 @@
 // "empty" barrier (all 8 warps done); warp (t mod 8) refills the stage of tile t,
 // so no warp waits for another except through data. The first tiles are issued
 // before the programmatic-dependent-launch wait: cache rows of earlier positions
-// never depend on the previous kernel.
+// were written before the host synchronisation that ends every decode step, so
+// they never depend on kernels still in flight.
 //   phase 0  every CTA normalises and rotates its REP query heads from the raw
 //            projection row; the CTA owning the newest position also normalises /
 //            rotates the new K, normalises the new V and appends both to the cache
@@ -243,6 +244,9 @@ __global__ void __launch_bounds__(kThreads) decode_attn_fused_kernel(const Decod
     const uint32_t tiles_u32 = smem_u32(tiles);
     const uint32_t full0 = smem_u32(smem_raw + lay.full), empty0 = smem_u32(smem_raw + lay.empty);
 
+    // The dependent kernel may launch at once (its PDL wait still waits for this grid)
+    // and stream its weights meanwhile.
+    pdl_launch_dependents();
     cluster_arrive_relaxed();  // matched by the wait before the first remote store
     if (threadIdx.x == 0) {
         for (int s = 0; s < stages; ++s) {
@@ -500,7 +504,6 @@ __global__ void __launch_bounds__(kThreads) decode_attn_fused_kernel(const Decod
         for (int c = 0; c < CS; ++c) v += recv[c * per_cta + (i - e0)];
         p.out[static_cast<size_t>(hk * REP) * HD + i] = f2bf(v);
     }
-    pdl_launch_dependents();
     if (__syncthreads_or(!waits_ok) && threadIdx.x == 0) {
         atomicAdd(&g_attn_wait_timeouts, 1);
         // copies that never signalled may still land: wait (bounded) before the CTA exits

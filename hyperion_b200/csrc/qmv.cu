@@ -128,6 +128,8 @@ __global__ void __launch_bounds__(kThreads, 1) qmv_kernel(const QmvParams p) {
     const int my_rbs = (blockIdx.x < geo.nrb) ? (geo.nrb - blockIdx.x + gridDim.x - 1) / gridDim.x : 0;
     const int n_items = my_rbs * my_units;
 
+    // the dependent kernel may launch at once: its PDL wait still waits for this grid
+    pdl_launch_dependents();
     Item<RT> cur;
     if (n_items > 0) load_item<RT>(cur, p, geo, blockIdx.x, warp, g, t);
 
@@ -182,7 +184,6 @@ __global__ void __launch_bounds__(kThreads, 1) qmv_kernel(const QmvParams p) {
         }
     }
     __syncthreads();
-    pdl_launch_dependents();
 
     int buf = 0;
     int it = 0;

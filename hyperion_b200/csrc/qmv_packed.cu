@@ -22,6 +22,7 @@
 #include "tma.cuh"
 
 #include <algorithm>
+#include <type_traits>
 
 namespace hyb {
 
@@ -93,8 +94,18 @@ __device__ __forceinline__ float gelu_tanh_bf16ops(float x) {
 // GEGLU: the interleaved gate/up matrix alternates 16-row gate blocks (even) and the
 // matching up blocks (odd); a CTA processes them as one pair so the epilogue can
 // combine them. BG = row blocks per work group.
+// Named barrier over `count` threads (a team of warps); id 0 is __syncthreads.
+__device__ __forceinline__ void team_sync(int id, int count) {
+    asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
+}
+
+// Work split: the CTA's 8 warps form teams of `team` warps (1, 2, 4 or 8). A team
+// owns whole work groups (one 16-row block, or a gate/up block pair for GEGLU) and
+// splits their K units among its warps; only the team synchronises, on its own
+// named barrier, to sum the warps' partials. With team = 1 warps run fully
+// independently, which keeps their bulk-copy rings streaming on large N.
 template <bool GEGLU>
-__global__ void __launch_bounds__(kThreads, kCtasPerSm) qmv_packed_kernel(const QmvParams p) {
+__global__ void __launch_bounds__(kThreads, kCtasPerSm) qmv_packed_kernel(const QmvParams p, int team) {
     constexpr int BG = GEGLU ? 2 : 1;
     extern __shared__ __align__(128) unsigned char smem_raw[];
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -103,7 +114,7 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) qmv_packed_kernel(const 
     const unsigned char* packed = static_cast<const unsigned char*>(p.packed);
 
     // shared memory: [rings kWarps x kStages x 4608][mbar kWarps x kStages][xp K/2 u32][zero 32]
-    //                [xsum G][red 2 x kWarps x 16][pair 32][tmp 32][xf K (prologue)]
+    //                [xsum G][red 2 x kWarps x 16][pair kWarps x 32][tmp 32]
     unsigned char* ring = smem_raw;
     uint64_t* bars = reinterpret_cast<uint64_t*>(ring + kWarps * kStages * kItemMax);
     uint32_t* xp = reinterpret_cast<uint32_t*>(bars + kWarps * kStages);
@@ -111,46 +122,61 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) qmv_packed_kernel(const 
     float* xsum = reinterpret_cast<float*>(zero_page + 32);
     float* red = xsum + ((pg.G + 3) & ~3);
     float* pairbuf = red + 2 * kWarps * 16;
-    float* tmp = pairbuf + 32;
+    float* tmp = pairbuf + kWarps * 32;
 
     unsigned char* my_ring = ring + warp * kStages * kItemMax;
     const uint32_t my_bar0 = smem_u32(bars + warp * kStages);
 
+    const int W = team;
+    const int tw = warp / W, wt = warp % W;  // team within the CTA, warp within the team
+    const int team_id = static_cast<int>(blockIdx.x) * (kWarps / W) + tw;
+    const int n_teams = static_cast<int>(gridDim.x) * (kWarps / W);
     const int n_groups = (pg.nrb + BG - 1) / BG;
-    const int my_units = (warp < pg.nunits) ? (pg.nunits - warp + kWarps - 1) / kWarps : 0;
-    const int my_groups = (static_cast<int>(blockIdx.x) < n_groups)
-                              ? (n_groups - static_cast<int>(blockIdx.x) + static_cast<int>(gridDim.x) - 1) / gridDim.x
-                              : 0;
+    const int my_units = (wt < pg.nunits) ? (pg.nunits - wt + W - 1) / W : 0;
+    const int my_groups = (team_id < n_groups) ? (n_groups - team_id + n_teams - 1) / n_teams : 0;
     const int per_group = BG * my_units;
     const int n_items = my_groups * per_group;
 
+    // The dependent kernel may launch at once: its own PDL wait still waits for this
+    // grid to complete, and meanwhile it streams its weights (which depend on nothing).
+    pdl_launch_dependents();
     if (lane == 0) {
         for (int s = 0; s < kStages; ++s) mbar_init(my_bar0 + 8 * s, 1);
         mbar_init_fence();
     }
     __syncwarp();
 
-    auto issue = [&](int i) {
+    // Issue cursor: the next item to copy, as (group, block, unit) counters of this
+    // warp's item order; advanced like an odometer (no divisions per item).
+    int ig = 0, ij = 0, iu = 0, n_issued = 0;
+    auto issue_next = [&]() {
+        const int rb = (team_id + ig * n_teams) * BG + ij;
+        const int unit = wt + iu * W;
+        const int s = n_issued % kStages;
+        const uint32_t bar = my_bar0 + 8 * s;
         if (lane == 0) {
-            const int grp = static_cast<int>(blockIdx.x) + (i / per_group) * static_cast<int>(gridDim.x);
-            const int rb = grp * BG + (i / my_units) % BG;
-            const int unit = warp + (i % my_units) * kWarps;
             if (rb < pg.nrb) {
                 const unsigned char* src = packed + rb * pg.rb_bytes + static_cast<long long>(unit) * kItemMax;
                 const uint32_t bytes =
                     (unit == pg.nunits - 1) ? static_cast<uint32_t>(pg.item_last) : static_cast<uint32_t>(kItemMax);
-                const int s = i % kStages;
-                const uint32_t bar = my_bar0 + 8 * s;
                 mbar_expect_tx(bar, bytes);
                 bulk_g2s(smem_u32(my_ring + s * kItemMax), src, bytes, bar);
             } else {
                 // a padding block of an odd block count: complete the phase without data
-                mbar_arrive(my_bar0 + 8 * (i % kStages));
+                mbar_arrive(bar);
+            }
+        }
+        ++n_issued;
+        if (++iu == my_units) {
+            iu = 0;
+            if (++ij == BG) {
+                ij = 0;
+                ++ig;
             }
         }
     };
-    // weights do not depend on the previous kernel: start streaming before the PDL wait
-    for (int i = 0; i < kStages - 1 && i < n_items; ++i) issue(i);
+    // weights do not depend on the previous kernel: fill the ring before the PDL wait
+    while (n_issued < kStages && n_issued < n_items) issue_next();
 
     pdl_wait();
     if (threadIdx.x < 32) zero_page[threadIdx.x] = 0u;
@@ -265,111 +291,136 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) qmv_packed_kernel(const 
         }
     }
     __syncthreads();
-    pdl_launch_dependents();
 
     uint32_t phase_bits = 0;  // one parity bit per stage
     int buf = 0, it = 0;
+    float gate0 = 0.f, gate1 = 0.f;  // team = 1 GEGLU: this lane's gate rows g, g + 8
     for (int gi = 0; gi < my_groups; ++gi) {
-        const int grp = static_cast<int>(blockIdx.x) + gi * static_cast<int>(gridDim.x);
+        const int grp = team_id + gi * n_teams;
         for (int j = 0; j < BG; ++j) {
             const int rb = grp * BG + j;
             float acc0 = 0.f, acc1 = 0.f;
             for (int ui = 0; ui < my_units; ++ui, ++it) {
-                const int unit = warp + ui * kWarps;
-                if (it + kStages - 1 < n_items) {
-                    fence_proxy_async();  // earlier generic reads of the reused stage come first
-                    issue(it + kStages - 1);
+                const int unit = wt + ui * W;
+                if (it >= 1 && n_issued < n_items) {
+                    // refill the stage item it - 1 used; its reads ended before this
+                    // warp's previous mma.sync
+                    fence_proxy_async();
+                    issue_next();
                 }
                 const int s = it % kStages;
                 const bool ok = mbar_wait(my_bar0 + 8 * s, (phase_bits >> s) & 1u);
                 phase_bits ^= (1u << s);
                 if (!ok || rb >= pg.nrb) continue;
-                const int gc = (unit == pg.nunits - 1) ? pg.gc_last : 8;
-                const int tv = (gc + 1) / 2;
-                const int nv = 8 * tv;
-                const bool valid = t < tv;
-                const int rank = g * tv + t;
                 const unsigned char* st = my_ring + s * kItemMax;
-                uint4 wv[8];
+                // Full units (8 groups: every lane valid) take a path without the
+                // per-lane validity selects; only the last unit can be partial.
+                auto item = [&](auto full_tag) {
+                    constexpr bool FULL = decltype(full_tag)::value;
+                    const int tv = FULL ? 4 : (pg.gc_last + 1) / 2;
+                    const int nv = 8 * tv;
+                    const bool valid = FULL || t < tv;
+                    const int rank = g * tv + t;
+                    uint4 wv[8];
 #pragma unroll
-                for (int c = 0; c < 8; ++c)
-                    wv[c] = valid ? *reinterpret_cast<const uint4*>(st + (c * nv + rank) * 16) : make_uint4(0, 0, 0, 0);
-                const uint4 sb =
-                    valid ? *reinterpret_cast<const uint4*>(st + (8 * nv + rank) * 16) : make_uint4(0, 0, 0, 0);
-                const int gA = unit * 8 + 2 * t;
-                const uint32_t* src0 = (g == 2 * t && gA < pg.G) ? xp + gA * 32 : zero_page;
-                const uint32_t* src1 = (g == 2 * t + 1 && gA + 1 < pg.G) ? xp + (gA + 1) * 32 : zero_page;
-                // four independent accumulator chains (one per nibble pair) shorten the
-                // MMA dependency chain to 8
-                float d[4][4];
+                    for (int c = 0; c < 8; ++c)
+                        wv[c] = valid ? *reinterpret_cast<const uint4*>(st + (c * nv + rank) * 16) : make_uint4(0, 0, 0, 0);
+                    const uint4 sb =
+                        valid ? *reinterpret_cast<const uint4*>(st + (8 * nv + rank) * 16) : make_uint4(0, 0, 0, 0);
+                    const int gA = unit * 8 + 2 * t;
+                    const uint32_t* src0 = (g == 2 * t && (FULL || gA < pg.G)) ? xp + gA * 32 : zero_page;
+                    const uint32_t* src1 = (g == 2 * t + 1 && (FULL || gA + 1 < pg.G)) ? xp + (gA + 1) * 32 : zero_page;
+                    // four independent accumulator chains (one per nibble pair) shorten the
+                    // MMA dependency chain to 8
+                    float d[4][4];
 #pragma unroll
-                for (int q = 0; q < 4; ++q) d[q][0] = d[q][1] = d[q][2] = d[q][3] = 0.f;
+                    for (int q = 0; q < 4; ++q) d[q][0] = d[q][1] = d[q][2] = d[q][3] = 0.f;
 #pragma unroll
-                for (int i = 0; i < 8; ++i) {
-                    const uint4 b0v = *reinterpret_cast<const uint4*>(src0 + 4 * i);
-                    const uint4 b1v = *reinterpret_cast<const uint4*>(src1 + 4 * i);
-                    const uint32_t b0s[4] = {b0v.x, b0v.y, b0v.z, b0v.w};
-                    const uint32_t b1s[4] = {b1v.x, b1v.y, b1v.z, b1v.w};
-                    // word i of group A (chunks 0,1 row g; 4,5 row g+8) and group B (2,3 / 6,7)
-                    const uint4 ra0 = wv[i >> 2], ra1 = wv[4 + (i >> 2)];
-                    const uint4 rb0 = wv[2 + (i >> 2)], rb1 = wv[6 + (i >> 2)];
-                    const int cc = i & 3;
-                    const uint32_t xa0 = cc == 0 ? ra0.x : cc == 1 ? ra0.y : cc == 2 ? ra0.z : ra0.w;
-                    const uint32_t xa1 = cc == 0 ? ra1.x : cc == 1 ? ra1.y : cc == 2 ? ra1.z : ra1.w;
-                    const uint32_t xb0 = cc == 0 ? rb0.x : cc == 1 ? rb0.y : cc == 2 ? rb0.z : rb0.w;
-                    const uint32_t xb1 = cc == 0 ? rb1.x : cc == 1 ? rb1.y : cc == 2 ? rb1.z : rb1.w;
+                    for (int i = 0; i < 8; ++i) {
+                        const uint4 b0v = *reinterpret_cast<const uint4*>(src0 + 4 * i);
+                        const uint4 b1v = *reinterpret_cast<const uint4*>(src1 + 4 * i);
+                        const uint32_t b0s[4] = {b0v.x, b0v.y, b0v.z, b0v.w};
+                        const uint32_t b1s[4] = {b1v.x, b1v.y, b1v.z, b1v.w};
+                        // word i of group A (chunks 0,1 row g; 4,5 row g+8) and group B (2,3 / 6,7)
+                        const uint4 ra0 = wv[i >> 2], ra1 = wv[4 + (i >> 2)];
+                        const uint4 rb0 = wv[2 + (i >> 2)], rb1 = wv[6 + (i >> 2)];
+                        const int cc = i & 3;
+                        const uint32_t xa0 = cc == 0 ? ra0.x : cc == 1 ? ra0.y : cc == 2 ? ra0.z : ra0.w;
+                        const uint32_t xa1 = cc == 0 ? ra1.x : cc == 1 ? ra1.y : cc == 2 ? ra1.z : ra1.w;
+                        const uint32_t xb0 = cc == 0 ? rb0.x : cc == 1 ? rb0.y : cc == 2 ? rb0.z : rb0.w;
+                        const uint32_t xb1 = cc == 0 ? rb1.x : cc == 1 ? rb1.y : cc == 2 ? rb1.z : rb1.w;
 #pragma unroll
-                    for (int pp = 0; pp < 4; ++pp) {
-                        const uint32_t a0 = lop3_and_or(xa0 >> (4 * pp), 0x000F000Fu, 0x43004300u);
-                        const uint32_t a1 = lop3_and_or(xa1 >> (4 * pp), 0x000F000Fu, 0x43004300u);
-                        const uint32_t a2 = lop3_and_or(xb0 >> (4 * pp), 0x000F000Fu, 0x43004300u);
-                        const uint32_t a3 = lop3_and_or(xb1 >> (4 * pp), 0x000F000Fu, 0x43004300u);
-                        mma_bf16_16816(d[pp], a0, a1, a2, a3, b0s[pp], b1s[pp]);
+                        for (int pp = 0; pp < 4; ++pp) {
+                            const uint32_t a0 = lop3_and_or(xa0 >> (4 * pp), 0x000F000Fu, 0x43004300u);
+                            const uint32_t a1 = lop3_and_or(xa1 >> (4 * pp), 0x000F000Fu, 0x43004300u);
+                            const uint32_t a2 = lop3_and_or(xb0 >> (4 * pp), 0x000F000Fu, 0x43004300u);
+                            const uint32_t a3 = lop3_and_or(xb1 >> (4 * pp), 0x000F000Fu, 0x43004300u);
+                            mma_bf16_16816(d[pp], a0, a1, a2, a3, b0s[pp], b1s[pp]);
+                        }
                     }
-                }
-                float d0[4], d1[4];
+                    float d0[4], d1[4];
 #pragma unroll
-                for (int c = 0; c < 4; ++c) {
-                    d0[c] = d[0][c] + d[2][c];
-                    d1[c] = d[1][c] + d[3][c];
-                }
-                const float xsA = (gA < pg.G) ? xsum[gA] : 0.f;
-                const float xsB = (gA + 1 < pg.G) ? xsum[gA + 1] : 0.f;
-                // record: {sA(g), sB(g), sA(g+8), sB(g+8), bA(g), bB(g), bA(g+8), bB(g+8)}
-                const float sA0 = __uint_as_float(sb.x << 16), sB0 = __uint_as_float(sb.x & 0xFFFF0000u);
-                const float sA1 = __uint_as_float(sb.y << 16), sB1 = __uint_as_float(sb.y & 0xFFFF0000u);
-                const float bA0 = __uint_as_float(sb.z << 16), bB0 = __uint_as_float(sb.z & 0xFFFF0000u);
-                const float bA1 = __uint_as_float(sb.w << 16), bB1 = __uint_as_float(sb.w & 0xFFFF0000u);
-                acc0 = fmaf(sA0, d0[0] + d1[0], acc0);
-                acc0 = fmaf(sB0, d0[1] + d1[1], acc0);
-                acc0 = fmaf(fmaf(-128.f, sA0, bA0), xsA, acc0);
-                acc0 = fmaf(fmaf(-128.f, sB0, bB0), xsB, acc0);
-                acc1 = fmaf(sA1, d0[2] + d1[2], acc1);
-                acc1 = fmaf(sB1, d0[3] + d1[3], acc1);
-                acc1 = fmaf(fmaf(-128.f, sA1, bA1), xsA, acc1);
-                acc1 = fmaf(fmaf(-128.f, sB1, bB1), xsB, acc1);
+                    for (int c = 0; c < 4; ++c) {
+                        d0[c] = d[0][c] + d[2][c];
+                        d1[c] = d[1][c] + d[3][c];
+                    }
+                    const float xsA = (FULL || gA < pg.G) ? xsum[gA] : 0.f;
+                    const float xsB = (FULL || gA + 1 < pg.G) ? xsum[gA + 1] : 0.f;
+                    // record: {sA(g), sB(g), sA(g+8), sB(g+8), bA(g), bB(g), bA(g+8), bB(g+8)}
+                    const float sA0 = __uint_as_float(sb.x << 16), sB0 = __uint_as_float(sb.x & 0xFFFF0000u);
+                    const float sA1 = __uint_as_float(sb.y << 16), sB1 = __uint_as_float(sb.y & 0xFFFF0000u);
+                    const float bA0 = __uint_as_float(sb.z << 16), bB0 = __uint_as_float(sb.z & 0xFFFF0000u);
+                    const float bA1 = __uint_as_float(sb.w << 16), bB1 = __uint_as_float(sb.w & 0xFFFF0000u);
+                    acc0 = fmaf(sA0, d0[0] + d1[0], acc0);
+                    acc0 = fmaf(sB0, d0[1] + d1[1], acc0);
+                    acc0 = fmaf(fmaf(-128.f, sA0, bA0), xsA, acc0);
+                    acc0 = fmaf(fmaf(-128.f, sB0, bB0), xsB, acc0);
+                    acc1 = fmaf(sA1, d0[2] + d1[2], acc1);
+                    acc1 = fmaf(sB1, d0[3] + d1[3], acc1);
+                    acc1 = fmaf(fmaf(-128.f, sA1, bA1), xsA, acc1);
+                    acc1 = fmaf(fmaf(-128.f, sB1, bB1), xsB, acc1);
+                };
+                if (unit != pg.nunits - 1 || pg.gc_last == 8) item(std::true_type{});
+                else item(std::false_type{});
             }
             acc0 += __shfl_xor_sync(0xffffffffu, acc0, 1);
             acc0 += __shfl_xor_sync(0xffffffffu, acc0, 2);
             acc1 += __shfl_xor_sync(0xffffffffu, acc1, 1);
             acc1 += __shfl_xor_sync(0xffffffffu, acc1, 2);
+            if (W == 1) {
+                // the warp holds the whole sums: lane (g, 0) has rows g and g + 8
+                if (t == 0) {
+                    if (!GEGLU) {
+                        if (rb * 16 + g < pg.N) p.y[rb * 16 + g] = f2bf(acc0);
+                        if (rb * 16 + g + 8 < pg.N) p.y[rb * 16 + g + 8] = f2bf(acc1);
+                    } else if (j == 0) {
+                        gate0 = acc0;
+                        gate1 = acc1;
+                    } else {
+                        const int row = grp * 16 + g;
+                        if (row < pg.N / 2) p.y[row] = f2bf(gelu_tanh_bf16ops(rbf(gate0)) * rbf(acc0));
+                        if (row + 8 < pg.N / 2) p.y[row + 8] = f2bf(gelu_tanh_bf16ops(rbf(gate1)) * rbf(acc1));
+                    }
+                }
+                continue;
+            }
             if (t == 0) {
                 red[(buf * kWarps + warp) * 16 + g] = acc0;
                 red[(buf * kWarps + warp) * 16 + g + 8] = acc1;
             }
-            __syncthreads();
-            if (threadIdx.x < 16) {
+            team_sync(1 + tw, 32 * W);
+            if (wt == 0 && lane < 16) {
                 float v = 0.f;
-#pragma unroll
-                for (int w = 0; w < kWarps; ++w) v += red[(buf * kWarps + w) * 16 + threadIdx.x];
+                for (int w = 0; w < W; ++w) v += red[(buf * kWarps + tw * W + w) * 16 + lane];
+                float* pb = pairbuf + tw * 32;
                 if (!GEGLU) {
-                    const int row = rb * 16 + threadIdx.x;
+                    const int row = rb * 16 + lane;
                     if (row < pg.N) p.y[row] = f2bf(v);
                 } else {
-                    pairbuf[j * 16 + threadIdx.x] = v;  // j = 0 gate rows, j = 1 up rows
+                    pb[j * 16 + lane] = v;  // j = 0 gate rows, j = 1 up rows
                     if (j == 1) {
-                        const float gv = pairbuf[threadIdx.x];
-                        const int row = grp * 16 + threadIdx.x;
+                        const float gv = pb[lane];
+                        const int row = grp * 16 + lane;
                         if (row < pg.N / 2) p.y[row] = f2bf(gelu_tanh_bf16ops(rbf(gv)) * rbf(v));
                     }
                 }
@@ -426,7 +477,7 @@ size_t packed_smem_bytes(int K, bool prologue) {
     const int G = K / 64;
     size_t b = static_cast<size_t>(kWarps) * kStages * kItemMax + kWarps * kStages * 8 +
                static_cast<size_t>(K / 2) * 4 + 32 * 4 + static_cast<size_t>((G + 3) & ~3) * 4 +
-               (2 * kWarps * 16 + 32 + 32) * 4;  // red, pair, tmp
+               (2 * kWarps * 16 + kWarps * 32 + 32) * 4;  // red, pair, tmp
     (void)prologue;  // the norm prologues work in registers
     return b;
 }
@@ -469,7 +520,22 @@ void launch_qmv_packed(const QmvParams& p, cudaStream_t stream, bool pdl) {
     const bool geglu = p.epilogue == QmvEpilogue::kGeglu;
     if (geglu && p.N % 32 != 0) throw ArgError("qmv geglu: interleaved rows must be a multiple of 32");
     const int groups = geglu ? (pg.nrb + 1) / 2 : pg.nrb;
-    const int grid = std::max(1, std::min(groups, kCtasPerSm * num_sms()));
+    // Team size: the one with the fewest items on the busiest warp, the smallest on
+    // ties (independent warps where N is large, the whole CTA on one row block where
+    // it is small).
+    const int max_ctas = kCtasPerSm * num_sms();
+    int team = kWarps, best = 1 << 30;
+    for (int w = kWarps; w >= 1; w /= 2) {
+        const int tpc_w = kWarps / w;
+        const int n_teams = std::min((groups + tpc_w - 1) / tpc_w, max_ctas) * tpc_w;
+        const int load = (groups + n_teams - 1) / n_teams * (geglu ? 2 : 1) * ((pg.nunits + w - 1) / w);
+        if (load <= best) {
+            best = load;
+            team = w;
+        }
+    }
+    const int tpc = kWarps / team;
+    const int grid = std::max(1, std::min((groups + tpc - 1) / tpc, max_ctas));
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(grid);
     cfg.blockDim = dim3(kThreads);
@@ -480,8 +546,8 @@ void launch_qmv_packed(const QmvParams& p, cudaStream_t stream, bool pdl) {
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = pdl ? 1 : 0;
-    if (geglu) HYB_CUDA(cudaLaunchKernelEx(&cfg, qmv_packed_kernel<true>, p));
-    else HYB_CUDA(cudaLaunchKernelEx(&cfg, qmv_packed_kernel<false>, p));
+    if (geglu) HYB_CUDA(cudaLaunchKernelEx(&cfg, qmv_packed_kernel<true>, p, team));
+    else HYB_CUDA(cudaLaunchKernelEx(&cfg, qmv_packed_kernel<false>, p, team));
 }
 
 int64_t read_qmv_wait_timeouts() {

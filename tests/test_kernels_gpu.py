@@ -225,7 +225,9 @@ def test_qmv_fused_prologue_epilogue(built_lib, oracle_lib, K, N, prologue, epil
     assert (got == want).mean() >= 0.98
 
 
-@pytest.mark.parametrize("K,N", CFG1_SHAPES + [(64, 8), (128, 40), (576, 33), (192, 4096), (1024, 17)])
+# (1024, 100008) and (3840, 100008): independent-warp split (team of 1) with a ragged last block
+@pytest.mark.parametrize("K,N", CFG1_SHAPES + [(64, 8), (128, 40), (576, 33), (192, 4096), (1024, 17),
+                                 (1024, 100008), (3840, 100008)])
 def test_qmv_packed_layout(built_lib, oracle_lib, K, N):
     """The TMA-streamed qmv over the packed resident layout (the decode engine's path)."""
     from hyperion_b200 import ops
@@ -249,7 +251,8 @@ def test_qmv_packed_layout(built_lib, oracle_lib, K, N):
 
 
 @pytest.mark.parametrize("K,N,prologue,epilogue,with_scalar", [
-    (256, 2048, 2, 1, False), (3840, 8192, 2, 0, True), (3840, 30720, 2, 1, False), (128, 64, 1, 1, True)])
+    (256, 2048, 2, 1, False), (3840, 8192, 2, 0, True), (3840, 30720, 2, 1, False), (128, 64, 1, 1, True),
+    (256, 151552, 1, 1, False)])  # the last: GEGLU pairs on independent warps
 def test_qmv_packed_fused(built_lib, oracle_lib, K, N, prologue, epilogue, with_scalar):
     """Packed path with the decode engine's fused prologues/epilogues vs the MLX-layout fused kernel."""
     from hyperion_b200 import ops
