@@ -11,7 +11,9 @@ qmv launches of one token, captured in a CUDA graph; value = algorithmic bytes /
 time (GB/s). Per-shape figures are timed separately over >= 48 distinct copies.
 
 `--workload decode` times the engine's full 12B-shaped decode (config 3) through
-hyp_decode_block after a 4096-token prefill: tokens/s.
+hyp_decode_block after a 4096-token prefill: tokens/s. `--workload attn-decode` times
+the fused decode attention alone over the model's 48 layer caches; `--workload
+qmv-shape` one qmv shape (both for profiling).
 
 `--impl reference` times the CPU restatement of the same qmv (the reference's
 own path is MLX, unavailable here) on the host cores.
@@ -165,6 +167,56 @@ def cpu_qmv_baseline(budget_s: float = 10.0):
     return {"value": round(total_bytes / el / 1e9, 2), "unit": "GB/s", "cores": threads, "kind": "port",
             "sample": f"{passes} passes over the six cfg-1 qmv shapes (655 MB each), {el:.1f} s, "
                       f"oracle/hyp_oracle.c orc_qmv_fast, OpenMP {threads} threads"}
+
+
+def cpu_decode_baseline(ctx: int, budget_s: float = 10.0):
+    """CPU tokens/s of the 12B-shaped decode step, from a bounded sample.
+
+    One decoder layer's four fused projections (qkv 3840x8192, o 4096x3840, gate/up
+    3840x30720, down 15360x3840), the lm_head (3840x262144), one sliding-window and
+    one global attention at `ctx` are each timed with the oracle's multithreaded C
+    kernels; a token costs 48 x projections + lm_head + 40 x local + 8 x global
+    attention (norms and elementwise work are left out, which favours the CPU).
+    """
+    import numpy as np
+    from oracle import gemma_oracle as go
+    from hyperion_b200.synth import f32_to_bf16_bits
+    rng = np.random.default_rng(0)
+    threads = go.lib().orc_max_threads()
+
+    def q4(N, K):
+        w = rng.integers(0, 2 ** 32, size=(N, K // 8), dtype=np.uint32)
+        s = f32_to_bf16_bits(np.abs(rng.standard_normal((N, K // 64), dtype=np.float32)) * 0.02)
+        b = f32_to_bf16_bits(-8 * (s.astype(np.uint32) << 16).view(np.float32))
+        return w, s, b
+
+    projs = [(3840, 8192), (4096, 3840), (3840, 30720), (15360, 3840)]
+    layer = [(K, q4(N, K), f32_to_bf16_bits(rng.standard_normal(K, dtype=np.float32))) for K, N in projs]
+    lm = (3840, q4(262144, 3840), f32_to_bf16_bits(rng.standard_normal(3840, dtype=np.float32)))
+    H, Hkv, D = 16, 8, 256
+    q = f32_to_bf16_bits(rng.standard_normal((1, H, D), dtype=np.float32))
+    kv = {n: (f32_to_bf16_bits(rng.standard_normal((n, Hkv, D), dtype=np.float32)),
+              f32_to_bf16_bits(rng.standard_normal((n, Hkv, D), dtype=np.float32))) for n in (1024, ctx)}
+
+    def timed(fn, share):
+        fn()  # warm-up
+        t0, n = time.perf_counter(), 0
+        while True:
+            fn()
+            n += 1
+            if time.perf_counter() - t0 >= share:
+                return (time.perf_counter() - t0) / n
+
+    t_layer = timed(lambda: [go.qmv_fast(x, *wsb, threads) for _, wsb, x in layer], 0.4 * budget_s)
+    t_lm = timed(lambda: go.qmv_fast(lm[2], *lm[1], threads), 0.3 * budget_s)
+    t_loc = timed(lambda: go.sdpa(q, *kv[1024], ctx - 1, ctx - 1024, 0, nthreads=threads), 0.15 * budget_s)
+    t_glb = timed(lambda: go.sdpa(q, *kv[ctx], ctx - 1, 0, 0, nthreads=threads), 0.15 * budget_s)
+    t_tok = 48 * t_layer + t_lm + 40 * t_loc + 8 * t_glb
+    return {"value": round(1.0 / t_tok, 3), "unit": "tok/s", "cores": threads, "kind": "port",
+            "sample": f"one layer's 4 projections ({t_layer * 1e3:.1f} ms), lm_head ({t_lm * 1e3:.1f} ms), "
+                      f"1024-key and {ctx}-key attention ({t_loc * 1e3:.2f} / {t_glb * 1e3:.2f} ms) timed with "
+                      f"oracle/hyp_oracle.c (OpenMP {threads} threads) for ~{budget_s:.0f} s, "
+                      "scaled to 48 layers (40 local, 8 global)"}
 
 
 def run_reference(args):
@@ -452,15 +504,21 @@ def run_decode(args, rank, world, local):
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(local) as clk:
         torch.cuda.synchronize()
+        w0 = time.perf_counter()
         e0.record(stream)
         for _ in range(args.steps):
-            kv.decode(1)
+            kv.decode(1)  # hyp_decode_block: host token in, greedy result read back every step
         e1.record(stream)
         torch.cuda.synchronize()
+        wall_ms = (time.perf_counter() - w0) * 1e3 / args.steps
     ms = max_over_ranks(e0.elapsed_time(e1) / args.steps, world)
+    wall_ms = max_over_ranks(wall_ms, world)
     tok_s = world / (ms * 1e-3)
     if rank != 0:
         return
+    # kernels per token: embed, 5 per layer (qkv, fused attention, o, gate/up+GeGLU, down),
+    # lm_head and the two soft-cap/top-k stages
+    launches_per_step = 1 + 5 * len(geo.layer_types) + 3
     w_bytes = 48 * sum(qmv_bytes(K, N) for _, K, N in PROJ) + qmv_bytes(3840, 262144)
     kv_bytes = 0
     for i, kind in enumerate(geo.layer_types):
@@ -476,11 +534,75 @@ def run_decode(args, rank, world, local):
             "roofline": {"bound": "hbm", "achieved": round(bytes_tok / (ms * 1e-3) / 1e9, 1), "peak": hbm,
                          "unit": "GB/s", "frac": round(bytes_tok / (ms * 1e-3) / 1e9 / hbm, 4), "traffic": None,
                          "peak_source": src, "kernel": "whole decode step (weights + KV bytes per token)"},
-            "gpu_launches": None,
-            "e2e": {"value": round(tok_s, 2), "unit": "tok/s", "h2d_bytes_per_step": 4, "d2h_bytes_per_step": 64,
-                    "path": "hyp_decode_block(n_tokens=1) via ctypes"},
+            "gpu_launches": launches_per_step * args.steps,
+            "e2e": {"value": round(world / (wall_ms * 1e-3), 2), "unit": "tok/s", "h2d_bytes_per_step": 4,
+                    "d2h_bytes_per_step": 64, "path": "hyp_decode_block(n_tokens=1) via ctypes, host wall clock"},
             "clocks": clk.summary()}
+    if world == 1 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_decode_baseline(ctx, args.cpu_seconds)
     print(json.dumps(line), flush=True)
+
+
+# ------------------------------------------------------------------ decode attention alone (profiling)
+def run_attn_decode(args, rank, world, local):
+    """The fused decode attention over the 48 layers of the 12B-shaped model at --ctx:
+    40 sliding layers (1024 keys) and 8 global layers (ctx + 1 keys), each with its own
+    K/V cache, one token per step, captured in a CUDA graph. value = K/V bytes / time."""
+    import torch
+    from hyperion_b200 import ops
+    from hyperion_b200.synth import config3
+    geo = config3()
+    H, ctx = 16, args.ctx
+    g = torch.Generator(device="cuda").manual_seed(7)
+    layers = []
+    for i, kind in enumerate(geo.layer_types):
+        hkv, hd = geo.n_kv(i), geo.head_dim(i)
+        cap = 1032 if kind == 0 else (ctx + 1 + 255) // 256 * 256
+        n_keys = min(1024, ctx + 1) if kind == 0 else ctx + 1
+        kc = torch.randn((cap, hkv, hd), generator=g, device="cuda").to(torch.bfloat16)
+        vc = torch.randn((cap, hkv, hd), generator=g, device="cuda").to(torch.bfloat16)
+        qkv = (3 * torch.randn((H + 2 * hkv) * hd, generator=g, device="cuda")).to(torch.bfloat16)
+        nw = (1 + 0.02 * torch.randn(hd, generator=g, device="cuda")).to(torch.bfloat16)
+        inv = (1.0 / (10000.0 ** (torch.arange(0, hd, 2, device="cuda").float() / hd))).contiguous()
+        out = torch.empty((H, hd), dtype=torch.bfloat16, device="cuda")
+        layers.append((qkv, nw, inv, kc, vc, n_keys, out, 2 * 2 * n_keys * hkv * hd))
+    stream = torch.cuda.Stream()
+
+    def step():
+        for qkv, nw, inv, kc, vc, n_keys, out, _ in layers:
+            ops.sdpa_decode_fused(qkv, False, nw, nw, inv, kc, vc, ctx, n_keys, H, out=out, stream=stream)
+
+    with torch.cuda.stream(stream):
+        step()
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=stream):
+            step()
+        for _ in range(args.warmup):
+            graph.replay()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with ClockSampler(local) as clk:
+            e0.record(stream)
+            for _ in range(args.steps):
+                graph.replay()
+            e1.record(stream)
+            torch.cuda.synchronize()
+    us = e0.elapsed_time(e1) * 1e3 / args.steps
+    kv_bytes = sum(l[7] for l in layers)
+    hbm, _, src = peaks()
+    gbs = kv_bytes / (us * 1e-6) / 1e9
+    print(json.dumps({"metric": "fused decode attention K/V GB/s (48 cfg3 layers per step)", "value": round(gbs, 1),
+                      "unit": "GB/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+                      "ms_per_step": round(us / 1e3, 4), "higher_is_better": True,
+                      "config": {"workload": f"cfg3 decode attention, ctx {ctx}: 40 x 1024-key sliding + 8 x "
+                                             f"{ctx + 1}-key global layers", "kv_bytes_per_step": kv_bytes,
+                                 "l2": "inputs larger than L2"},
+                      "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": hbm, "unit": "GB/s",
+                                   "frac": round(gbs / hbm, 4), "traffic": None, "peak_source": src,
+                                   "kernel": "decode_attn_fused_kernel"},
+                      "us_per_layer_avg": round(us / len(layers), 2), "gpu_launches": len(layers) * args.steps,
+                      "clocks": clk.summary()}), flush=True)
 
 
 def main():
@@ -489,7 +611,7 @@ def main():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="qmv", choices=["qmv", "decode", "qmv-shape"])
+    ap.add_argument("--workload", default="qmv", choices=["qmv", "decode", "qmv-shape", "attn-decode"])
     ap.add_argument("--shape", default="3840,262144", help="K,N for --workload qmv-shape")
     ap.add_argument("--layout", default="packed", choices=["packed", "mlx"], help="weights for qmv-shape")
     ap.add_argument("--ctx", type=int, default=4096)
@@ -508,6 +630,8 @@ def main():
     try:
         if args.workload == "qmv":
             run_qmv(args, rank, world, local)
+        elif args.workload == "attn-decode":
+            run_attn_decode(args, rank, world, local)
         elif args.workload == "qmv-shape":
             run_qmv_shape(args, rank, world, local)
         else:
