@@ -105,8 +105,10 @@ __device__ __forceinline__ float score_round(float dot, float scale, float cap, 
 
 // Normalise one head row of the raw projection (optionally rotate) into `dst`
 // (floats holding bf16-rounded values). One warp; elements e = lane + 32 i.
+// Not inlined: its call sites (query heads, new K, new V) share one copy of the code,
+// which keeps the kernel's cold instruction fetch small (each CTA runs it once).
 template <int PER>
-__device__ void norm_rope_row(const bf16* src, const bf16* nw, const float* inv_freq, int pos, float eps,
+__device__ __noinline__ void norm_rope_row(const bf16* src, const bf16* nw, const float* inv_freq, int pos, float eps,
                               bool rope, float* dst, bf16* cache_dst) {
     const int lane = threadIdx.x & 31;
     constexpr int HD = PER * 32;
@@ -193,7 +195,7 @@ __device__ __forceinline__ uint32_t tile_off(int r, int c) {
     return static_cast<uint32_t>((c >> 3) * (kTileKeys * 128) + r * 128 + (((c & 7) ^ (r & 7)) << 4));
 }
 
-template <int PER, int REP>
+template <int PER, int REP, int ROUND>
 __global__ void __launch_bounds__(kThreads) decode_attn_fused_kernel(const DecodeFusedParams p, int chunk,
                                                                      int stages,
                                                                      const __grid_constant__ CUtensorMap tmk,
@@ -363,8 +365,8 @@ __global__ void __launch_bounds__(kThreads) decode_attn_fused_kernel(const Decod
             }
             if (g < REP) {
                 const int j = kb + 8 * warp + 2 * t4;
-                if (j < ke) s_sc[g * chunk + (j - j0)] = score_round(acc[0], p.scale, p.softcap, p.rounding);
-                if (j + 1 < ke) s_sc[g * chunk + (j + 1 - j0)] = score_round(acc[1], p.scale, p.softcap, p.rounding);
+                if (j < ke) s_sc[g * chunk + (j - j0)] = score_round(acc[0], p.scale, p.softcap, ROUND);
+                if (j + 1 < ke) s_sc[g * chunk + (j + 1 - j0)] = score_round(acc[1], p.scale, p.softcap, ROUND);
             }
             release(it);
         }
@@ -426,7 +428,7 @@ __global__ void __launch_bounds__(kThreads) decode_attn_fused_kernel(const Decod
                 const int k = my_key(i);
                 if (k >= 0) {
                     const float e = expf(s_sc[h * chunk + k] - M) * iL;
-                    s_sc[h * chunk + k] = (p.rounding == 0) ? rbf(e) : e;
+                    s_sc[h * chunk + k] = (ROUND == 0) ? rbf(e) : e;
                 }
             }
         }
@@ -457,7 +459,7 @@ __global__ void __launch_bounds__(kThreads) decode_attn_fused_kernel(const Decod
             const bf16 h0 = f2bf(pv[0]), h1 = f2bf(pv[1]), h2 = f2bf(pv[2]), h3 = f2bf(pv[3]);
             const uint32_t a0 = pack_bf2(h0, h1), a2 = pack_bf2(h2, h3);
             uint32_t l0 = 0u, l2 = 0u;  // rounding mode 1: fp32 p = hi + lo in two bf16 products
-            if (p.rounding != 0) {
+            if (ROUND != 0) {
                 l0 = pack_bf2(f2bf(pv[0] - bf2f(h0)), f2bf(pv[1] - bf2f(h1)));
                 l2 = pack_bf2(f2bf(pv[2] - bf2f(h2)), f2bf(pv[3] - bf2f(h3)));
             }
@@ -466,7 +468,7 @@ __global__ void __launch_bounds__(kThreads) decode_attn_fused_kernel(const Decod
                 uint32_t b0, b1;
                 ldsm_x2_t(tile + tile_off(lr, warp), b0, b1);
                 mma_bf16_16816(o[0], a0, 0u, a2, 0u, b0, b1);
-                if (p.rounding != 0) mma_bf16_16816(o[0], l0, 0u, l2, 0u, b0, b1);
+                if (ROUND != 0) mma_bf16_16816(o[0], l0, 0u, l2, 0u, b0, b1);
             } else {
 #pragma unroll
                 for (int nn = 0; nn < NTW; nn += 2) {
@@ -474,7 +476,7 @@ __global__ void __launch_bounds__(kThreads) decode_attn_fused_kernel(const Decod
                     ldsm_x4_t(tile + tile_off(lr, warp * NTW + nn + (lane >> 4)), b0, b1, b2, b3);
                     mma_bf16_16816(o[nn], a0, 0u, a2, 0u, b0, b1);
                     mma_bf16_16816(o[nn + 1], a0, 0u, a2, 0u, b2, b3);
-                    if (p.rounding != 0) {
+                    if (ROUND != 0) {
                         mma_bf16_16816(o[nn], l0, 0u, l2, 0u, b0, b1);
                         mma_bf16_16816(o[nn + 1], l0, 0u, l2, 0u, b2, b3);
                     }
@@ -534,11 +536,11 @@ FusedPlan plan_fused(int hd, int rep, int n_keys) {
     return f;
 }
 
-template <int PER, int REP>
+template <int PER, int REP, int ROUND>
 void launch_fused_t(const DecodeFusedParams& p, cudaStream_t stream, bool pdl) {
     const FusedPlan f = plan_fused(PER * 32, REP, p.n_keys);
     if (f.stages == 0) throw ArgError("decode attention: too many keys for the shared-memory plan");
-    auto kern = decode_attn_fused_kernel<PER, REP>;
+    auto kern = decode_attn_fused_kernel<PER, REP, ROUND>;
     static int attr_dev = -1;
     int dev = 0;
     HYB_CUDA(cudaGetDevice(&dev));
@@ -571,10 +573,22 @@ void launch_fused_t(const DecodeFusedParams& p, cudaStream_t stream, bool pdl) {
 template <int PER>
 void launch_fused_rep(const DecodeFusedParams& p, cudaStream_t stream, bool pdl) {
     switch (p.n_heads / p.n_kv) {
-        case 1: launch_fused_t<PER, 1>(p, stream, pdl); break;
-        case 2: launch_fused_t<PER, 2>(p, stream, pdl); break;
-        case 4: launch_fused_t<PER, 4>(p, stream, pdl); break;
-        case 8: launch_fused_t<PER, 8>(p, stream, pdl); break;
+        case 1:
+            if (p.rounding == 0) launch_fused_t<PER, 1, 0>(p, stream, pdl);
+            else launch_fused_t<PER, 1, 1>(p, stream, pdl);
+            break;
+        case 2:
+            if (p.rounding == 0) launch_fused_t<PER, 2, 0>(p, stream, pdl);
+            else launch_fused_t<PER, 2, 1>(p, stream, pdl);
+            break;
+        case 4:
+            if (p.rounding == 0) launch_fused_t<PER, 4, 0>(p, stream, pdl);
+            else launch_fused_t<PER, 4, 1>(p, stream, pdl);
+            break;
+        case 8:
+            if (p.rounding == 0) launch_fused_t<PER, 8, 0>(p, stream, pdl);
+            else launch_fused_t<PER, 8, 1>(p, stream, pdl);
+            break;
         default: throw ArgError("decode attention: GQA group must be 1, 2, 4 or 8");
     }
 }
