@@ -438,6 +438,66 @@ def run_qmv(args, rank, world, local):
     print(json.dumps(line), flush=True)
 
 
+# ------------------------------------------------------------------ prefill qmm (config 2)
+def run_qmm(args, rank, world, local):
+    """Config 2: the 12B-shaped projections of one decoder layer (q/k/v fused 3840x8192,
+    o 4096x3840, gate/up fused 3840x30720, down 15360x3840) at M tokens, through
+    hyb_quantized_matmul (tcgen05 tensor cores). value = useful TFLOP/s (2 M K N)."""
+    import torch
+    from hyperion_b200 import ops
+    dev = torch.device("cuda", local)
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(99)
+    shapes = [("qkv", 3840, 8192), ("o", 4096, 3840), ("gate_up", 3840, 30720), ("down", 15360, 3840)]
+    Ms = [int(m) for m in args.qmm_m.split(",")]
+    weights = {nm: make_q4(N, K, gen, dev) for nm, K, N in shapes}
+    stream = torch.cuda.Stream(device=dev)
+    rows, flop_tot, us_tot = [], 0.0, 0.0
+    for M in Ms:
+        xs = {K: torch.randn((M, K), device=dev, generator=gen).to(torch.bfloat16) for _, K, _ in shapes}
+        ys = {nm: torch.empty((M, N), dtype=torch.bfloat16, device=dev) for nm, _, N in shapes}
+
+        def layer():
+            for nm, K, N in shapes:
+                w, s, b = weights[nm]
+                ops.quantized_matmul(xs[K], w, s, b, out=ys[nm], stream=stream)
+
+        with torch.cuda.stream(stream):
+            layer()
+            torch.cuda.synchronize()
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=stream):
+                layer()
+            for _ in range(args.warmup):
+                g.replay()
+            torch.cuda.synchronize()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            with ClockSampler(local) as clk:
+                e0.record(stream)
+                for _ in range(args.steps):
+                    g.replay()
+                e1.record(stream)
+                torch.cuda.synchronize()
+        us = e0.elapsed_time(e1) * 1e3 / args.steps
+        flops = sum(2.0 * M * K * N for _, K, N in shapes)
+        rows.append({"M": M, "us_per_layer": round(us, 1), "TFLOP/s": round(flops / (us * 1e-6) / 1e12, 1)})
+        flop_tot += flops
+        us_tot += us
+        del g
+    _, tf_peak, src = peaks()
+    value = flop_tot / (us_tot * 1e-6) / 1e12
+    print(json.dumps({"metric": "prefill Q4/g64 qmm TFLOP/s (cfg2 12B layer projections)", "value": round(value, 1),
+                      "unit": "TFLOP/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+                      "ms_per_step": round(us_tot / 1e3, 4), "higher_is_better": True, "dtype": "u4->f16, f32 acc",
+                      "data": "synthetic",
+                      "config": {"workload": "cfg2 prefill qmm: qkv 3840x8192, o 4096x3840, gate/up 3840x30720, "
+                                             f"down 15360x3840 at M = {args.qmm_m}"},
+                      "roofline": {"bound": "tensor", "achieved": round(value, 1), "peak": tf_peak, "unit": "TFLOP/s",
+                                   "frac": round(value / tf_peak, 4), "traffic": None, "peak_source": src,
+                                   "kernel": "qmm_tc_kernel"},
+                      "per_m": rows, "gpu_launches": 4 * len(Ms) * args.steps, "clocks": clk.summary()}), flush=True)
+
+
 # ------------------------------------------------------------------ single qmv shape (profiling)
 def run_qmv_shape(args, rank, world, local):
     """One cfg-1 shape over enough distinct copies to exceed 2x L2 (the workload the
@@ -611,7 +671,8 @@ def main():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="qmv", choices=["qmv", "decode", "qmv-shape", "attn-decode"])
+    ap.add_argument("--workload", default="qmv", choices=["qmv", "decode", "qmv-shape", "attn-decode", "qmm"])
+    ap.add_argument("--qmm-m", default="512,2048,8192", help="token counts for --workload qmm")
     ap.add_argument("--shape", default="3840,262144", help="K,N for --workload qmv-shape")
     ap.add_argument("--layout", default="packed", choices=["packed", "mlx"], help="weights for qmv-shape")
     ap.add_argument("--ctx", type=int, default=4096)
@@ -630,6 +691,8 @@ def main():
     try:
         if args.workload == "qmv":
             run_qmv(args, rank, world, local)
+        elif args.workload == "qmm":
+            run_qmm(args, rank, world, local)
         elif args.workload == "attn-decode":
             run_attn_decode(args, rank, world, local)
         elif args.workload == "qmv-shape":

@@ -40,8 +40,6 @@
 #include "kernels.h"
 #include "tma.cuh"
 
-#include <cudaTypedefs.h>
-
 #include <algorithm>
 #include <cfloat>
 #include <string>
@@ -596,25 +594,12 @@ void launch_fused_rep(const DecodeFusedParams& p, cudaStream_t stream, bool pdl)
 }  // namespace
 
 void encode_kv_tensor_map(CUtensorMap* map, const bf16* cache, int cap, int n_kv, int hd) {
-    if ((reinterpret_cast<uintptr_t>(cache) & 15) || cap <= 0 || n_kv <= 0 || (hd != 64 && hd != 128 && hd != 256))
+    if (cap <= 0 || n_kv <= 0 || (hd != 64 && hd != 128 && hd != 256))
         throw ArgError("decode attention: bad K/V cache for a tensor map");
-    const cuuint64_t dims[3] = {static_cast<cuuint64_t>(hd), static_cast<cuuint64_t>(n_kv), static_cast<cuuint64_t>(cap)};
-    const cuuint64_t strides[2] = {static_cast<cuuint64_t>(hd) * 2, static_cast<cuuint64_t>(n_kv) * hd * 2};
-    const cuuint32_t box[3] = {64, 1, static_cast<cuuint32_t>(kTileKeys)};  // 128-byte rows, swizzled
-    const cuuint32_t estr[3] = {1, 1, 1};
-    // through the runtime's driver entry point, so the library loads without libcuda
-    static PFN_cuTensorMapEncodeTiled_v12000 encode = nullptr;
-    if (!encode) {
-        void* fn = nullptr;
-        cudaDriverEntryPointQueryResult q = cudaDriverEntryPointSymbolNotFound;
-        HYB_CUDA(cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q));
-        if (q != cudaDriverEntryPointSuccess || !fn) throw CudaError("cuTensorMapEncodeTiled is not available");
-        encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
-    }
-    const CUresult r = encode(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<bf16*>(cache), dims, strides, box,
-                              estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-                              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-    if (r != CUDA_SUCCESS) throw CudaError("cuTensorMapEncodeTiled failed with CUresult " + std::to_string(static_cast<int>(r)));
+    const uint64_t dims[3] = {static_cast<uint64_t>(hd), static_cast<uint64_t>(n_kv), static_cast<uint64_t>(cap)};
+    const uint64_t strides[2] = {static_cast<uint64_t>(hd) * 2, static_cast<uint64_t>(n_kv) * hd * 2};
+    const uint32_t box[3] = {64, 1, static_cast<uint32_t>(kTileKeys)};  // 128-byte rows, swizzled
+    encode_tma(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, cache, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
 }
 
 bool decode_attn_fused_fits(int n_heads, int n_kv, int hd, int n_keys) {

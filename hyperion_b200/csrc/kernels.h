@@ -57,6 +57,13 @@ void launch_qmv_pack(const uint32_t* w, const bf16* s, const bf16* b, int K, int
 void launch_qmv_packed(const QmvParams& p, cudaStream_t stream, bool pdl = false);
 
 // Prefill GEMM for M >= 2 (tensor cores; fp16 operands, fp32 accumulation).
+// Prefill qmm on tcgen05 tensor cores with TMEM accumulators (qmm_tc.cu): 128x256 output
+// tiles, f16 operands dequantised in shared memory, fp32 accumulation.
+bool qmm_tc_supported(int M, int K, int N);
+void launch_qmm_tc(const bf16* x, const uint32_t* w, const bf16* s, const bf16* b, bf16* y, int M, int K, int N,
+                   cudaStream_t stream);
+int64_t read_qmm_wait_timeouts();
+// Legacy prefill qmm on mma.sync (qmm.cu).
 void launch_qmm(const bf16* x, const uint32_t* w, const bf16* s, const bf16* b, bf16* y,
                 int M, int K, int N, cudaStream_t stream);
 
@@ -167,6 +174,11 @@ struct DecodeFusedParams {
     const CUtensorMap* tmap_k = nullptr;
     const CUtensorMap* tmap_v = nullptr;
 };
+// Tiled TMA tensor map (rank <= 5): dims innermost first, strides in bytes for dims
+// 1..rank-1, box in elements; no interleave, zero fill out of bounds (tma_host.cu).
+void encode_tma(CUtensorMap* map, CUtensorMapDataType dtype, int rank, const void* base, const uint64_t* dims,
+                const uint64_t* strides_bytes, const uint32_t* box, CUtensorMapSwizzle swizzle);
+
 // 3-D tensor map over a [cap, n_kv, hd] bf16 cache whose box is 64 consecutive
 // slots x 64 dims of one KV head, 128-byte swizzled (the fused decode attention's
 // tile is hd/64 such boxes).

@@ -318,7 +318,7 @@ HypStatus hyb_qkv_post(const void* qkv, int32_t L, int32_t ld, int32_t n_heads, 
 
 HypStatus hyb_wait_timeouts(int64_t* count) {
     if (!count) return hyb::abi_fail(HYP_STATUS_INVALID_ARGUMENT, "count is null");
-    return run([&] { *count = hyb::read_qmv_wait_timeouts() + hyb::read_attn_wait_timeouts(); });
+    return run([&] { *count = hyb::read_qmv_wait_timeouts() + hyb::read_attn_wait_timeouts() + hyb::read_qmm_wait_timeouts(); });
 }
 
 }  // extern "C"

@@ -204,6 +204,8 @@ void launch_quantized_matmul(const bf16* x, const uint32_t* w, const bf16* s, co
         // Programmatic dependent launch: the kernel reads only weights before
         // griddepcontrol.wait, so its first loads may overlap the previous kernel.
         launch_qmv(p, stream, true);
+    } else if (qmm_tc_supported(M, K, N)) {
+        launch_qmm_tc(x, w, s, b, y, M, K, N, stream);
     } else {
         launch_qmm(x, w, s, b, y, M, K, N, stream);
     }

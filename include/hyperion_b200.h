@@ -151,7 +151,7 @@ HypStatus hyb_sdpa_decode_fused(const void* qkv, int32_t v_from_k, const void* q
 /*
  * Count of bounded shared-memory waits (mbarrier, bulk-copy completion) that gave
  * up on the current device since the library was loaded, summed over the
- * streaming qmv and the fused decode attention. A wait that gives up leaves that
+ * streaming qmv, the fused decode attention and the tensor-core prefill qmm. A wait that gives up leaves that
  * launch's output undefined but never hangs the GPU; the count is expected to stay
  * 0. No reference counterpart (the reference's kernels are MLX's).
  */
