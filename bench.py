@@ -551,9 +551,13 @@ def run_decode(args, rank, world, local):
     from hyperion_b200.synth import config3
     geo = config3()
     eng = hb.Engine(geo, synthetic_seed=1 + rank)
-    kv = eng.new_kv()
     ctx = args.ctx
     prompt = [int(t) for t in torch.randint(0, geo.vocab_size, (ctx,), generator=torch.Generator().manual_seed(5))]
+    warm = eng.new_kv()  # first prefill pays one-time costs (module load, pools, tensor maps)
+    warm.prefill(prompt)
+    del warm
+    kv = eng.new_kv()
+    torch.cuda.synchronize()
     t0 = time.perf_counter()
     kv.prefill(prompt)
     prefill_s = time.perf_counter() - t0
@@ -590,6 +594,7 @@ def run_decode(args, rank, world, local):
             "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "u4/bf16->f32", "data": "synthetic",
             "config": {"workload": f"cfg3 12B-shaped decode, ctx {ctx}, batch 1", "prefill_s": round(prefill_s, 3),
+                       "prefill_tok_s": round(ctx / prefill_s, 1),
                        "l2": "inputs larger than L2"},
             "roofline": {"bound": "hbm", "achieved": round(bytes_tok / (ms * 1e-3) / 1e9, 1), "peak": hbm,
                          "unit": "GB/s", "frac": round(bytes_tok / (ms * 1e-3) / 1e9 / hbm, 4), "traffic": None,

@@ -103,7 +103,7 @@ ABI_FUNCTIONS = [
 EXT_FUNCTIONS = [
     "hyb_build_info", "hyb_quantized_matmul", "hyb_qmv_fused", "hyb_qmv_packed_bytes", "hyb_qmv_pack",
     "hyb_qmv_packed", "hyb_sdpa_decode_scratch_bytes", "hyb_sdpa_decode", "hyb_sdpa_decode_noalloc",
-    "hyb_sdpa_decode_fused", "hyb_wait_timeouts",
+    "hyb_sdpa_decode_fused", "hyb_wait_timeouts", "hyb_nccl_unique_id", "hyb_model_set_tensor_parallel",
     "hyb_sdpa_prefill", "hyb_rms_norm", "hyb_qkv_post", "hyb_model_load_synthetic",
     "hyb_model_set_attention_rounding", "hyb_model_stream",
     "hyb_kv_copy_layer", "hyb_kv_cursor", "hyb_prefill_logits", "hyb_decode_logits", "hyb_decode_forced",
@@ -149,6 +149,8 @@ def lib() -> ctypes.CDLL:
         "hyb_sdpa_decode_fused": [P, c.c_int32, P, P, P, c.c_float, P, P, c.c_int32, c.c_int32, c.c_int32,
                                   c.c_int32, c.c_int32, c.c_int32, c.c_float, c.c_float, c.c_int32, P, P],
         "hyb_wait_timeouts": [c.POINTER(c.c_int64)],
+        "hyb_nccl_unique_id": [P],
+        "hyb_model_set_tensor_parallel": [P, c.c_int32, c.c_int32, P],
         "hyb_sdpa_decode_noalloc": [P, P, P, P, c.c_int32, c.c_int32, c.c_int32, c.c_int32, c.c_int32,
                                     c.c_int32, c.c_float, c.c_float, c.c_int32, P],
         "hyb_sdpa_prefill": [P, P, P, P, c.c_int32, c.c_int32, c.c_int32, c.c_int32, c.c_int32, c.c_int32,
@@ -182,6 +184,31 @@ def last_error() -> str:
     buf = ctypes.create_string_buffer(1024)
     lib().hyp_last_error(buf, 1024)
     return buf.value.decode(errors="replace")
+
+
+def tp_shard_check(geo, tp: int) -> Optional[str]:
+    """Why `geo` cannot be split over `tp` ranks (the engine's rule), or None if it can:
+    heads and KV heads split evenly, MLP rows in 16-row tiles and 64-wide K groups, the
+    per-rank attention width in 64-wide groups, and the vocabulary evenly."""
+    if tp < 1 or tp > 8:
+        return "tensor parallel size must be 1..8"
+    if tp == 1:
+        return None
+    h, i, v = geo.num_attention_heads, geo.intermediate_size, geo.vocab_size
+    if h % tp or i % (16 * tp) or v % tp or (i // tp) % 64:
+        return "heads, MLP rows and vocabulary must split evenly over the ranks"
+    if (h // tp) * geo.head_dim_local % 64 or (h // tp) * geo.head_dim_global % 64:
+        return "the per-rank attention width must be a multiple of 64"
+    if geo.num_kv_heads_local % tp or geo.num_kv_heads_global % tp:
+        return "KV heads must split evenly over the ranks"
+    return None
+
+
+def nccl_unique_id() -> bytes:
+    """128-byte NCCL unique id for hyb_model_set_tensor_parallel (created on rank 0)."""
+    buf = ctypes.create_string_buffer(128)
+    check(lib().hyb_nccl_unique_id(buf))
+    return buf.raw
 
 
 def check(status: int) -> None:
@@ -223,13 +250,23 @@ def geometry_params(geo) -> HypGeometryParams:
 class Engine:
     """Owns a HypModel; thin Pythonic layer over the C ABI (used by tests and bench)."""
 
-    def __init__(self, geo, weights_dir: Optional[str] = None, synthetic_seed: Optional[int] = None):
+    def __init__(self, geo, weights_dir: Optional[str] = None, synthetic_seed: Optional[int] = None,
+                 tp: Optional[tuple] = None):
+        """tp = (rank, size, unique_id bytes) loads this rank's tensor-parallel shard."""
         L = lib()
         self.geo = geo
         self.vocab = geo.vocab_size
         self._model = ctypes.c_void_p()
         check(L.hyp_model_create(ctypes.byref(self._model)))
         self._params = geometry_params(geo)
+        if tp is not None:
+            rank, size, uid = tp
+            buf = ctypes.create_string_buffer(bytes(uid), 128)
+            st = L.hyb_model_set_tensor_parallel(self._model, rank, size, buf)
+            if st != OK:
+                msg = last_error()
+                L.hyp_model_free(ctypes.byref(self._model))
+                raise HypError(st, msg)
         if synthetic_seed is not None:
             st = L.hyb_model_load_synthetic(self._model, ctypes.byref(self._params), synthetic_seed)
         else:

@@ -19,7 +19,7 @@ NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 FLAGS = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC,-Wall", "--expt-relaxed-constexpr",
          "-I", os.path.join(REPO, "include"), "-I", CSRC]
-SOURCES = ["qmv.cu", "qmv_packed.cu", "qmm.cu", "attention.cu", "attention_fused.cu", "tma_host.cu", "qmm_tc.cu", "elementwise.cu", "engine.cu", "abi.cu", "ops_abi.cu",
+SOURCES = ["qmv.cu", "qmv_packed.cu", "qmm.cu", "attention.cu", "attention_fused.cu", "tma_host.cu", "qmm_tc.cu", "tp.cu", "elementwise.cu", "engine.cu", "abi.cu", "ops_abi.cu",
            "geometry.cc", "safetensors.cc"]
 
 
@@ -61,7 +61,7 @@ def build(force: bool = False, verbose_ptxas: bool = False) -> str:
         list(ex.map(lambda s: _compile(s, extra), todo))
     objs = [_obj(s) for s in SOURCES]
     if force or todo or not os.path.exists(LIB) or os.path.getmtime(LIB) < max(os.path.getmtime(o) for o in objs):
-        cmd = [NVCC, *ARCH, "-shared", "-o", LIB + ".tmp", *objs, "-lcudart", "-lcuda"]
+        cmd = [NVCC, *ARCH, "-shared", "-o", LIB + ".tmp", *objs, "-lcudart", "-lcuda", "-ldl"]
         r = subprocess.run(cmd, capture_output=True, text=True)
         if r.returncode != 0:
             raise RuntimeError(f"link failed:\n{r.stdout}\n{r.stderr}")

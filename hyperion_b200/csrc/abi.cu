@@ -27,6 +27,8 @@ struct HypModelOpaque {
     uint32_t magic;
     bool loaded = false;
     std::unique_ptr<hyb::Model> model;
+    int tp_rank = 0, tp_size = 1;       // tensor parallelism requested before the load
+    unsigned char tp_id[128] = {};
 };
 
 struct HypKvStateOpaque {
@@ -327,6 +329,7 @@ HypStatus load_common(HypModel model, const HypGeometryParams* geometry, const c
             return fail(HYP_STATUS_UNSUPPORTED, "no CUDA device is available");
         }
         auto m = std::make_unique<hyb::Model>();
+        if (model->tp_size > 1) m->set_tensor_parallel(model->tp_rank, model->tp_size, model->tp_id);
         if (synthetic) m->load_synthetic(g, seed);
         else m->load_dir(g, path);
         model->model = std::move(m);
@@ -599,6 +602,27 @@ HypStatus hyb_model_stream(HypModel model, void** out_stream) {
     if (out_stream == nullptr) return fail(HYP_STATUS_INVALID_ARGUMENT, "out_stream is null");
     if (!model->loaded) return fail(HYP_STATUS_INVALID_ARGUMENT, "model is not loaded");
     *out_stream = model->model->stream();
+    return ok();
+}
+
+HypStatus hyb_nccl_unique_id(void* out128) {
+    if (out128 == nullptr) return fail(HYP_STATUS_INVALID_ARGUMENT, "output buffer is null");
+    return guarded("hyb_nccl_unique_id", [&]() -> HypStatus {
+        hyb::TpComm::unique_id(out128);
+        return ok();
+    });
+}
+
+HypStatus hyb_model_set_tensor_parallel(HypModel model, int32_t rank, int32_t size, const void* unique_id) {
+    HypStatus st = validate_model(model);
+    if (st != HYP_STATUS_OK) return st;
+    if (model->loaded) return fail(HYP_STATUS_INVALID_ARGUMENT, "tensor parallelism must be set before hyp_model_load");
+    if (size < 1 || size > 8 || rank < 0 || rank >= size)
+        return fail(HYP_STATUS_INVALID_ARGUMENT, "tensor parallel rank/size out of range (size 1..8)");
+    if (size > 1 && unique_id == nullptr) return fail(HYP_STATUS_INVALID_ARGUMENT, "unique_id is null");
+    model->tp_rank = rank;
+    model->tp_size = size;
+    if (unique_id) std::memcpy(model->tp_id, unique_id, sizeof(model->tp_id));
     return ok();
 }
 

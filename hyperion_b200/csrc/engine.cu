@@ -96,16 +96,26 @@ __device__ __forceinline__ float hash_normal(uint64_t key) {
     return sqrtf(-2.0f * logf(u1)) * cospif(2.0f * u2);
 }
 
-__global__ void synth_words_kernel(uint32_t* w, size_t n, uint64_t seed) {
+// A [rows, cols] block of a [*, ld] logical matrix whose element (r, c) is keyed by its
+// flat index r * ld + c, so a tensor-parallel shard generates exactly the values of
+// the TP = 1 matrix at (row0 + r, col0 + c).
+struct Block {
+    size_t rows, cols, ld, row0, col0;
+    __device__ size_t key(size_t i) const { return (row0 + i / cols) * ld + col0 + i % cols; }
+};
+
+__global__ void synth_words_kernel(uint32_t* w, Block blk, uint64_t seed) {
+    const size_t n = blk.rows * blk.cols;
     for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < n;
          i += static_cast<size_t>(gridDim.x) * blockDim.x)
-        w[i] = static_cast<uint32_t>(mix64(seed * 0x100000001B3ull + i));
+        w[i] = static_cast<uint32_t>(mix64(seed * 0x100000001B3ull + blk.key(i)));
 }
 // scales = bf16(|N(0, std)|), biases = bf16(-8 * scales)
-__global__ void synth_sb_kernel(bf16* s, bf16* b, size_t n, uint64_t seed, float std) {
+__global__ void synth_sb_kernel(bf16* s, bf16* b, Block blk, uint64_t seed, float std) {
+    const size_t n = blk.rows * blk.cols;
     for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < n;
          i += static_cast<size_t>(gridDim.x) * blockDim.x) {
-        const bf16 sv = f2bf(fabsf(std * hash_normal(seed * 0x100000001B3ull + i)));
+        const bf16 sv = f2bf(fabsf(std * hash_normal(seed * 0x100000001B3ull + blk.key(i))));
         s[i] = sv;
         b[i] = f2bf(-8.0f * bf2f(sv));
     }
@@ -135,17 +145,45 @@ __global__ void geglu_interleaved_kernel(const bf16* __restrict__ gu, bf16* __re
     }
 }
 
+// (idx0 + vocab0, val0, idx1 + vocab0, val1) of this rank's top-2 as four 32-bit words
+__global__ void tp_candidates_kernel(const uint32_t* idx, const float* val, uint32_t vocab0, uint32_t* cand) {
+    if (threadIdx.x == 0) {
+        cand[0] = idx[0] + vocab0;
+        cand[1] = __float_as_uint(val[0]);
+        cand[2] = idx[1] + vocab0;
+        cand[3] = __float_as_uint(val[1]);
+    }
+}
+
 int grid_for(size_t n) { return static_cast<int>(std::min<size_t>((n + 255) / 256, 4096)); }
 
-void synth_qlin(QLin& q, int N, int K, uint64_t seed, cudaStream_t st) {
+// Rows [row0, row0 + rows) x columns [col0, col0 + K) of a synthetic [*, K_full] Q4
+// matrix, written at row dst_row of q (whose shape is [q.N, q.K]).
+void synth_block(QLin& q, int dst_row, int rows, int row0, int col0, int K_full, uint64_t seed, cudaStream_t st) {
+    const int K = q.K;
+    const Block bw{static_cast<size_t>(rows), static_cast<size_t>(K / 8), static_cast<size_t>(K_full / 8),
+                   static_cast<size_t>(row0), static_cast<size_t>(col0 / 8)};
+    const Block bs{static_cast<size_t>(rows), static_cast<size_t>(K / 64), static_cast<size_t>(K_full / 64),
+                   static_cast<size_t>(row0), static_cast<size_t>(col0 / 64)};
+    synth_words_kernel<<<grid_for(bw.rows * bw.cols), 256, 0, st>>>(q.w.p + static_cast<size_t>(dst_row) * (K / 8), bw,
+                                                                     seed);
+    synth_sb_kernel<<<grid_for(bs.rows * bs.cols), 256, 0, st>>>(q.s.p + static_cast<size_t>(dst_row) * (K / 64),
+                                                                 q.b.p + static_cast<size_t>(dst_row) * (K / 64), bs,
+                                                                 seed ^ 0x5151, 0.02f);
+    HYB_LAUNCH_CHECK("synth_block");
+}
+
+void alloc_qlin(QLin& q, int N, int K) {
     q.N = N;
     q.K = K;
     q.w.reset(static_cast<size_t>(N) * K / 8);
     q.s.reset(static_cast<size_t>(N) * K / 64);
     q.b.reset(static_cast<size_t>(N) * K / 64);
-    synth_words_kernel<<<grid_for(q.w.n), 256, 0, st>>>(q.w.p, q.w.n, seed);
-    synth_sb_kernel<<<grid_for(q.s.n), 256, 0, st>>>(q.s.p, q.b.p, q.s.n, seed ^ 0x5151, 0.02f);
-    HYB_LAUNCH_CHECK("synth_qlin");
+}
+
+void synth_qlin(QLin& q, int N, int K, uint64_t seed, cudaStream_t st) {
+    alloc_qlin(q, N, K);
+    synth_block(q, 0, N, 0, 0, K, seed, st);
 }
 
 void synth_norm(DevPtr<bf16>& d, size_t n, uint64_t seed, cudaStream_t st) {
@@ -180,12 +218,34 @@ void load_vec(DevPtr<bf16>& d, const Checkpoint& ck, const std::string& name, in
 Model::~Model() {
     if (ws_.h_topk_idx) cudaFreeHost(ws_.h_topk_idx);
     if (ws_.h_topk_val) cudaFreeHost(ws_.h_topk_val);
+    if (ws_.h_cand) cudaFreeHost(ws_.h_cand);
     if (ws_.h_ids) cudaFreeHost(ws_.h_ids);
     if (stream_) cudaStreamDestroy(stream_);
 }
 
+void Model::set_tensor_parallel(int rank, int size, const void* id) {
+    if (loaded_) throw ArgError("tensor parallelism must be set before the model is loaded");
+    if (size < 1 || rank < 0 || rank >= size) throw ArgError("tensor parallel: bad rank / size");
+    tp_rank_ = rank;
+    tp_size_ = size;
+    if (id) std::memcpy(tp_id_, id, sizeof(tp_id_));
+}
+
 void Model::init_common(const Geometry& g) {
+    const int T = tp_size_;
+    if (T > 1) {
+        if (g.n_heads % T || g.intermediate % (16 * T) || g.vocab % T || (g.n_heads / T) * g.hd_local % 64 ||
+            (g.n_heads / T) * g.hd_global % 64 || (g.intermediate / T) % 64)
+            throw ArgError("tensor parallel: heads, MLP rows (16-row tiles, 64-wide groups) and vocabulary must "
+                           "split evenly over the ranks");
+        for (uint32_t i = 0; i < g.n_layers; ++i)
+            if (g.n_kv(i) % T) throw ArgError("tensor parallel: KV heads must split evenly over the ranks");
+    }
     geo_ = g;
+    heads_local_ = static_cast<int>(g.n_heads) / T;
+    inter_local_ = static_cast<int>(g.intermediate) / T;
+    vocab_local_ = static_cast<int>(g.vocab) / T;
+    vocab0_ = tp_rank_ * vocab_local_;
     HYB_CUDA(cudaGetDevice(&device_));
     if (!stream_) HYB_CUDA(cudaStreamCreateWithFlags(&stream_, cudaStreamNonBlocking));
     auto inv_l = rope_inv_freq(g.hd_local, g.rope_local);
@@ -201,8 +261,8 @@ void Model::init_common(const Geometry& g) {
         LayerW& L = layers_[i];
         L.kind = g.kinds[i];
         L.hd = static_cast<int>(g.head_dim(i));
-        L.nkv = static_cast<int>(g.n_kv(i));
-        L.q_rows = static_cast<int>(g.n_heads) * L.hd;
+        L.nkv = static_cast<int>(g.n_kv(i)) / T;
+        L.q_rows = heads_local_ * L.hd;
         L.k_rows = L.nkv * L.hd;
         L.v_rows = (L.kind == LayerKind::Full && g.k_eq_v_global) ? 0 : L.nkv * L.hd;
         L.inv_freq = L.kind == LayerKind::Full ? inv_freq_global_.p : inv_freq_local_.p;
@@ -220,21 +280,40 @@ void Model::pack_all() {
         pack(L.gateup);
         pack(L.down);
     }
-    pack(embed_);
+    // the lm_head: this rank's rows of the tied embedding table
+    const int H = embed_.K;
+    lm_packed_.reset(qmv_packed_bytes(H, vocab_local_));
+    launch_qmv_pack(embed_.w.p + static_cast<size_t>(vocab0_) * (H / 8), embed_.s.p + static_cast<size_t>(vocab0_) * (H / 64),
+                    embed_.b.p + static_cast<size_t>(vocab0_) * (H / 64), H, vocab_local_, lm_packed_.p, stream_);
     HYB_CUDA(cudaStreamSynchronize(stream_));
 }
 
 void Model::load_synthetic(const Geometry& g, uint64_t seed) {
     init_common(g);
+    if (tp_size_ > 1) tp_.init(tp_rank_, tp_size_, tp_id_);
     const int H = static_cast<int>(g.hidden), I = static_cast<int>(g.intermediate);
+    const int r = tp_rank_, T = tp_size_;
     uint64_t tag = seed * 1000003ull;
-    synth_qlin(embed_, static_cast<int>(g.vocab), H, ++tag, stream_);
+    synth_qlin(embed_, static_cast<int>(g.vocab), H, ++tag, stream_);  // replicated table
     synth_norm(final_norm_, H, ++tag, stream_);
     for (auto& L : layers_) {
-        synth_qlin(L.qkv, L.q_rows + L.k_rows + L.v_rows, H, ++tag, stream_);
-        synth_qlin(L.o, H, static_cast<int>(g.n_heads) * L.hd, ++tag, stream_);
-        synth_qlin(L.gateup, 2 * I, H, ++tag, stream_);
-        synth_qlin(L.down, H, I, ++tag, stream_);
+        // q/k/v: this rank's head rows of the TP = 1 [q; k; v] matrix
+        const int qf = static_cast<int>(g.n_heads) * L.hd, kf = L.k_rows * T, vf = L.v_rows * T;
+        alloc_qlin(L.qkv, L.q_rows + L.k_rows + L.v_rows, H);
+        const uint64_t tq = ++tag;
+        synth_block(L.qkv, 0, L.q_rows, r * L.q_rows, 0, H, tq, stream_);
+        synth_block(L.qkv, L.q_rows, L.k_rows, qf + r * L.k_rows, 0, H, tq, stream_);
+        if (L.v_rows) synth_block(L.qkv, L.q_rows + L.k_rows, L.v_rows, qf + kf + r * L.v_rows, 0, H, tq, stream_);
+        (void)vf;
+        // o: all rows, this rank's heads' K range
+        alloc_qlin(L.o, H, L.q_rows);
+        synth_block(L.o, 0, H, 0, r * L.q_rows, qf, ++tag, stream_);
+        // gate/up interleaved by 16-row tiles: this rank's contiguous range of tiles
+        alloc_qlin(L.gateup, 2 * inter_local_, H);
+        synth_block(L.gateup, 0, 2 * inter_local_, r * 2 * inter_local_, 0, H, ++tag, stream_);
+        // down: all rows, this rank's K range of the MLP
+        alloc_qlin(L.down, H, inter_local_);
+        synth_block(L.down, 0, H, 0, r * inter_local_, I, ++tag, stream_);
         synth_norm(L.q_norm, L.hd, ++tag, stream_);
         synth_norm(L.k_norm, L.hd, ++tag, stream_);
         synth_norm(L.in_ln, H, ++tag, stream_);
@@ -249,6 +328,7 @@ void Model::load_synthetic(const Geometry& g, uint64_t seed) {
 }
 
 void Model::load_dir(const Geometry& g, const std::string& dir) {
+    if (tp_size_ > 1) throw ArgError("tensor-parallel loading from a checkpoint directory is not supported yet");
     Checkpoint ck(dir);
     init_common(g);
     const int64_t H = g.hidden, I = g.intermediate, V = g.vocab;
@@ -431,7 +511,7 @@ uint64_t Model::global_kv_bytes(const KvState& kv) const {
 
 void Model::ensure_workspace(int tokens, uint32_t max_keys) {
     const Geometry& g = geo_;
-    const int H = static_cast<int>(g.hidden), I = static_cast<int>(g.intermediate);
+    const int H = static_cast<int>(g.hidden), I = inter_local_;
     int max_qkv = 0, max_attn = 0, max_kv_row = 0, max_hd = 0;
     for (const auto& L : layers_) {
         max_qkv = std::max(max_qkv, L.q_rows + L.k_rows + L.v_rows);
@@ -464,17 +544,22 @@ void Model::ensure_workspace(int tokens, uint32_t max_keys) {
         ws_.h_ids_cap = tokens;
     }
     if (ws_.logits.n == 0) {
-        ws_.logits.reset(g.vocab);
-        const int tsf = softcap_topk_scratch_floats(static_cast<int>(g.vocab));
+        ws_.logits.reset(vocab_local_);
+        if (tp_size_ > 1) {
+            ws_.cand.reset(static_cast<size_t>(4) * tp_size_ * 2);  // [own 4][gathered TP x 4]
+            ws_.logits_all.reset(g.vocab);
+        }
+        const int tsf = softcap_topk_scratch_floats(vocab_local_);
         ws_.topk_scratch.reset(tsf);
         ws_.topk_idx.reset(8);
         ws_.topk_val.reset(8);
         HYB_CUDA(cudaMallocHost(&ws_.h_topk_idx, 8 * sizeof(uint32_t)));
         HYB_CUDA(cudaMallocHost(&ws_.h_topk_val, 8 * sizeof(float)));
+        HYB_CUDA(cudaMallocHost(&ws_.h_cand, static_cast<size_t>(4) * tp_size_ * sizeof(uint32_t)));
     }
     size_t need = 0;
     for (const auto& L : layers_)
-        need = std::max(need, decode_attn_scratch_bytes(static_cast<int>(g.n_heads), L.nkv, L.hd,
+        need = std::max(need, decode_attn_scratch_bytes(heads_local_, L.nkv, L.hd,
                                                         static_cast<int>(std::max<uint32_t>(max_keys, 1))));
     if (need > ws_.attn_scratch_bytes) {
         // grow geometrically so decode does not reallocate every 256 tokens
@@ -487,8 +572,8 @@ void Model::ensure_workspace(int tokens, uint32_t max_keys) {
 
 void Model::forward_chunk(KvState& kv, int L, uint32_t offset) {
     const Geometry& g = geo_;
-    const int H = static_cast<int>(g.hidden), I = static_cast<int>(g.intermediate);
-    const int nh = static_cast<int>(g.n_heads);
+    const int H = static_cast<int>(g.hidden), I = inter_local_;
+    const int nh = heads_local_;
     cudaStream_t st = stream_;
     bf16* h_cur = ws_.h_a.p;
     bf16* h_alt = ws_.h_b.p;
@@ -568,6 +653,7 @@ void Model::forward_chunk(KvState& kv, int L, uint32_t offset) {
         }
         launch_prefill_attn(ap, st);
         launch_quantized_matmul(ws_.attn.p, W.o.w.p, W.o.s.p, W.o.b.p, ws_.o.p, L, W.o.K, H, st);
+        tp_.all_reduce_sum_bf16(ws_.o.p, static_cast<size_t>(L) * H, st);  // row-parallel o_proj
         launch_resid_norm(ws_.o.p, W.post_attn.p, h_cur, nullptr, h_alt, W.pre_ff.p, ws_.xn.p, L, H, g.eps, st);
         launch_quantized_matmul(ws_.xn.p, W.gateup.w.p, W.gateup.s.p, W.gateup.b.p, ws_.gu.p, L, H, 2 * I, st);
         {
@@ -576,6 +662,7 @@ void Model::forward_chunk(KvState& kv, int L, uint32_t offset) {
             HYB_LAUNCH_CHECK("geglu_interleaved_kernel");
         }
         launch_quantized_matmul(ws_.act.p, W.down.w.p, W.down.s.p, W.down.b.p, ws_.dn.p, L, I, H, st);
+        tp_.all_reduce_sum_bf16(ws_.dn.p, static_cast<size_t>(L) * H, st);  // row-parallel down_proj
         const bf16* next_w = (layer + 1 < g.n_layers) ? layers_[layer + 1].in_ln.p : final_norm_.p;
         launch_resid_norm(ws_.dn.p, W.post_ff.p, h_alt, W.scalar.p, h_cur, next_w, ws_.xn.p, L, H, g.eps, st);
     }
@@ -584,14 +671,15 @@ void Model::forward_chunk(KvState& kv, int L, uint32_t offset) {
 StepOut Model::epilogue(const bf16* final_row, bool fused_prologue, const bf16* dn, const bf16* resid,
                         std::vector<uint16_t>* logits_out) {
     const Geometry& g = geo_;
-    QmvParams p;
-    p.w = embed_.w.p;
-    p.packed = embed_.packed.p;
-    p.s = embed_.s.p;
-    p.b = embed_.b.p;
+    const int H = static_cast<int>(g.hidden);
+    QmvParams p;  // lm_head over this rank's vocabulary rows (all of them when TP = 1)
+    p.w = embed_.w.p + static_cast<size_t>(vocab0_) * (H / 8);
+    p.packed = lm_packed_.p;
+    p.s = embed_.s.p + static_cast<size_t>(vocab0_) * (H / 64);
+    p.b = embed_.b.p + static_cast<size_t>(vocab0_) * (H / 64);
     p.y = ws_.logits.p;
-    p.K = static_cast<int>(g.hidden);
-    p.N = static_cast<int>(g.vocab);
+    p.K = H;
+    p.N = vocab_local_;
     p.eps = g.eps;
     if (fused_prologue) {
         const LayerW& last = layers_.back();
@@ -606,26 +694,61 @@ StepOut Model::epilogue(const bf16* final_row, bool fused_prologue, const bf16* 
         p.x = final_row;
     }
     launch_qmv(p, stream_, fused_prologue);
-    launch_softcap_topk(ws_.logits.p, static_cast<int>(g.vocab), g.softcap, ws_.topk_scratch.p,
+    launch_softcap_topk(ws_.logits.p, vocab_local_, g.softcap, ws_.topk_scratch.p,
                         static_cast<int>(ws_.topk_scratch.n), ws_.topk_idx.p, ws_.topk_val.p, stream_);
-    HYB_CUDA(cudaMemcpyAsync(ws_.h_topk_idx, ws_.topk_idx.p, 8 * sizeof(uint32_t), cudaMemcpyDeviceToHost, stream_));
-    HYB_CUDA(cudaMemcpyAsync(ws_.h_topk_val, ws_.topk_val.p, 8 * sizeof(float), cudaMemcpyDeviceToHost, stream_));
-    if (logits_out) {
-        logits_out->resize(g.vocab);
-        HYB_CUDA(cudaMemcpyAsync(logits_out->data(), ws_.logits.p, static_cast<size_t>(g.vocab) * 2,
-                                 cudaMemcpyDeviceToHost, stream_));
+    const int T = tp_size_;
+    if (T > 1) {
+        // every rank's (winner, runner-up) with global vocabulary indices, all-gathered
+        tp_candidates_kernel<<<1, 32, 0, stream_>>>(ws_.topk_idx.p, ws_.topk_val.p, static_cast<uint32_t>(vocab0_),
+                                                   ws_.cand.p);
+        HYB_LAUNCH_CHECK("tp_candidates_kernel");
+        tp_.all_gather_bytes(ws_.cand.p, ws_.cand.p + 4, 16, stream_);
+        HYB_CUDA(cudaMemcpyAsync(ws_.h_cand, ws_.cand.p + 4, static_cast<size_t>(T) * 16, cudaMemcpyDeviceToHost,
+                                 stream_));
+        if (logits_out) {
+            tp_.all_gather_bytes(ws_.logits.p, ws_.logits_all.p, static_cast<size_t>(vocab_local_) * 2, stream_);
+            logits_out->resize(g.vocab);
+            HYB_CUDA(cudaMemcpyAsync(logits_out->data(), ws_.logits_all.p, static_cast<size_t>(g.vocab) * 2,
+                                     cudaMemcpyDeviceToHost, stream_));
+        }
+    } else {
+        HYB_CUDA(cudaMemcpyAsync(ws_.h_topk_idx, ws_.topk_idx.p, 8 * sizeof(uint32_t), cudaMemcpyDeviceToHost, stream_));
+        HYB_CUDA(cudaMemcpyAsync(ws_.h_topk_val, ws_.topk_val.p, 8 * sizeof(float), cudaMemcpyDeviceToHost, stream_));
+        if (logits_out) {
+            logits_out->resize(g.vocab);
+            HYB_CUDA(cudaMemcpyAsync(logits_out->data(), ws_.logits.p, static_cast<size_t>(g.vocab) * 2,
+                                     cudaMemcpyDeviceToHost, stream_));
+        }
     }
     HYB_CUDA(cudaStreamSynchronize(stream_));
     StepOut out;
-    const int n = static_cast<int>(std::min<uint32_t>(2, g.vocab));  // device top-2: winner + runner-up
-    for (int i = 0; i < n; ++i) {
-        out.topk_idx[i] = ws_.h_topk_idx[i];
-        out.topk_val[i] = ws_.h_topk_val[i];
+    if (T > 1) {
+        // merge: highest value first, lowest vocabulary index on ties (the TP = 1 order)
+        std::vector<std::pair<float, uint32_t>> c;
+        for (int r = 0; r < T; ++r)
+            for (int k = 0; k < 2; ++k) {
+                float v;
+                std::memcpy(&v, &ws_.h_cand[4 * r + 2 * k + 1], 4);
+                c.emplace_back(v, ws_.h_cand[4 * r + 2 * k]);
+            }
+        std::sort(c.begin(), c.end(), [](const auto& x, const auto& y) {
+            return x.first > y.first || (x.first == y.first && x.second < y.second);
+        });
+        for (int i = 0; i < 2; ++i) {
+            out.topk_idx[i] = c[i].second;
+            out.topk_val[i] = c[i].first;
+        }
+    } else {
+        const int n = static_cast<int>(std::min<uint32_t>(2, g.vocab));  // device top-2: winner + runner-up
+        for (int i = 0; i < n; ++i) {
+            out.topk_idx[i] = ws_.h_topk_idx[i];
+            out.topk_val[i] = ws_.h_topk_val[i];
+        }
+        if (n < 2) out.topk_val[1] = -INFINITY;
     }
     out.token = out.topk_idx[0];
     out.logit = out.topk_val[0];
-    const float top2 = n > 1 ? out.topk_val[1] : -INFINITY;
-    out.near_tie = (out.logit - top2) < 0.5f;
+    out.near_tie = (out.logit - out.topk_val[1]) < 0.5f;
     return out;
 }
 
@@ -657,7 +780,7 @@ StepOut Model::prefill(KvState& kv, const uint32_t* tokens, uint32_t count, std:
 void Model::decode_layers(KvState& kv) {
     const Geometry& g = geo_;
     const int H = static_cast<int>(g.hidden);
-    const int nh = static_cast<int>(g.n_heads);
+    const int nh = heads_local_;
     cudaStream_t st = stream_;
     const uint32_t pos = kv.offset;  // position of the token being decoded
     launch_embed(ws_.ids.p, 1, embed_.w.p, embed_.s.p, embed_.b.p, H, embed_scale_, ws_.h_e.p, st);
@@ -775,6 +898,7 @@ void Model::decode_layers(KvState& kv) {
         po.K = W.o.K;
         po.N = H;
         launch_qmv(po, st, true);
+        tp_.all_reduce_sum_bf16(ws_.o.p, static_cast<size_t>(H), st);  // row-parallel o_proj
         // gate/up with the post-attention residual + pre-MLP norm in the prologue
         // and GeGLU in the epilogue
         QmvParams pg;
@@ -805,6 +929,7 @@ void Model::decode_layers(KvState& kv) {
         pd.K = W.down.K;
         pd.N = H;
         launch_qmv(pd, st, true);
+        tp_.all_reduce_sum_bf16(ws_.dn.p, static_cast<size_t>(H), st);  // row-parallel down_proj
     }
 }
 

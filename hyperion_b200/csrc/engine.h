@@ -9,12 +9,19 @@
 //     halves of GeGLU and applies it in its epilogue;
 //   * norms ride in the prologue of the next projection in decode;
 //   * local KV rings are [window + 8, nkv, hd] bf16 (slot = pos % cap) and global
-//     caches grow in 256-token steps, as in the reference.
+//     caches grow in 256-token steps, as in the reference;
+//   * with tensor parallelism over TP GPUs (one process per GPU), each rank holds
+//     the rows of its query/KV heads and its 1/TP of the MLP for the column-parallel
+//     q/k/v and gate/up, the matching K ranges of the row-parallel o and down
+//     projections (whose partial outputs are summed by an NCCL all-reduce), its KV
+//     heads' caches, and 1/TP of the vocabulary for the lm_head (the greedy
+//     candidates are all-gathered). Norms and the embedding table are replicated.
 #pragma once
 
 #include "common.cuh"
 #include "geometry.h"
 #include "kernels.h"
+#include "tp.h"
 
 #include <cstdint>
 #include <memory>
@@ -106,10 +113,13 @@ struct Workspace {
     DevPtr<float> topk_scratch;
     DevPtr<uint32_t> topk_idx;
     DevPtr<float> topk_val;
+    DevPtr<uint32_t> cand;          // tensor parallel: [TP][4] gathered (idx0, val0, idx1, val1)
+    DevPtr<bf16> logits_all;        // tensor parallel: the gathered full vocabulary (debug paths)
     DevPtr<unsigned char> attn_scratch;
     size_t attn_scratch_bytes = 0;
     uint32_t* h_topk_idx = nullptr;  // pinned host mirrors
     float* h_topk_val = nullptr;
+    uint32_t* h_cand = nullptr;      // tensor parallel: gathered candidates
     uint32_t* h_ids = nullptr;
     int h_ids_cap = 0;
 };
@@ -121,8 +131,14 @@ class Model {
 
     // Load from a directory of *.safetensors (mlx-lm converted names).
     void load_dir(const Geometry& g, const std::string& dir);
-    // Fill every tensor with seeded synthetic values on the device (benchmarks).
+    // Fill every tensor with seeded synthetic values on the device (benchmarks). With
+    // tensor parallelism each rank generates exactly its shard of the TP = 1 model.
     void load_synthetic(const Geometry& g, uint64_t seed);
+    // Tensor parallelism: call before loading; `id` is the 128-byte NCCL unique id
+    // rank 0 created (TpComm::unique_id). The communicator is set up by the load.
+    void set_tensor_parallel(int rank, int size, const void* id);
+    int tp_rank() const { return tp_rank_; }
+    int tp_size() const { return tp_size_; }
 
     std::unique_ptr<KvState> new_kv() const;
     // Grow global caches so that `n_tokens` more tokens fit (reference
@@ -172,6 +188,15 @@ class Model {
     bf16 embed_scale_{};
     int attn_rounding_ = 0;
     Workspace ws_;
+    // tensor parallelism (tp_size_ == 1: everything local)
+    TpComm tp_;
+    int tp_rank_ = 0, tp_size_ = 1;
+    unsigned char tp_id_[128] = {};
+    int heads_local_ = 0;   // query heads on this rank
+    int inter_local_ = 0;   // MLP intermediate rows on this rank
+    int vocab_local_ = 0;   // lm_head rows on this rank, starting at vocab0_
+    int vocab0_ = 0;
+    DevPtr<unsigned char> lm_packed_;  // packed lm_head rows of this rank
 };
 
 }  // namespace hyb

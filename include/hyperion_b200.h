@@ -149,6 +149,21 @@ HypStatus hyb_sdpa_decode_fused(const void* qkv, int32_t v_from_k, const void* q
                                 void* stream);
 
 /*
+ * Tensor parallelism over TP GPUs of one node, one process per GPU (no reference
+ * counterpart: the reference engine is single-device). Rank 0 creates a 128-byte NCCL
+ * unique id and shares it with the other ranks by any host channel; every rank then
+ * calls hyb_model_set_tensor_parallel on a created, not yet loaded model and loads it
+ * (hyb_model_load_synthetic) at the same time, on its own current device. Each rank holds
+ * its query/KV heads, 1/TP of the MLP and 1/TP of the vocabulary; o_proj and down_proj
+ * partial sums are combined with an NCCL all-reduce, the greedy candidates with an
+ * all-gather, and every rank returns the same tokens. Heads, KV heads, MLP rows (in
+ * 16-row tiles and 64-wide groups) and the vocabulary must split evenly.
+ */
+HypStatus hyb_nccl_unique_id(void* out128);
+HypStatus hyb_model_set_tensor_parallel(HypModel model, int32_t rank, int32_t size,
+                                        const void* unique_id);
+
+/*
  * Count of bounded shared-memory waits (mbarrier, bulk-copy completion) that gave
  * up on the current device since the library was loaded, summed over the
  * streaming qmv, the fused decode attention and the tensor-core prefill qmm. A wait that gives up leaves that
