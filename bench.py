@@ -670,13 +670,81 @@ def run_attn_decode(args, rank, world, local):
                       "clocks": clk.summary()}), flush=True)
 
 
+# ------------------------------------------------------------------ 27B-shaped tensor-parallel decode (config 4)
+def run_tp_decode(args, rank, world, local):
+    """Config 4: the 27B-shaped decoder split over the job's GPUs (one rank per GPU,
+    column/row-parallel projections, NCCL all-reduce after o_proj and down_proj,
+    vocab-parallel lm_head), batch-1 greedy decode after a --ctx prefill."""
+    import torch
+    import hyperion_b200 as hb
+    from hyperion_b200.synth import config4
+    geo = config4()
+    why = hb.tp_shard_check(geo, world)
+    if why:
+        raise SystemExit(f"config 4 does not split over {world} ranks: {why}")
+    tp = None
+    if world > 1:
+        import torch.distributed as dist
+        obj = [hb.nccl_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(obj, src=0)
+        tp = (rank, world, obj[0])
+    eng = hb.Engine(geo, synthetic_seed=1, tp=tp)
+    ctx = args.ctx
+    prompt = [int(t) for t in torch.randint(0, geo.vocab_size, (ctx,), generator=torch.Generator().manual_seed(5))]
+    kv = eng.new_kv()
+    barrier(world)
+    t0 = time.perf_counter()
+    kv.prefill(prompt)
+    prefill_s = max_over_ranks(time.perf_counter() - t0, world)
+    stream = torch.cuda.ExternalStream(eng.stream())
+    for _ in range(args.warmup):
+        kv.decode(1)
+    barrier(world)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        torch.cuda.synchronize()
+        w0 = time.perf_counter()
+        e0.record(stream)
+        for _ in range(args.steps):
+            kv.decode(1)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        wall_ms = (time.perf_counter() - w0) * 1e3 / args.steps
+    ms = max_over_ranks(e0.elapsed_time(e1) / args.steps, world)
+    wall_ms = max_over_ranks(wall_ms, world)
+    if rank != 0:
+        return
+    # weight bytes each rank streams per token: its shard of the projections + its lm_head rows
+    per_layer = (qmv_bytes(5376, 8192 + 2 * 4096) + qmv_bytes(4096, 5376) + qmv_bytes(5376, 2 * 21504) +
+                 qmv_bytes(21504, 5376)) / world
+    w_bytes = 62 * per_layer + qmv_bytes(5376, 262144) / world
+    hbm, _, src = peaks()
+    gbs = w_bytes / (ms * 1e-3) / 1e9
+    print(json.dumps({"metric": "27B-shaped tensor-parallel decode tok/s (cfg4, batch 1)",
+                      "value": round(1e3 / ms, 2), "unit": "tok/s", "n_gpus": world, "steps": args.steps,
+                      "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True,
+                      "scaling": "strong", "vs_baseline": None, "dtype": "u4/bf16->f32", "data": "synthetic",
+                      "config": {"workload": f"cfg4 27B-shaped decode, ctx {ctx}, batch 1",
+                                 "parallelism": f"tp{world}", "prefill_s": round(prefill_s, 3),
+                                 "l2": "inputs larger than L2"},
+                      "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": hbm, "unit": "GB/s",
+                                   "frac": round(gbs / hbm, 4), "traffic": None, "peak_source": src,
+                                   "kernel": "whole decode step per rank (weight bytes of its shard per token)"},
+                      "gpu_launches": (1 + 5 * 62 + 4) * args.steps,
+                      "e2e": {"value": round(1e3 / wall_ms, 2), "unit": "tok/s", "h2d_bytes_per_step": 4,
+                              "d2h_bytes_per_step": 64 * world,
+                              "path": "hyp_decode_block(n_tokens=1) on every rank, host wall clock"},
+                      "clocks": clk.summary()}), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="qmv", choices=["qmv", "decode", "qmv-shape", "attn-decode", "qmm"])
+    ap.add_argument("--workload", default="qmv",
+                    choices=["qmv", "decode", "qmv-shape", "attn-decode", "qmm", "tp-decode"])
     ap.add_argument("--qmm-m", default="512,2048,8192", help="token counts for --workload qmm")
     ap.add_argument("--shape", default="3840,262144", help="K,N for --workload qmv-shape")
     ap.add_argument("--layout", default="packed", choices=["packed", "mlx"], help="weights for qmv-shape")
@@ -696,6 +764,8 @@ def main():
     try:
         if args.workload == "qmv":
             run_qmv(args, rank, world, local)
+        elif args.workload == "tp-decode":
+            run_tp_decode(args, rank, world, local)
         elif args.workload == "qmm":
             run_qmm(args, rank, world, local)
         elif args.workload == "attn-decode":

@@ -290,7 +290,10 @@ void Model::pack_all() {
 
 void Model::load_synthetic(const Geometry& g, uint64_t seed) {
     init_common(g);
-    if (tp_size_ > 1) tp_.init(tp_rank_, tp_size_, tp_id_);
+    if (tp_size_ > 1) {
+        tp_.init(tp_rank_, tp_size_, tp_id_);
+        tp_.setup_p2p(g.hidden);  // decode's [hidden] all-reduces go peer to peer
+    }
     const int H = static_cast<int>(g.hidden), I = static_cast<int>(g.intermediate);
     const int r = tp_rank_, T = tp_size_;
     uint64_t tag = seed * 1000003ull;
@@ -721,6 +724,8 @@ StepOut Model::epilogue(const bf16* final_row, bool fused_prologue, const bf16* 
         }
     }
     HYB_CUDA(cudaStreamSynchronize(stream_));
+    if (T > 1 && tp_.take_wait_errors(stream_))
+        throw CudaError("tensor-parallel all-reduce: a wait for a peer's flag gave up");
     StepOut out;
     if (T > 1) {
         // merge: highest value first, lowest vocabulary index on ties (the TP = 1 order)
@@ -898,7 +903,7 @@ void Model::decode_layers(KvState& kv) {
         po.K = W.o.K;
         po.N = H;
         launch_qmv(po, st, true);
-        tp_.all_reduce_sum_bf16(ws_.o.p, static_cast<size_t>(H), st);  // row-parallel o_proj
+        tp_.all_reduce_small_bf16(ws_.o.p, static_cast<size_t>(H), st, true);  // row-parallel o_proj
         // gate/up with the post-attention residual + pre-MLP norm in the prologue
         // and GeGLU in the epilogue
         QmvParams pg;
@@ -929,7 +934,7 @@ void Model::decode_layers(KvState& kv) {
         pd.K = W.down.K;
         pd.N = H;
         launch_qmv(pd, st, true);
-        tp_.all_reduce_sum_bf16(ws_.dn.p, static_cast<size_t>(H), st);  // row-parallel down_proj
+        tp_.all_reduce_small_bf16(ws_.dn.p, static_cast<size_t>(H), st, true);  // row-parallel down_proj
     }
 }
 

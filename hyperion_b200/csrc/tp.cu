@@ -6,6 +6,7 @@
 
 #include <mutex>
 #include <string>
+#include <vector>
 
 namespace hyb {
 
@@ -51,8 +52,157 @@ void nccl_check(ncclResult_t r, const char* what) {
 
 }  // namespace
 
+namespace {
+
+struct PeerTable {
+    unsigned char* base[8];  // every rank's buffer, own one included (mapped into this process)
+};
+
+constexpr int kArThreads = 512;
+
+__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
+    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
+    uint32_t v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+__device__ __forceinline__ uint4 ld_cg(const uint4* p) {
+    uint4 v;
+    asm volatile("ld.global.cg.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "l"(p));
+    return v;
+}
+
+// Layout of a rank's buffer: data[set][src][max] bf16, then flags[src] u32, then err u32.
+__global__ void __launch_bounds__(kArThreads) oneshot_allreduce_kernel(bf16* buf, int n, PeerTable peers, int me,
+                                                                       int T, size_t max_count, uint32_t epoch) {
+    pdl_wait();
+    const size_t set_bytes = static_cast<size_t>(T) * max_count * 2;
+    const size_t slot = (epoch & 1u) * set_bytes + static_cast<size_t>(me) * max_count * 2;
+    const int nv = n / 8;  // 16-byte vectors (n is a multiple of 8)
+    const uint4* src = reinterpret_cast<const uint4*>(buf);
+    // 1. my partial into slot `me` of every rank's current set (my own buffer included)
+    for (int i = threadIdx.x; i < nv; i += blockDim.x) {
+        const uint4 v = src[i];
+        for (int r = 0; r < T; ++r) reinterpret_cast<uint4*>(peers.base[r] + slot)[i] = v;
+    }
+    __threadfence_system();
+    __syncthreads();
+    // 2. raise my flag on every rank (release at system scope orders the stores above)
+    if (threadIdx.x < T) {
+        uint32_t* flags = reinterpret_cast<uint32_t*>(peers.base[threadIdx.x] + 2 * set_bytes);
+        st_release_sys(flags + me, epoch);
+    }
+    // 3. wait for every rank's flag of this epoch (bounded)
+    __shared__ int gave_up;
+    if (threadIdx.x == 0) gave_up = 0;
+    __syncthreads();
+    if (threadIdx.x < T) {
+        const uint32_t* flags = reinterpret_cast<const uint32_t*>(peers.base[me] + 2 * set_bytes);
+        bool ok = false;
+        for (int it = 0; it < (1 << 24); ++it) {
+            if (static_cast<int32_t>(ld_acquire_sys(flags + threadIdx.x) - epoch) >= 0) {
+                ok = true;
+                break;
+            }
+            if (it > 64) __nanosleep(64);
+        }
+        if (!ok) gave_up = 1;
+    }
+    __syncthreads();
+    if (gave_up && threadIdx.x == 0) atomicAdd(reinterpret_cast<int*>(peers.base[me] + 2 * set_bytes + 4 * T), 1);
+    // 4. sum the T partials in rank order (the same bits on every rank)
+    const unsigned char* mine = peers.base[me] + (epoch & 1u) * set_bytes;
+    for (int i = threadIdx.x; i < nv; i += blockDim.x) {
+        float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+        for (int r = 0; r < T; ++r) {
+            const uint4 v = ld_cg(reinterpret_cast<const uint4*>(mine + static_cast<size_t>(r) * max_count * 2) + i);
+            const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                acc[2 * k] += __uint_as_float(w[k] << 16);
+                acc[2 * k + 1] += __uint_as_float(w[k] & 0xFFFF0000u);
+            }
+        }
+        uint4 o;
+        o.x = pack_bf2(f2bf(acc[0]), f2bf(acc[1]));
+        o.y = pack_bf2(f2bf(acc[2]), f2bf(acc[3]));
+        o.z = pack_bf2(f2bf(acc[4]), f2bf(acc[5]));
+        o.w = pack_bf2(f2bf(acc[6]), f2bf(acc[7]));
+        reinterpret_cast<uint4*>(buf)[i] = o;
+    }
+    pdl_launch_dependents();
+}
+
+}  // namespace
+
 TpComm::~TpComm() {
+    for (int r = 0; r < 8; ++r)
+        if (p2p_peer_[r] && r != rank_) cudaIpcCloseMemHandle(p2p_peer_[r]);
+    if (p2p_local_) cudaFree(p2p_local_);
     if (comm_) nccl().comm_destroy(comm_);
+}
+
+void TpComm::setup_p2p(size_t max_count) {
+    if (!active() || size_ > 8) return;
+    max_count = (max_count + 7) / 8 * 8;
+    const size_t bytes = 2 * static_cast<size_t>(size_) * max_count * 2 + 4 * static_cast<size_t>(size_) + 64;
+    HYB_CUDA(cudaMalloc(&p2p_local_, bytes));
+    HYB_CUDA(cudaMemset(p2p_local_, 0, bytes));
+    cudaIpcMemHandle_t mine;
+    HYB_CUDA(cudaIpcGetMemHandle(&mine, p2p_local_));
+    void* dev_handles = nullptr;
+    HYB_CUDA(cudaMalloc(&dev_handles, sizeof(cudaIpcMemHandle_t) * (size_ + 1)));
+    HYB_CUDA(cudaMemcpy(dev_handles, &mine, sizeof(mine), cudaMemcpyHostToDevice));
+    all_gather_bytes(dev_handles, static_cast<char*>(dev_handles) + sizeof(mine), sizeof(mine), nullptr);
+    HYB_CUDA(cudaStreamSynchronize(nullptr));
+    std::vector<cudaIpcMemHandle_t> all(size_);
+    HYB_CUDA(cudaMemcpy(all.data(), static_cast<char*>(dev_handles) + sizeof(mine), sizeof(mine) * size_,
+                        cudaMemcpyDeviceToHost));
+    cudaFree(dev_handles);
+    for (int r = 0; r < size_; ++r) {
+        if (r == rank_) {
+            p2p_peer_[r] = p2p_local_;
+        } else {
+            HYB_CUDA(cudaIpcOpenMemHandle(&p2p_peer_[r], all[r], cudaIpcMemLazyEnablePeerAccess));
+        }
+    }
+    p2p_max_ = max_count;
+    epoch_ = 0;
+}
+
+void TpComm::all_reduce_small_bf16(bf16* buf, size_t count, cudaStream_t stream, bool pdl) {
+    if (!active()) return;
+    if (!p2p_local_ || count > p2p_max_ || count % 8 != 0 || (reinterpret_cast<uintptr_t>(buf) & 15)) {
+        all_reduce_sum_bf16(buf, count, stream);
+        return;
+    }
+    PeerTable t{};
+    for (int r = 0; r < size_; ++r) t.base[r] = static_cast<unsigned char*>(p2p_peer_[r]);
+    ++epoch_;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(1);
+    cfg.blockDim = dim3(kArThreads);
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    HYB_CUDA(cudaLaunchKernelEx(&cfg, oneshot_allreduce_kernel, buf, static_cast<int>(count), t, rank_, size_, p2p_max_,
+                                epoch_));
+}
+
+int TpComm::take_wait_errors(cudaStream_t stream) {
+    if (!p2p_local_) return 0;
+    int* err = reinterpret_cast<int*>(static_cast<unsigned char*>(p2p_local_) + 2 * static_cast<size_t>(size_) * p2p_max_ * 2 +
+                                      4 * static_cast<size_t>(size_));
+    int h = 0;
+    HYB_CUDA(cudaMemcpyAsync(&h, err, sizeof(int), cudaMemcpyDeviceToHost, stream));
+    HYB_CUDA(cudaStreamSynchronize(stream));
+    if (h) HYB_CUDA(cudaMemsetAsync(err, 0, sizeof(int), stream));
+    return h;
 }
 
 void TpComm::unique_id(void* out) {

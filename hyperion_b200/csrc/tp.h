@@ -27,14 +27,30 @@ class TpComm {
     int rank() const { return rank_; }
     int size() const { return size_; }
 
-    // In-place bf16 sum over the ranks on `stream`.
+    // In-place bf16 sum over the ranks on `stream` (NCCL).
     void all_reduce_sum_bf16(bf16* buf, size_t count, cudaStream_t stream);
+
+    // One-shot all-reduce for small decode messages over NVLink peer memory: each rank
+    // stores its partial into every peer's receive buffer (IPC-mapped, plain stores),
+    // raises a release flag, waits (bounded) for all flags and sums in rank order, so
+    // every rank gets the same bits. setup_p2p is collective; messages above the set-up
+    // size (or without peer access) go through NCCL.
+    void setup_p2p(size_t max_count);
+    void all_reduce_small_bf16(bf16* buf, size_t count, cudaStream_t stream, bool pdl);
+    // Number of flag waits that gave up since the last call (then resets it); a wait that
+    // gives up leaves that step's result undefined but never hangs the GPU.
+    int take_wait_errors(cudaStream_t stream);
     // Rank r's `bytes` land at recv + r * bytes on every rank.
     void all_gather_bytes(const void* send, void* recv, size_t bytes, cudaStream_t stream);
 
   private:
     ncclComm_t comm_ = nullptr;
     int rank_ = 0, size_ = 1;
+    // one-shot all-reduce: local buffer = [2 sets][size][max] bf16 + [size] u32 flags + u32 error
+    void* p2p_local_ = nullptr;
+    void* p2p_peer_[8] = {};
+    size_t p2p_max_ = 0;
+    uint32_t epoch_ = 0;
 };
 
 }  // namespace hyb
