@@ -498,6 +498,49 @@ def run_qmm(args, rank, world, local):
                       "per_m": rows, "gpu_launches": 4 * len(Ms) * args.steps, "clocks": clk.summary()}), flush=True)
 
 
+# ------------------------------------------------------------------ prefill causal SDPA (config 2)
+def run_sdpa_prefill(args, rank, world, local):
+    """Config 2's attention: causal SDPA at M tokens over 16 query / 8 KV heads, head_dim
+    256, on a local layer (window 1024) and a global layer (full context), one M-token
+    chunk at position 0 through hyb_sdpa_prefill. value = useful TFLOP/s (4 H hd per
+    visible query-key pair: QK^T and PV)."""
+    import torch
+    from hyperion_b200 import ops
+    H, Hkv, hd = 16, 8, 256
+    rows = []
+    flop_tot = us_tot = 0.0
+    g = torch.Generator(device="cuda").manual_seed(3)
+    for M in [int(m) for m in args.qmm_m.split(",")]:
+        q = torch.randn((M, H, hd), generator=g, device="cuda").to(torch.bfloat16)
+        k = torch.randn((M, Hkv, hd), generator=g, device="cuda").to(torch.bfloat16)
+        v = torch.randn((M, Hkv, hd), generator=g, device="cuda").to(torch.bfloat16)
+        for window in (1024, 0):
+            vis = sum(min(i + 1, window) if window else i + 1 for i in range(M))
+            flops = 4.0 * H * hd * vis
+            ops.sdpa_prefill(q, k, v, 0, 0, window)
+            torch.cuda.synchronize()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            for _ in range(args.steps):
+                ops.sdpa_prefill(q, k, v, 0, 0, window)
+            e1.record()
+            torch.cuda.synchronize()
+            us = e0.elapsed_time(e1) * 1e3 / args.steps
+            rows.append({"M": M, "window": window, "us": round(us, 1), "TFLOP/s": round(flops / (us * 1e-6) / 1e12, 1)})
+            flop_tot += flops
+            us_tot += us
+    _, tf_peak, src = peaks()
+    value = flop_tot / (us_tot * 1e-6) / 1e12
+    print(json.dumps({"metric": "prefill causal SDPA TFLOP/s (cfg2: 16/8 heads, hd 256, window 1024 and global)",
+                      "value": round(value, 1), "unit": "TFLOP/s", "n_gpus": 1, "steps": args.steps,
+                      "higher_is_better": True, "dtype": "bf16, f32 acc", "data": "synthetic",
+                      "config": {"workload": f"cfg2 causal SDPA at M = {args.qmm_m}"},
+                      "roofline": {"bound": "tensor", "achieved": round(value, 1), "peak": tf_peak, "unit": "TFLOP/s",
+                                   "frac": round(value / tf_peak, 4), "traffic": None, "peak_source": src,
+                                   "kernel": "prefill_attn_kernel"},
+                      "per_case": rows}), flush=True)
+
+
 # ------------------------------------------------------------------ single qmv shape (profiling)
 def run_qmv_shape(args, rank, world, local):
     """One cfg-1 shape over enough distinct copies to exceed 2x L2 (the workload the
@@ -744,13 +787,14 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--workload", default="qmv",
-                    choices=["qmv", "decode", "qmv-shape", "attn-decode", "qmm", "tp-decode"])
+                    choices=["qmv", "decode", "qmv-shape", "attn-decode", "qmm", "tp-decode", "sdpa-prefill"])
     ap.add_argument("--qmm-m", default="512,2048,8192", help="token counts for --workload qmm")
     ap.add_argument("--shape", default="3840,262144", help="K,N for --workload qmv-shape")
     ap.add_argument("--layout", default="packed", choices=["packed", "mlx"], help="weights for qmv-shape")
     ap.add_argument("--ctx", type=int, default=4096)
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
@@ -766,6 +810,8 @@ def main():
             run_qmv(args, rank, world, local)
         elif args.workload == "tp-decode":
             run_tp_decode(args, rank, world, local)
+        elif args.workload == "sdpa-prefill":
+            run_sdpa_prefill(args, rank, world, local)
         elif args.workload == "qmm":
             run_qmm(args, rank, world, local)
         elif args.workload == "attn-decode":

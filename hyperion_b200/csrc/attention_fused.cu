@@ -268,7 +268,8 @@ __global__ void __launch_bounds__(kThreads) decode_attn_fused_kernel(const Decod
         mbar_expect_tx(fb, TILE);
 #pragma unroll
         for (int sub = 0; sub < SUB; ++sub)
-            tma_load_3d(tiles_u32 + s * TILE + sub * (T * 128), isv ? &tmv : &tmk, 64 * sub, hk, tk.z, fb);
+            tma_load_3d_hint(tiles_u32 + s * TILE + sub * (T * 128), isv ? &tmv : &tmk, 64 * sub, hk, tk.z, fb,
+                             l2_evict_first());
     };
     if (threadIdx.x == 0)
         for (int it = 0; it < stages && it < items; ++it) issue(it);

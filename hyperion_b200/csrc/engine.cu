@@ -789,13 +789,10 @@ void Model::decode_layers(KvState& kv) {
     cudaStream_t st = stream_;
     const uint32_t pos = kv.offset;  // position of the token being decoded
     launch_embed(ws_.ids.p, 1, embed_.w.p, embed_.s.p, embed_.b.p, H, embed_scale_, ws_.h_e.p, st);
-    const bf16* resid = ws_.h_e.p;  // residual entering the current layer's attention block
-    size_t li = 0, gi = 0;
-    for (uint32_t layer = 0; layer < g.n_layers; ++layer) {
-        LayerW& W = layers_[layer];
-        const int qkv_rows = W.q_rows + W.k_rows + W.v_rows;
-        // qkv projection with the layer's input norm (and the previous layer's
-        // post-MLP residual/scalar) fused into its prologue
+    // qkv projection of `layer` with its input norm (and the previous layer's
+    // post-MLP residual/scalar) fused into its prologue
+    auto qkv_params = [&](uint32_t layer) {
+        const LayerW& W = layers_[layer];
         QmvParams p;
         p.w = W.qkv.w.p;
         p.packed = W.qkv.packed.p;
@@ -803,7 +800,7 @@ void Model::decode_layers(KvState& kv) {
         p.b = W.qkv.b.p;
         p.y = ws_.qkv.p;
         p.K = H;
-        p.N = qkv_rows;
+        p.N = W.q_rows + W.k_rows + W.v_rows;
         p.eps = g.eps;
         p.norm_w = W.in_ln.p;
         if (layer == 0) {
@@ -817,9 +814,16 @@ void Model::decode_layers(KvState& kv) {
             p.post_w = P.post_ff.p;
             p.scalar = P.scalar.p;
             p.h_out = ws_.h_a.p;
-            resid = ws_.h_a.p;
         }
-        launch_qmv(p, st, true);
+        return p;
+    };
+    size_t li = 0, gi = 0;
+    for (uint32_t layer = 0; layer < g.n_layers; ++layer) {
+        LayerW& W = layers_[layer];
+        const int qkv_rows = W.q_rows + W.k_rows + W.v_rows;
+        // residual entering this layer's attention block
+        const bf16* resid = layer == 0 ? ws_.h_e.p : ws_.h_a.p;
+        launch_qmv(qkv_params(layer), st, true);
         // QK-norm + RoPE + cache append + attention in one cluster kernel
         DecodeFusedParams ap;
         ap.qkv = ws_.qkv.p;
@@ -902,8 +906,6 @@ void Model::decode_layers(KvState& kv) {
         po.y = ws_.o.p;
         po.K = W.o.K;
         po.N = H;
-        launch_qmv(po, st, true);
-        tp_.all_reduce_small_bf16(ws_.o.p, static_cast<size_t>(H), st, true);  // row-parallel o_proj
         // gate/up with the post-attention residual + pre-MLP norm in the prologue
         // and GeGLU in the epilogue
         QmvParams pg;
@@ -923,7 +925,6 @@ void Model::decode_layers(KvState& kv) {
         pg.norm_w = W.pre_ff.p;
         pg.h_out = ws_.h_b.p;
         pg.eps = g.eps;
-        launch_qmv(pg, st, true);
         QmvParams pd;
         pd.w = W.down.w.p;
         pd.packed = W.down.packed.p;
@@ -933,6 +934,9 @@ void Model::decode_layers(KvState& kv) {
         pd.y = ws_.dn.p;
         pd.K = W.down.K;
         pd.N = H;
+        launch_qmv(po, st, true);
+        tp_.all_reduce_small_bf16(ws_.o.p, static_cast<size_t>(H), st, true);  // row-parallel o_proj
+        launch_qmv(pg, st, true);
         launch_qmv(pd, st, true);
         tp_.all_reduce_small_bf16(ws_.dn.p, static_cast<size_t>(H), st, true);  // row-parallel down_proj
     }

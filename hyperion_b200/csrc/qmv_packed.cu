@@ -91,6 +91,196 @@ __device__ __forceinline__ float gelu_tanh_bf16ops(float x) {
     return rbf(hx * op);
 }
 
+// The input vector into shared memory: x (or its norm prologue) as the permuted
+// bf16 pairs the MMA B fragments read, and the per-group sums of x.
+__device__ __forceinline__ void stage_input(const QmvParams& p, uint32_t* xp, float* xsum, float* tmp) {
+    auto ld = [](const uint4* a) { return *a; };
+    const int K = p.K;
+    if (p.prologue == QmvPrologue::kNone) {
+        // One cooperative round trip: 16-byte chunk j of x holds x[8j .. 8j+7], which is
+        // exactly the four permuted pairs xp[4j .. 4j+3] = (x[8j+p], x[8j+p+4]), p < 4.
+        // The 8 chunks of a group sit in 8 consecutive lanes, which reduce its sum.
+        const uint4* xv = reinterpret_cast<const uint4*>(p.x);
+        for (int j0 = 0; j0 < K / 8; j0 += kThreads) {
+            const int j = j0 + static_cast<int>(threadIdx.x);
+            uint4 v = make_uint4(0, 0, 0, 0);
+            if (j < K / 8) v = ld(xv + j);
+            const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+            float part = 0.f;
+#pragma unroll
+            for (int q = 0; q < 4; ++q) part += __uint_as_float(w[q] << 16) + __uint_as_float(w[q] & 0xFFFF0000u);
+            if (j < K / 8) {
+                // pairs: p = 0: (w0.lo, w2.lo), p = 1: (w0.hi, w2.hi), p = 2: (w1.lo, w3.lo), p = 3: (w1.hi, w3.hi)
+                uint4 o;
+                o.x = (w[0] & 0xFFFFu) | (w[2] << 16);
+                o.y = (w[0] >> 16) | (w[2] & 0xFFFF0000u);
+                o.z = (w[1] & 0xFFFFu) | (w[3] << 16);
+                o.w = (w[1] >> 16) | (w[3] & 0xFFFF0000u);
+                *reinterpret_cast<uint4*>(xp + 4 * j) = o;
+            }
+            part += __shfl_xor_sync(0xffffffffu, part, 1);
+            part += __shfl_xor_sync(0xffffffffu, part, 2);
+            part += __shfl_xor_sync(0xffffffffu, part, 4);
+            if (j < K / 8 && (j & 7) == 0) xsum[j >> 3] = part;
+        }
+    } else {
+        // Norm prologues in one round trip: every thread loads its 16-byte chunks of
+        // x (and resid, post_w, norm_w) with independent vector loads into registers,
+        // then the reductions and the permuted-pair writes work from registers.
+        constexpr int kMaxC = kMaxPrologueK / 8 / kThreads;
+        const int nch = K / 8;
+        const uint4* x4 = reinterpret_cast<const uint4*>(p.x);
+        const uint4* n4 = reinterpret_cast<const uint4*>(p.norm_w);
+        const bool resid = p.prologue == QmvPrologue::kResidNorm;
+        const uint64_t keep = l2_evict_last();  // norm weights: re-read every token
+        uint4 xv[kMaxC], nv4[kMaxC], rv[kMaxC], pv[kMaxC];
+#pragma unroll
+        for (int c = 0; c < kMaxC; ++c) {
+            const int j = static_cast<int>(threadIdx.x) + c * kThreads;
+            const uint4 z = make_uint4(0, 0, 0, 0);
+            xv[c] = j < nch ? ld(x4 + j) : z;
+            nv4[c] = j < nch ? ld_v4_hint(n4 + j, keep) : z;
+            rv[c] = (resid && j < nch) ? ld(reinterpret_cast<const uint4*>(p.resid) + j) : z;
+            pv[c] = (resid && j < nch) ? ld_v4_hint(reinterpret_cast<const uint4*>(p.post_w) + j, keep) : z;
+        }
+        auto lo = [](uint32_t w) { return __uint_as_float(w << 16); };
+        auto hi = [](uint32_t w) { return __uint_as_float(w & 0xFFFF0000u); };
+        float ss = 0.f;
+#pragma unroll
+        for (int c = 0; c < kMaxC; ++c) {
+            const uint32_t w[4] = {xv[c].x, xv[c].y, xv[c].z, xv[c].w};
+#pragma unroll
+            for (int q = 0; q < 4; ++q) ss += lo(w[q]) * lo(w[q]) + hi(w[q]) * hi(w[q]);
+        }
+        float inv = 1.0f / sqrtf(block_sum(ss, tmp) / static_cast<float>(K) + p.eps);
+        if (resid) {
+            const float sc = p.scalar ? bf2f(p.scalar[0]) : 1.0f;
+            float ss2 = 0.f;
+#pragma unroll
+            for (int c = 0; c < kMaxC; ++c) {
+                uint32_t w[4] = {xv[c].x, xv[c].y, xv[c].z, xv[c].w};
+                const uint32_t r[4] = {rv[c].x, rv[c].y, rv[c].z, rv[c].w};
+                const uint32_t pw[4] = {pv[c].x, pv[c].y, pv[c].z, pv[c].w};
+#pragma unroll
+                for (int q = 0; q < 4; ++q) {
+                    float h0 = rbf(lo(r[q]) + rbf(rbf(lo(w[q]) * inv) * lo(pw[q])));
+                    float h1 = rbf(hi(r[q]) + rbf(rbf(hi(w[q]) * inv) * hi(pw[q])));
+                    if (p.scalar) {
+                        h0 = rbf(h0 * sc);
+                        h1 = rbf(h1 * sc);
+                    }
+                    ss2 += h0 * h0 + h1 * h1;
+                    w[q] = pack_bf2(f2bf(h0), f2bf(h1));
+                }
+                xv[c] = make_uint4(w[0], w[1], w[2], w[3]);
+                const int j = static_cast<int>(threadIdx.x) + c * kThreads;
+                if (blockIdx.x == 0 && p.h_out && j < nch) reinterpret_cast<uint4*>(p.h_out)[j] = xv[c];
+            }
+            inv = 1.0f / sqrtf(block_sum(ss2, tmp) / static_cast<float>(K) + p.eps);
+        }
+#pragma unroll
+        for (int c = 0; c < kMaxC; ++c) {
+            const int j = static_cast<int>(threadIdx.x) + c * kThreads;
+            const uint32_t w[4] = {xv[c].x, xv[c].y, xv[c].z, xv[c].w};
+            const uint32_t nw[4] = {nv4[c].x, nv4[c].y, nv4[c].z, nv4[c].w};
+            uint32_t o[4];
+            float part = 0.f;
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+                const float y0 = rbf(rbf(lo(w[q]) * inv) * lo(nw[q]));
+                const float y1 = rbf(rbf(hi(w[q]) * inv) * hi(nw[q]));
+                part += y0 + y1;
+                o[q] = pack_bf2(f2bf(y0), f2bf(y1));
+            }
+            if (j < nch) {
+                uint4 pr;  // permuted pairs (x[8j+p], x[8j+p+4])
+                pr.x = (o[0] & 0xFFFFu) | (o[2] << 16);
+                pr.y = (o[0] >> 16) | (o[2] & 0xFFFF0000u);
+                pr.z = (o[1] & 0xFFFFu) | (o[3] << 16);
+                pr.w = (o[1] >> 16) | (o[3] & 0xFFFF0000u);
+                *reinterpret_cast<uint4*>(xp + 4 * j) = pr;
+            }
+            part += __shfl_xor_sync(0xffffffffu, part, 1);
+            part += __shfl_xor_sync(0xffffffffu, part, 2);
+            part += __shfl_xor_sync(0xffffffffu, part, 4);
+            if (j < nch && (j & 7) == 0) xsum[j >> 3] = part;
+        }
+    }
+}
+
+// One 16-row x 512-code item from shared memory `st`: the lane's rows g and g + 8
+// accumulate into acc0 / acc1 (codes as bf16 128 + q times the permuted activation
+// pairs on the tensor cores, then the per-group scale and bias fold in fp32). Full
+// units (8 groups: every lane valid) skip the per-lane validity selects; only the
+// last unit of a row can be partial.
+template <bool FULL>
+__device__ __forceinline__ void qmv_item(const unsigned char* st, const uint32_t* xp, const uint32_t* zero_page,
+                                         const float* xsum, const PackGeo& pg, int unit, int g, int t, float& acc0,
+                                         float& acc1) {
+    const int tv = FULL ? 4 : (pg.gc_last + 1) / 2;
+    const int nv = 8 * tv;
+    const bool valid = FULL || t < tv;
+    const int rank = g * tv + t;
+    uint4 wv[8];
+#pragma unroll
+    for (int c = 0; c < 8; ++c)
+        wv[c] = valid ? *reinterpret_cast<const uint4*>(st + (c * nv + rank) * 16) : make_uint4(0, 0, 0, 0);
+    const uint4 sb =
+        valid ? *reinterpret_cast<const uint4*>(st + (8 * nv + rank) * 16) : make_uint4(0, 0, 0, 0);
+    const int gA = unit * 8 + 2 * t;
+    const uint32_t* src0 = (g == 2 * t && (FULL || gA < pg.G)) ? xp + gA * 32 : zero_page;
+    const uint32_t* src1 = (g == 2 * t + 1 && (FULL || gA + 1 < pg.G)) ? xp + (gA + 1) * 32 : zero_page;
+    // four independent accumulator chains (one per nibble pair) shorten the
+    // MMA dependency chain to 8
+    float d[4][4];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) d[q][0] = d[q][1] = d[q][2] = d[q][3] = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        const uint4 b0v = *reinterpret_cast<const uint4*>(src0 + 4 * i);
+        const uint4 b1v = *reinterpret_cast<const uint4*>(src1 + 4 * i);
+        const uint32_t b0s[4] = {b0v.x, b0v.y, b0v.z, b0v.w};
+        const uint32_t b1s[4] = {b1v.x, b1v.y, b1v.z, b1v.w};
+        // word i of group A (chunks 0,1 row g; 4,5 row g+8) and group B (2,3 / 6,7)
+        const uint4 ra0 = wv[i >> 2], ra1 = wv[4 + (i >> 2)];
+        const uint4 rb0 = wv[2 + (i >> 2)], rb1 = wv[6 + (i >> 2)];
+        const int cc = i & 3;
+        const uint32_t xa0 = cc == 0 ? ra0.x : cc == 1 ? ra0.y : cc == 2 ? ra0.z : ra0.w;
+        const uint32_t xa1 = cc == 0 ? ra1.x : cc == 1 ? ra1.y : cc == 2 ? ra1.z : ra1.w;
+        const uint32_t xb0 = cc == 0 ? rb0.x : cc == 1 ? rb0.y : cc == 2 ? rb0.z : rb0.w;
+        const uint32_t xb1 = cc == 0 ? rb1.x : cc == 1 ? rb1.y : cc == 2 ? rb1.z : rb1.w;
+#pragma unroll
+        for (int pp = 0; pp < 4; ++pp) {
+            const uint32_t a0 = lop3_and_or(xa0 >> (4 * pp), 0x000F000Fu, 0x43004300u);
+            const uint32_t a1 = lop3_and_or(xa1 >> (4 * pp), 0x000F000Fu, 0x43004300u);
+            const uint32_t a2 = lop3_and_or(xb0 >> (4 * pp), 0x000F000Fu, 0x43004300u);
+            const uint32_t a3 = lop3_and_or(xb1 >> (4 * pp), 0x000F000Fu, 0x43004300u);
+            mma_bf16_16816(d[pp], a0, a1, a2, a3, b0s[pp], b1s[pp]);
+        }
+    }
+    float d0[4], d1[4];
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+        d0[c] = d[0][c] + d[2][c];
+        d1[c] = d[1][c] + d[3][c];
+    }
+    const float xsA = (FULL || gA < pg.G) ? xsum[gA] : 0.f;
+    const float xsB = (FULL || gA + 1 < pg.G) ? xsum[gA + 1] : 0.f;
+    // record: {sA(g), sB(g), sA(g+8), sB(g+8), bA(g), bB(g), bA(g+8), bB(g+8)}
+    const float sA0 = __uint_as_float(sb.x << 16), sB0 = __uint_as_float(sb.x & 0xFFFF0000u);
+    const float sA1 = __uint_as_float(sb.y << 16), sB1 = __uint_as_float(sb.y & 0xFFFF0000u);
+    const float bA0 = __uint_as_float(sb.z << 16), bB0 = __uint_as_float(sb.z & 0xFFFF0000u);
+    const float bA1 = __uint_as_float(sb.w << 16), bB1 = __uint_as_float(sb.w & 0xFFFF0000u);
+    acc0 = fmaf(sA0, d0[0] + d1[0], acc0);
+    acc0 = fmaf(sB0, d0[1] + d1[1], acc0);
+    acc0 = fmaf(fmaf(-128.f, sA0, bA0), xsA, acc0);
+    acc0 = fmaf(fmaf(-128.f, sB0, bB0), xsB, acc0);
+    acc1 = fmaf(sA1, d0[2] + d1[2], acc1);
+    acc1 = fmaf(sB1, d0[3] + d1[3], acc1);
+    acc1 = fmaf(fmaf(-128.f, sA1, bA1), xsA, acc1);
+    acc1 = fmaf(fmaf(-128.f, sB1, bB1), xsB, acc1);
+}
+
 // GEGLU: the interleaved gate/up matrix alternates 16-row gate blocks (even) and the
 // matching up blocks (odd); a CTA processes them as one pair so the epilogue can
 // combine them. BG = row blocks per work group.
@@ -160,7 +350,7 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) qmv_packed_kernel(const 
                 const uint32_t bytes =
                     (unit == pg.nunits - 1) ? static_cast<uint32_t>(pg.item_last) : static_cast<uint32_t>(kItemMax);
                 mbar_expect_tx(bar, bytes);
-                bulk_g2s(smem_u32(my_ring + s * kItemMax), src, bytes, bar);
+                bulk_g2s_hint(smem_u32(my_ring + s * kItemMax), src, bytes, bar, l2_evict_first());
             } else {
                 // a padding block of an odd block count: complete the phase without data
                 mbar_arrive(bar);
@@ -180,116 +370,7 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) qmv_packed_kernel(const 
 
     pdl_wait();
     if (threadIdx.x < 32) zero_page[threadIdx.x] = 0u;
-    const int K = p.K;
-    if (p.prologue == QmvPrologue::kNone) {
-        // One cooperative round trip: 16-byte chunk j of x holds x[8j .. 8j+7], which is
-        // exactly the four permuted pairs xp[4j .. 4j+3] = (x[8j+p], x[8j+p+4]), p < 4.
-        // The 8 chunks of a group sit in 8 consecutive lanes, which reduce its sum.
-        const uint4* xv = reinterpret_cast<const uint4*>(p.x);
-        for (int j0 = 0; j0 < K / 8; j0 += kThreads) {
-            const int j = j0 + static_cast<int>(threadIdx.x);
-            uint4 v = make_uint4(0, 0, 0, 0);
-            if (j < K / 8) v = xv[j];
-            const uint32_t w[4] = {v.x, v.y, v.z, v.w};
-            float part = 0.f;
-#pragma unroll
-            for (int q = 0; q < 4; ++q) part += __uint_as_float(w[q] << 16) + __uint_as_float(w[q] & 0xFFFF0000u);
-            if (j < K / 8) {
-                // pairs: p = 0: (w0.lo, w2.lo), p = 1: (w0.hi, w2.hi), p = 2: (w1.lo, w3.lo), p = 3: (w1.hi, w3.hi)
-                uint4 o;
-                o.x = (w[0] & 0xFFFFu) | (w[2] << 16);
-                o.y = (w[0] >> 16) | (w[2] & 0xFFFF0000u);
-                o.z = (w[1] & 0xFFFFu) | (w[3] << 16);
-                o.w = (w[1] >> 16) | (w[3] & 0xFFFF0000u);
-                *reinterpret_cast<uint4*>(xp + 4 * j) = o;
-            }
-            part += __shfl_xor_sync(0xffffffffu, part, 1);
-            part += __shfl_xor_sync(0xffffffffu, part, 2);
-            part += __shfl_xor_sync(0xffffffffu, part, 4);
-            if (j < K / 8 && (j & 7) == 0) xsum[j >> 3] = part;
-        }
-    } else {
-        // Norm prologues in one round trip: every thread loads its 16-byte chunks of
-        // x (and resid, post_w, norm_w) with independent vector loads into registers,
-        // then the reductions and the permuted-pair writes work from registers.
-        constexpr int kMaxC = kMaxPrologueK / 8 / kThreads;
-        const int nch = K / 8;
-        const uint4* x4 = reinterpret_cast<const uint4*>(p.x);
-        const uint4* n4 = reinterpret_cast<const uint4*>(p.norm_w);
-        const bool resid = p.prologue == QmvPrologue::kResidNorm;
-        uint4 xv[kMaxC], nv4[kMaxC], rv[kMaxC], pv[kMaxC];
-#pragma unroll
-        for (int c = 0; c < kMaxC; ++c) {
-            const int j = static_cast<int>(threadIdx.x) + c * kThreads;
-            const uint4 z = make_uint4(0, 0, 0, 0);
-            xv[c] = j < nch ? x4[j] : z;
-            nv4[c] = j < nch ? n4[j] : z;
-            rv[c] = (resid && j < nch) ? reinterpret_cast<const uint4*>(p.resid)[j] : z;
-            pv[c] = (resid && j < nch) ? reinterpret_cast<const uint4*>(p.post_w)[j] : z;
-        }
-        auto lo = [](uint32_t w) { return __uint_as_float(w << 16); };
-        auto hi = [](uint32_t w) { return __uint_as_float(w & 0xFFFF0000u); };
-        float ss = 0.f;
-#pragma unroll
-        for (int c = 0; c < kMaxC; ++c) {
-            const uint32_t w[4] = {xv[c].x, xv[c].y, xv[c].z, xv[c].w};
-#pragma unroll
-            for (int q = 0; q < 4; ++q) ss += lo(w[q]) * lo(w[q]) + hi(w[q]) * hi(w[q]);
-        }
-        float inv = 1.0f / sqrtf(block_sum(ss, tmp) / static_cast<float>(K) + p.eps);
-        if (resid) {
-            const float sc = p.scalar ? bf2f(p.scalar[0]) : 1.0f;
-            float ss2 = 0.f;
-#pragma unroll
-            for (int c = 0; c < kMaxC; ++c) {
-                uint32_t w[4] = {xv[c].x, xv[c].y, xv[c].z, xv[c].w};
-                const uint32_t r[4] = {rv[c].x, rv[c].y, rv[c].z, rv[c].w};
-                const uint32_t pw[4] = {pv[c].x, pv[c].y, pv[c].z, pv[c].w};
-#pragma unroll
-                for (int q = 0; q < 4; ++q) {
-                    float h0 = rbf(lo(r[q]) + rbf(rbf(lo(w[q]) * inv) * lo(pw[q])));
-                    float h1 = rbf(hi(r[q]) + rbf(rbf(hi(w[q]) * inv) * hi(pw[q])));
-                    if (p.scalar) {
-                        h0 = rbf(h0 * sc);
-                        h1 = rbf(h1 * sc);
-                    }
-                    ss2 += h0 * h0 + h1 * h1;
-                    w[q] = pack_bf2(f2bf(h0), f2bf(h1));
-                }
-                xv[c] = make_uint4(w[0], w[1], w[2], w[3]);
-                const int j = static_cast<int>(threadIdx.x) + c * kThreads;
-                if (blockIdx.x == 0 && p.h_out && j < nch) reinterpret_cast<uint4*>(p.h_out)[j] = xv[c];
-            }
-            inv = 1.0f / sqrtf(block_sum(ss2, tmp) / static_cast<float>(K) + p.eps);
-        }
-#pragma unroll
-        for (int c = 0; c < kMaxC; ++c) {
-            const int j = static_cast<int>(threadIdx.x) + c * kThreads;
-            const uint32_t w[4] = {xv[c].x, xv[c].y, xv[c].z, xv[c].w};
-            const uint32_t nw[4] = {nv4[c].x, nv4[c].y, nv4[c].z, nv4[c].w};
-            uint32_t o[4];
-            float part = 0.f;
-#pragma unroll
-            for (int q = 0; q < 4; ++q) {
-                const float y0 = rbf(rbf(lo(w[q]) * inv) * lo(nw[q]));
-                const float y1 = rbf(rbf(hi(w[q]) * inv) * hi(nw[q]));
-                part += y0 + y1;
-                o[q] = pack_bf2(f2bf(y0), f2bf(y1));
-            }
-            if (j < nch) {
-                uint4 pr;  // permuted pairs (x[8j+p], x[8j+p+4])
-                pr.x = (o[0] & 0xFFFFu) | (o[2] << 16);
-                pr.y = (o[0] >> 16) | (o[2] & 0xFFFF0000u);
-                pr.z = (o[1] & 0xFFFFu) | (o[3] << 16);
-                pr.w = (o[1] >> 16) | (o[3] & 0xFFFF0000u);
-                *reinterpret_cast<uint4*>(xp + 4 * j) = pr;
-            }
-            part += __shfl_xor_sync(0xffffffffu, part, 1);
-            part += __shfl_xor_sync(0xffffffffu, part, 2);
-            part += __shfl_xor_sync(0xffffffffu, part, 4);
-            if (j < nch && (j & 7) == 0) xsum[j >> 3] = part;
-        }
-    }
+    stage_input(p, xp, xsum, tmp);
     __syncthreads();
 
     uint32_t phase_bits = 0;  // one parity bit per stage
@@ -315,73 +396,10 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) qmv_packed_kernel(const 
                 const unsigned char* st = my_ring + s * kItemMax;
                 // Full units (8 groups: every lane valid) take a path without the
                 // per-lane validity selects; only the last unit can be partial.
-                auto item = [&](auto full_tag) {
-                    constexpr bool FULL = decltype(full_tag)::value;
-                    const int tv = FULL ? 4 : (pg.gc_last + 1) / 2;
-                    const int nv = 8 * tv;
-                    const bool valid = FULL || t < tv;
-                    const int rank = g * tv + t;
-                    uint4 wv[8];
-#pragma unroll
-                    for (int c = 0; c < 8; ++c)
-                        wv[c] = valid ? *reinterpret_cast<const uint4*>(st + (c * nv + rank) * 16) : make_uint4(0, 0, 0, 0);
-                    const uint4 sb =
-                        valid ? *reinterpret_cast<const uint4*>(st + (8 * nv + rank) * 16) : make_uint4(0, 0, 0, 0);
-                    const int gA = unit * 8 + 2 * t;
-                    const uint32_t* src0 = (g == 2 * t && (FULL || gA < pg.G)) ? xp + gA * 32 : zero_page;
-                    const uint32_t* src1 = (g == 2 * t + 1 && (FULL || gA + 1 < pg.G)) ? xp + (gA + 1) * 32 : zero_page;
-                    // four independent accumulator chains (one per nibble pair) shorten the
-                    // MMA dependency chain to 8
-                    float d[4][4];
-#pragma unroll
-                    for (int q = 0; q < 4; ++q) d[q][0] = d[q][1] = d[q][2] = d[q][3] = 0.f;
-#pragma unroll
-                    for (int i = 0; i < 8; ++i) {
-                        const uint4 b0v = *reinterpret_cast<const uint4*>(src0 + 4 * i);
-                        const uint4 b1v = *reinterpret_cast<const uint4*>(src1 + 4 * i);
-                        const uint32_t b0s[4] = {b0v.x, b0v.y, b0v.z, b0v.w};
-                        const uint32_t b1s[4] = {b1v.x, b1v.y, b1v.z, b1v.w};
-                        // word i of group A (chunks 0,1 row g; 4,5 row g+8) and group B (2,3 / 6,7)
-                        const uint4 ra0 = wv[i >> 2], ra1 = wv[4 + (i >> 2)];
-                        const uint4 rb0 = wv[2 + (i >> 2)], rb1 = wv[6 + (i >> 2)];
-                        const int cc = i & 3;
-                        const uint32_t xa0 = cc == 0 ? ra0.x : cc == 1 ? ra0.y : cc == 2 ? ra0.z : ra0.w;
-                        const uint32_t xa1 = cc == 0 ? ra1.x : cc == 1 ? ra1.y : cc == 2 ? ra1.z : ra1.w;
-                        const uint32_t xb0 = cc == 0 ? rb0.x : cc == 1 ? rb0.y : cc == 2 ? rb0.z : rb0.w;
-                        const uint32_t xb1 = cc == 0 ? rb1.x : cc == 1 ? rb1.y : cc == 2 ? rb1.z : rb1.w;
-#pragma unroll
-                        for (int pp = 0; pp < 4; ++pp) {
-                            const uint32_t a0 = lop3_and_or(xa0 >> (4 * pp), 0x000F000Fu, 0x43004300u);
-                            const uint32_t a1 = lop3_and_or(xa1 >> (4 * pp), 0x000F000Fu, 0x43004300u);
-                            const uint32_t a2 = lop3_and_or(xb0 >> (4 * pp), 0x000F000Fu, 0x43004300u);
-                            const uint32_t a3 = lop3_and_or(xb1 >> (4 * pp), 0x000F000Fu, 0x43004300u);
-                            mma_bf16_16816(d[pp], a0, a1, a2, a3, b0s[pp], b1s[pp]);
-                        }
-                    }
-                    float d0[4], d1[4];
-#pragma unroll
-                    for (int c = 0; c < 4; ++c) {
-                        d0[c] = d[0][c] + d[2][c];
-                        d1[c] = d[1][c] + d[3][c];
-                    }
-                    const float xsA = (FULL || gA < pg.G) ? xsum[gA] : 0.f;
-                    const float xsB = (FULL || gA + 1 < pg.G) ? xsum[gA + 1] : 0.f;
-                    // record: {sA(g), sB(g), sA(g+8), sB(g+8), bA(g), bB(g), bA(g+8), bB(g+8)}
-                    const float sA0 = __uint_as_float(sb.x << 16), sB0 = __uint_as_float(sb.x & 0xFFFF0000u);
-                    const float sA1 = __uint_as_float(sb.y << 16), sB1 = __uint_as_float(sb.y & 0xFFFF0000u);
-                    const float bA0 = __uint_as_float(sb.z << 16), bB0 = __uint_as_float(sb.z & 0xFFFF0000u);
-                    const float bA1 = __uint_as_float(sb.w << 16), bB1 = __uint_as_float(sb.w & 0xFFFF0000u);
-                    acc0 = fmaf(sA0, d0[0] + d1[0], acc0);
-                    acc0 = fmaf(sB0, d0[1] + d1[1], acc0);
-                    acc0 = fmaf(fmaf(-128.f, sA0, bA0), xsA, acc0);
-                    acc0 = fmaf(fmaf(-128.f, sB0, bB0), xsB, acc0);
-                    acc1 = fmaf(sA1, d0[2] + d1[2], acc1);
-                    acc1 = fmaf(sB1, d0[3] + d1[3], acc1);
-                    acc1 = fmaf(fmaf(-128.f, sA1, bA1), xsA, acc1);
-                    acc1 = fmaf(fmaf(-128.f, sB1, bB1), xsB, acc1);
-                };
-                if (unit != pg.nunits - 1 || pg.gc_last == 8) item(std::true_type{});
-                else item(std::false_type{});
+                if (unit != pg.nunits - 1 || pg.gc_last == 8)
+                    qmv_item<true>(st, xp, zero_page, xsum, pg, unit, g, t, acc0, acc1);
+                else
+                    qmv_item<false>(st, xp, zero_page, xsum, pg, unit, g, t, acc0, acc1);
             }
             acc0 += __shfl_xor_sync(0xffffffffu, acc0, 1);
             acc0 += __shfl_xor_sync(0xffffffffu, acc0, 2);
@@ -499,31 +517,27 @@ void launch_qmv_pack(const uint32_t* w, const bf16* s, const bf16* b, int K, int
     HYB_LAUNCH_CHECK("qmv_pack_kernel");
 }
 
-void launch_qmv_packed(const QmvParams& p, cudaStream_t stream, bool pdl) {
+namespace {
+
+void check_packed_stage(const QmvParams& p) {
     if (p.K <= 0 || p.K % 64 != 0 || p.N <= 0) throw ArgError("qmv: K must be a positive multiple of 64");
     if (!p.packed) throw ArgError("qmv_packed: packed weights are required");
     if ((reinterpret_cast<uintptr_t>(p.packed) & 15u) != 0) throw ArgError("qmv_packed: packed weights must be 16-byte aligned");
     const bool pro = p.prologue != QmvPrologue::kNone;
     if (pro && p.K > kMaxPrologueK) throw ArgError("qmv_packed: norm prologues support K <= 8192");
     if (reinterpret_cast<uintptr_t>(p.x) & 15u) throw ArgError("qmv_packed: x must be 16-byte aligned");
-    const size_t smem = packed_smem_bytes(p.K, pro);
-    if (smem > 227 * 1024) throw ArgError("qmv_packed: K too large for the shared-memory plan");
-    int dev = 0;
-    HYB_CUDA(cudaGetDevice(&dev));
-    static int attr_dev = -1;
-    if (attr_dev != dev) {
-        HYB_CUDA(cudaFuncSetAttribute(qmv_packed_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024));
-        HYB_CUDA(cudaFuncSetAttribute(qmv_packed_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024));
-        attr_dev = dev;
-    }
+    if (packed_smem_bytes(p.K, pro) > 227 * 1024) throw ArgError("qmv_packed: K too large for the shared-memory plan");
+    if (p.epilogue == QmvEpilogue::kGeglu && p.N % 32 != 0)
+        throw ArgError("qmv geglu: interleaved rows must be a multiple of 32");
+}
+
+// Team size: the one with the fewest items on the busiest warp, the smallest on ties
+// (independent warps where N is large, the whole CTA on one row block where it is
+// small). Returns the team; *grid_needed = CTAs that have work.
+int choose_team(const QmvParams& p, int max_ctas, int* grid_needed) {
     const PackGeo pg = pack_geo(p.K, p.N);
     const bool geglu = p.epilogue == QmvEpilogue::kGeglu;
-    if (geglu && p.N % 32 != 0) throw ArgError("qmv geglu: interleaved rows must be a multiple of 32");
     const int groups = geglu ? (pg.nrb + 1) / 2 : pg.nrb;
-    // Team size: the one with the fewest items on the busiest warp, the smallest on
-    // ties (independent warps where N is large, the whole CTA on one row block where
-    // it is small).
-    const int max_ctas = kCtasPerSm * num_sms();
     int team = kWarps, best = 1 << 30;
     for (int w = kWarps; w >= 1; w /= 2) {
         const int tpc_w = kWarps / w;
@@ -535,7 +549,25 @@ void launch_qmv_packed(const QmvParams& p, cudaStream_t stream, bool pdl) {
         }
     }
     const int tpc = kWarps / team;
-    const int grid = std::max(1, std::min((groups + tpc - 1) / tpc, max_ctas));
+    *grid_needed = std::max(1, std::min((groups + tpc - 1) / tpc, max_ctas));
+    return team;
+}
+
+}  // namespace
+
+void launch_qmv_packed(const QmvParams& p, cudaStream_t stream, bool pdl) {
+    check_packed_stage(p);
+    const size_t smem = packed_smem_bytes(p.K, p.prologue != QmvPrologue::kNone);
+    int dev = 0;
+    HYB_CUDA(cudaGetDevice(&dev));
+    static int attr_dev = -1;
+    if (attr_dev != dev) {
+        HYB_CUDA(cudaFuncSetAttribute(qmv_packed_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024));
+        HYB_CUDA(cudaFuncSetAttribute(qmv_packed_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024));
+        attr_dev = dev;
+    }
+    int grid = 1;
+    const int team = choose_team(p, kCtasPerSm * num_sms(), &grid);
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(grid);
     cfg.blockDim = dim3(kThreads);
@@ -546,7 +578,7 @@ void launch_qmv_packed(const QmvParams& p, cudaStream_t stream, bool pdl) {
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = pdl ? 1 : 0;
-    if (geglu) HYB_CUDA(cudaLaunchKernelEx(&cfg, qmv_packed_kernel<true>, p, team));
+    if (p.epilogue == QmvEpilogue::kGeglu) HYB_CUDA(cudaLaunchKernelEx(&cfg, qmv_packed_kernel<true>, p, team));
     else HYB_CUDA(cudaLaunchKernelEx(&cfg, qmv_packed_kernel<false>, p, team));
 }
 
