@@ -717,7 +717,9 @@ def run_attn_decode(args, rank, world, local):
 def run_tp_decode(args, rank, world, local):
     """Config 4: the 27B-shaped decoder split over the job's GPUs (one rank per GPU,
     column/row-parallel projections, NCCL all-reduce after o_proj and down_proj,
-    vocab-parallel lm_head), batch-1 greedy decode after a --ctx prefill."""
+    vocab-parallel lm_head), greedy decode after a --ctx prefill. --batch B > 1 decodes B
+    sequences per step through hyb_decode_batch: the prefilled context is cloned B times
+    (hyb_kvstate_clone) with distinct next tokens, so every sequence attends over ctx keys."""
     import torch
     import hyperion_b200 as hb
     from hyperion_b200.synth import config4
@@ -739,9 +741,13 @@ def run_tp_decode(args, rank, world, local):
     t0 = time.perf_counter()
     kv.prefill(prompt)
     prefill_s = max_over_ranks(time.perf_counter() - t0, world)
+    B = args.batch
+    seqs = [kv] if B == 1 else [kv.clone(last_token=int(t)) for t in
+                                torch.randint(0, geo.vocab_size, (B,), generator=torch.Generator().manual_seed(9))]
+    step = (lambda: kv.decode(1)) if B == 1 else (lambda: eng.decode_batch(seqs))
     stream = torch.cuda.ExternalStream(eng.stream())
     for _ in range(args.warmup):
-        kv.decode(1)
+        step()
     barrier(world)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(local) as clk:
@@ -749,7 +755,7 @@ def run_tp_decode(args, rank, world, local):
         w0 = time.perf_counter()
         e0.record(stream)
         for _ in range(args.steps):
-            kv.decode(1)
+            step()  # host tokens in, greedy results read back every step
         e1.record(stream)
         torch.cuda.synchronize()
         wall_ms = (time.perf_counter() - w0) * 1e3 / args.steps
@@ -757,26 +763,35 @@ def run_tp_decode(args, rank, world, local):
     wall_ms = max_over_ranks(wall_ms, world)
     if rank != 0:
         return
-    # weight bytes each rank streams per token: its shard of the projections + its lm_head rows
+    # bytes each rank streams per step: its shard of the projections and lm_head rows once,
+    # plus its KV heads of every sequence
     per_layer = (qmv_bytes(5376, 8192 + 2 * 4096) + qmv_bytes(4096, 5376) + qmv_bytes(5376, 2 * 21504) +
                  qmv_bytes(21504, 5376)) / world
     w_bytes = 62 * per_layer + qmv_bytes(5376, 262144) / world
+    kv_bytes = 0
+    for i, kind in enumerate(geo.layer_types):
+        n = min(geo.sliding_window, ctx + args.warmup) if kind == 0 else ctx + args.warmup
+        kv_bytes += 2 * n * geo.n_kv(i) * geo.head_dim(i) * 2
+    step_bytes = w_bytes + B * kv_bytes / world
     hbm, _, src = peaks()
-    gbs = w_bytes / (ms * 1e-3) / 1e9
-    print(json.dumps({"metric": "27B-shaped tensor-parallel decode tok/s (cfg4, batch 1)",
-                      "value": round(1e3 / ms, 2), "unit": "tok/s", "n_gpus": world, "steps": args.steps,
+    gbs = step_bytes / (ms * 1e-3) / 1e9
+    launches = (1 + 5 * 62 + 4) if B == 1 else (2 + 11 * 62 + 4 + (1 if world > 1 else 0))
+    print(json.dumps({"metric": f"27B-shaped tensor-parallel decode tok/s (cfg4, batch {B})",
+                      "value": round(B * 1e3 / ms, 2), "unit": "tok/s", "n_gpus": world, "steps": args.steps,
                       "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True,
                       "scaling": "strong", "vs_baseline": None, "dtype": "u4/bf16->f32", "data": "synthetic",
-                      "config": {"workload": f"cfg4 27B-shaped decode, ctx {ctx}, batch 1",
+                      "config": {"workload": f"cfg4 27B-shaped decode, ctx {ctx}, batch {B}",
                                  "parallelism": f"tp{world}", "prefill_s": round(prefill_s, 3),
                                  "l2": "inputs larger than L2"},
                       "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": hbm, "unit": "GB/s",
                                    "frac": round(gbs / hbm, 4), "traffic": None, "peak_source": src,
-                                   "kernel": "whole decode step per rank (weight bytes of its shard per token)"},
-                      "gpu_launches": (1 + 5 * 62 + 4) * args.steps,
-                      "e2e": {"value": round(1e3 / wall_ms, 2), "unit": "tok/s", "h2d_bytes_per_step": 4,
-                              "d2h_bytes_per_step": 64 * world,
-                              "path": "hyp_decode_block(n_tokens=1) on every rank, host wall clock"},
+                                   "kernel": "whole decode step per rank (its weight shard + its KV heads of "
+                                             "every sequence)"},
+                      "gpu_launches": launches * args.steps,
+                      "e2e": {"value": round(B * 1e3 / wall_ms, 2), "unit": "tok/s", "h2d_bytes_per_step": 4 * B,
+                              "d2h_bytes_per_step": (64 if B == 1 else 8 * B) * world,
+                              "path": ("hyp_decode_block(n_tokens=1)" if B == 1 else "hyb_decode_batch") +
+                                      " on every rank, host wall clock"},
                       "clocks": clk.summary()}), flush=True)
 
 
@@ -792,6 +807,7 @@ def main():
     ap.add_argument("--shape", default="3840,262144", help="K,N for --workload qmv-shape")
     ap.add_argument("--layout", default="packed", choices=["packed", "mlx"], help="weights for qmv-shape")
     ap.add_argument("--ctx", type=int, default=4096)
+    ap.add_argument("--batch", type=int, default=1, help="tp-decode: sequences decoded per step (1..64)")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
 

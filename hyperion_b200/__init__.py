@@ -105,7 +105,7 @@ EXT_FUNCTIONS = [
     "hyb_qmv_packed", "hyb_sdpa_decode_scratch_bytes", "hyb_sdpa_decode", "hyb_sdpa_decode_noalloc",
     "hyb_sdpa_decode_fused", "hyb_wait_timeouts", "hyb_nccl_unique_id", "hyb_model_set_tensor_parallel",
     "hyb_sdpa_prefill", "hyb_rms_norm", "hyb_qkv_post", "hyb_model_load_synthetic",
-    "hyb_model_set_attention_rounding", "hyb_model_stream",
+    "hyb_model_set_attention_rounding", "hyb_model_stream", "hyb_decode_batch", "hyb_kvstate_clone", "hyb_qmv_batched",
     "hyb_kv_copy_layer", "hyb_kv_cursor", "hyb_prefill_logits", "hyb_decode_logits", "hyb_decode_forced",
     "hyb_test_arm_post_append_fault",
 ]
@@ -160,6 +160,9 @@ def lib() -> ctypes.CDLL:
                          c.c_int32, c.c_float, P, P, P, P, P, c.c_int32, c.c_int32, P],
         "hyb_model_load_synthetic": [P, ctypes.POINTER(HypGeometryParams), c.c_uint64],
         "hyb_model_set_attention_rounding": [P, c.c_int32],
+        "hyb_kvstate_clone": [P, P, c.c_uint32, ctypes.POINTER(P)],
+        "hyb_qmv_batched": [P, c.c_int32, c.c_int64, P, P, c.c_int64, c.c_int64, c.c_int64, c.c_int32, P],
+        "hyb_decode_batch": [P, ctypes.POINTER(P), c.c_uint32, ctypes.POINTER(c.c_uint32), ctypes.POINTER(c.c_float)],
         "hyb_model_stream": [P, ctypes.POINTER(P)],
         "hyb_kv_copy_layer": [P, P, c.c_uint32, c.c_int32, P, ctypes.POINTER(c.c_uint32)],
         "hyb_kv_cursor": [P, ctypes.POINTER(c.c_uint32), ctypes.POINTER(c.c_uint32)],
@@ -303,6 +306,16 @@ class Engine:
     def set_attention_rounding(self, mode: int) -> None:
         check(lib().hyb_model_set_attention_rounding(self._model, mode))
 
+    def decode_batch(self, kvs: Sequence["KvState"]):
+        """One greedy step of every state in `kvs` together (hyb_decode_batch):
+        returns (tokens, post-softcap logits), one per state."""
+        n = len(kvs)
+        arr = (ctypes.c_void_p * n)(*[k._kv.value for k in kvs])
+        toks = (ctypes.c_uint32 * n)()
+        logs = (ctypes.c_float * n)()
+        check(lib().hyb_decode_batch(self._model, arr, n, toks, logs))
+        return list(toks), list(logs)
+
     def new_kv(self) -> "KvState":
         return KvState(self)
 
@@ -317,6 +330,15 @@ class KvState:
         self.eng = eng
         self._kv = ctypes.c_void_p()
         check(lib().hyp_kvstate_create(eng.handle, ctypes.byref(self._kv)))
+
+    def clone(self, last_token: Optional[int] = None) -> "KvState":
+        """A copy of this state (hyb_kvstate_clone) whose next input is `last_token`."""
+        k = KvState.__new__(KvState)
+        k.eng = self.eng
+        k._kv = ctypes.c_void_p()
+        check(lib().hyb_kvstate_clone(self.eng.handle, self._kv, 0xFFFFFFFF if last_token is None else last_token,
+                                      ctypes.byref(k._kv)))
+        return k
 
     def close(self):
         if self._kv:

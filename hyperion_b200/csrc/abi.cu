@@ -605,6 +605,69 @@ HypStatus hyb_model_stream(HypModel model, void** out_stream) {
     return ok();
 }
 
+HypStatus hyb_kvstate_clone(HypModel model, HypKvState src, uint32_t last_token, HypKvState* out) {
+    HypStatus st = validate_model(model);
+    if (st != HYP_STATUS_OK) return st;
+    st = validate_kv(src);
+    if (st != HYP_STATUS_OK) return st;
+    if (out == nullptr) return fail(HYP_STATUS_INVALID_ARGUMENT, "out is null");
+    if (!model->loaded) return fail(HYP_STATUS_INVALID_ARGUMENT, "model is not loaded");
+    if (src->owner != model) return fail(HYP_STATUS_INVALID_ARGUMENT, "kvstate belongs to another model");
+    hyb::Model& m = *model->model;
+    if (last_token != UINT32_MAX && last_token >= m.geometry().vocab)
+        return fail(HYP_STATUS_INVALID_ARGUMENT, "token id is outside the vocabulary");
+    return guarded("hyb_kvstate_clone", [&]() -> HypStatus {
+        DeviceGuard dg(m.device());
+        auto kv = m.clone_kv(*src->kv, last_token == UINT32_MAX ? src->kv->last_token : last_token);
+        auto* h = new HypKvStateOpaque{};
+        h->magic = kKvStateMagic;
+        h->kv = std::move(kv);
+        h->owner = model;
+        *out = h;
+        return ok();
+    });
+}
+
+HypStatus hyb_decode_batch(HypModel model, const HypKvState* kvstates, uint32_t n, uint32_t* tokens_out,
+                           float* logits_out) {
+    HypStatus st = validate_model(model);
+    if (st != HYP_STATUS_OK) return st;
+    if (!model->loaded) return fail(HYP_STATUS_INVALID_ARGUMENT, "model is not loaded");
+    if (kvstates == nullptr || tokens_out == nullptr) return fail(HYP_STATUS_INVALID_ARGUMENT, "null argument");
+    if (n == 0 || n > static_cast<uint32_t>(hyb::kMaxDecodeBatch))
+        return fail(HYP_STATUS_INVALID_ARGUMENT, "batch must hold 1 to 64 states");
+    for (uint32_t i = 0; i < n; ++i) {
+        st = validate_kv(kvstates[i]);
+        if (st != HYP_STATUS_OK) return st;
+        if (kvstates[i]->owner != model) return fail(HYP_STATUS_INVALID_ARGUMENT, "kvstate belongs to another model");
+        if (kvstates[i]->kv->offset == 0)
+            return fail(HYP_STATUS_INVALID_ARGUMENT, "decode requires a populated KV state (prefill first)");
+        for (uint32_t j = 0; j < i; ++j)
+            if (kvstates[j] == kvstates[i]) return fail(HYP_STATUS_INVALID_ARGUMENT, "a kvstate appears twice in the batch");
+    }
+    hyb::Model& m = *model->model;
+    return guarded("hyb_decode_batch", [&]() -> HypStatus {
+        DeviceGuard dg(m.device());
+        std::string why;
+        for (uint32_t i = 0; i < n; ++i)
+            if (!admit(m, *kvstates[i]->kv, 1, why)) return fail(HYP_STATUS_OOM_GOVERNOR, why);
+        std::vector<hyb::KvState*> ks(n);
+        for (uint32_t i = 0; i < n; ++i) ks[i] = kvstates[i]->kv.get();
+        std::vector<hyb::StepOut> outs(n);
+        try {
+            m.decode_batch(ks.data(), static_cast<int>(n), outs.data());
+        } catch (...) {
+            for (auto* k : ks) k->poisoned = true;  // a failed step consumes every state of the batch
+            throw;
+        }
+        for (uint32_t i = 0; i < n; ++i) {
+            tokens_out[i] = outs[i].token;
+            if (logits_out) logits_out[i] = outs[i].logit;
+        }
+        return ok();
+    });
+}
+
 HypStatus hyb_nccl_unique_id(void* out128) {
     if (out128 == nullptr) return fail(HYP_STATUS_INVALID_ARGUMENT, "output buffer is null");
     return guarded("hyb_nccl_unique_id", [&]() -> HypStatus {

@@ -221,17 +221,28 @@ __global__ void __launch_bounds__(kThreads) decode_attn_fused_kernel(const Decod
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int g = lane >> 2, t4 = lane & 3;  // MMA fragment coordinates
     const int hk = blockIdx.y;
+    // this CTA's sequence: the launch's own fields, or entry blockIdx.z of a batched launch
+    const DecodeSeq* sq = p.seqs ? p.seqs + blockIdx.z : nullptr;
+    const bf16* qkv = sq ? sq->qkv : p.qkv;
+    bf16* out = sq ? sq->out : p.out;
+    bf16* k_cache = sq ? sq->k_cache : p.k_cache;
+    bf16* v_cache = sq ? sq->v_cache : p.v_cache;
+    const int cap = sq ? sq->cap : p.cap;
+    const int pos = sq ? sq->pos : p.pos;
+    const int n_keys = sq ? sq->n_keys : p.n_keys;
+    const CUtensorMap* map_k = sq ? &sq->tk : &tmk;
+    const CUtensorMap* map_v = sq ? &sq->tv : &tmv;
     const int CS = gridDim.x;
     const uint32_t rank = cluster_rank();
     const int j0 = static_cast<int>(rank) * chunk;
-    const int j1 = min(p.n_keys, j0 + chunk);
+    const int j1 = min(n_keys, j0 + chunk);
     const int n = max(0, j1 - j0);
-    const bool owns_newest = (j1 == p.n_keys) && n > 0;
-    const int newest = p.n_keys - 1;
-    const int first_pos = p.pos - p.n_keys + 1;
+    const bool owns_newest = (j1 == n_keys) && n > 0;
+    const int newest = n_keys - 1;
+    const int first_pos = pos - n_keys + 1;
     // tiles: segment A = keys before the ring wraps to slot 0, segment B = the rest
-    const int s_first = (first_pos + j0) % p.cap;
-    const int lenA = min(n, p.cap - s_first);
+    const int s_first = (first_pos + j0) % cap;
+    const int lenA = min(n, cap - s_first);
     const int ntA = (lenA + T - 1) / T;
     const int nt = ntA + (n - lenA + T - 1) / T;  // K tiles (and V tiles) of this CTA
     const int items = 2 * nt;                     // item t < nt: K tile t; t >= nt: V tile t - nt
@@ -268,11 +279,16 @@ __global__ void __launch_bounds__(kThreads) decode_attn_fused_kernel(const Decod
         mbar_expect_tx(fb, TILE);
 #pragma unroll
         for (int sub = 0; sub < SUB; ++sub)
-            tma_load_3d_hint(tiles_u32 + s * TILE + sub * (T * 128), isv ? &tmv : &tmk, 64 * sub, hk, tk.z, fb,
+            tma_load_3d_hint(tiles_u32 + s * TILE + sub * (T * 128), isv ? map_v : map_k, 64 * sub, hk, tk.z, fb,
                              l2_evict_first());
     };
-    if (threadIdx.x == 0)
+    if (threadIdx.x == 0) {
+        if (sq) {  // tensor maps written to global memory by a copy: acquire them for the TMA unit
+            asm volatile("fence.proxy.tensormap::generic.acquire.gpu [%0], 128;" ::"l"(map_k) : "memory");
+            asm volatile("fence.proxy.tensormap::generic.acquire.gpu [%0], 128;" ::"l"(map_v) : "memory");
+        }
         for (int it = 0; it < stages && it < items; ++it) issue(it);
+    }
 
     pdl_wait();
     // ---- phase 0: query heads of this KV head, and the new token's K/V
@@ -280,16 +296,16 @@ __global__ void __launch_bounds__(kThreads) decode_attn_fused_kernel(const Decod
     const int k_col = p.n_heads * HD + hk * HD;
     const int v_col = p.v_from_k ? k_col : p.n_heads * HD + p.n_kv * HD + hk * HD;
     for (int r = warp; r < REP; r += kWarps - 2)
-        norm_rope_row<PER>(p.qkv + q_col + r * HD, p.q_norm, p.inv_freq, p.pos, p.eps, true, q_s + r * HD,
+        norm_rope_row<PER>(qkv + q_col + r * HD, p.q_norm, p.inv_freq, pos, p.eps, true, q_s + r * HD,
                            nullptr);
     if (owns_newest) {
-        const int slot = p.pos % p.cap;
+        const int slot = pos % cap;
         if (warp == kWarps - 1)
-            norm_rope_row<PER>(p.qkv + k_col, p.k_norm, p.inv_freq, p.pos, p.eps, true, knew,
-                               p.k_cache + (static_cast<size_t>(slot) * p.n_kv + hk) * HD);
+            norm_rope_row<PER>(qkv + k_col, p.k_norm, p.inv_freq, pos, p.eps, true, knew,
+                               k_cache + (static_cast<size_t>(slot) * p.n_kv + hk) * HD);
         if (warp == kWarps - 2)
-            norm_rope_row<PER>(p.qkv + v_col, nullptr, p.inv_freq, p.pos, p.eps, false, vnew,
-                               p.v_cache + (static_cast<size_t>(slot) * p.n_kv + hk) * HD);
+            norm_rope_row<PER>(qkv + v_col, nullptr, p.inv_freq, pos, p.eps, false, vnew,
+                               v_cache + (static_cast<size_t>(slot) * p.n_kv + hk) * HD);
     }
     __syncthreads();
 
@@ -503,7 +519,7 @@ __global__ void __launch_bounds__(kThreads) decode_attn_fused_kernel(const Decod
     for (int i = e0 + static_cast<int>(threadIdx.x); i < e1; i += kThreads) {
         float v = 0.f;
         for (int c = 0; c < CS; ++c) v += recv[c * per_cta + (i - e0)];
-        p.out[static_cast<size_t>(hk * REP) * HD + i] = f2bf(v);
+        out[static_cast<size_t>(hk * REP) * HD + i] = f2bf(v);
     }
     if (__syncthreads_or(!waits_ok) && threadIdx.x == 0) {
         atomicAdd(&g_attn_wait_timeouts, 1);
@@ -548,7 +564,7 @@ void launch_fused_t(const DecodeFusedParams& p, cudaStream_t stream, bool pdl) {
         attr_dev = dev;
     }
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(f.cs, p.n_kv);
+    cfg.gridDim = dim3(f.cs, p.n_kv, p.seqs ? p.n_seq : 1);
     cfg.blockDim = dim3(kThreads);
     cfg.dynamicSmemBytes = f.smem;
     cfg.stream = stream;
@@ -561,11 +577,13 @@ void launch_fused_t(const DecodeFusedParams& p, cudaStream_t stream, bool pdl) {
     attr[1].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = pdl ? 2 : 1;
-    CUtensorMap tk, tv;
-    if (p.tmap_k) tk = *p.tmap_k;
-    else encode_kv_tensor_map(&tk, p.k_cache, p.cap, p.n_kv, p.hd);
-    if (p.tmap_v) tv = *p.tmap_v;
-    else encode_kv_tensor_map(&tv, p.v_cache, p.cap, p.n_kv, p.hd);
+    CUtensorMap tk{}, tv{};  // a batched launch reads every sequence's maps from p.seqs
+    if (!p.seqs) {
+        if (p.tmap_k) tk = *p.tmap_k;
+        else encode_kv_tensor_map(&tk, p.k_cache, p.cap, p.n_kv, p.hd);
+        if (p.tmap_v) tv = *p.tmap_v;
+        else encode_kv_tensor_map(&tv, p.v_cache, p.cap, p.n_kv, p.hd);
+    }
     HYB_CUDA(cudaLaunchKernelEx(&cfg, kern, p, f.chunk, f.stages, tk, tv));
 }
 
@@ -620,6 +638,22 @@ void launch_decode_attn_fused(const DecodeFusedParams& p, cudaStream_t stream, b
         case 64: launch_fused_rep<2>(p, stream, pdl); break;
         case 128: launch_fused_rep<4>(p, stream, pdl); break;
         case 256: launch_fused_rep<8>(p, stream, pdl); break;
+        default: throw ArgError("decode attention: head_dim must be 64, 128 or 256");
+    }
+}
+
+void launch_decode_attn_fused_batch(const DecodeFusedParams& p, int n_keys_max, cudaStream_t stream, bool pdl) {
+    if (!p.seqs || p.n_seq < 1 || p.n_seq > 65535 || (reinterpret_cast<uintptr_t>(p.seqs) & 63))
+        throw ArgError("decode attention batch: sequences must be a 64-byte aligned device array");
+    if (n_keys_max <= 0 || p.n_kv <= 0 || p.n_heads % p.n_kv != 0)
+        throw ArgError("decode attention batch: bad shape");
+    if ((p.n_heads / p.n_kv) * p.hd > 1024) throw ArgError("decode attention: GQA group x head_dim > 1024");
+    DecodeFusedParams q = p;
+    q.n_keys = n_keys_max;  // the shared-memory plan covers the longest sequence
+    switch (p.hd) {
+        case 64: launch_fused_rep<2>(q, stream, pdl); break;
+        case 128: launch_fused_rep<4>(q, stream, pdl); break;
+        case 256: launch_fused_rep<8>(q, stream, pdl); break;
         default: throw ArgError("decode attention: head_dim must be 64, 128 or 256");
     }
 }

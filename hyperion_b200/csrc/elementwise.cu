@@ -217,6 +217,7 @@ __global__ void gather_ring_kernel(const bf16* __restrict__ cache, int cap, int 
 // sampled epilogue works on the full host copy of the logits.
 constexpr int kTopK = 2;
 constexpr int kTkThreads = 256;
+static_assert(kTopK <= kTopkRowStride, "a row's candidates fit its output slot");
 
 // Insert (v, i) into a descending list; ties keep the smaller index first.
 __device__ __forceinline__ void topk_insert(float (&vals)[kTopK], int (&idx)[kTopK], float v, int i) {
@@ -231,8 +232,12 @@ __device__ __forceinline__ void topk_insert(float (&vals)[kTopK], int (&idx)[kTo
     idx[pos] = i;
 }
 
-// Stage 1: each block applies the softcap to its slice and emits its top-8.
-__global__ void softcap_topk_stage1(bf16* logits, int N, float cap, float* part_val, int* part_idx) {
+// Stage 1: each block applies the softcap to its slice and emits its top kTopK. Row
+// blockIdx.y of a [rows][ld] logits batch; its candidates at part_* + y * gridDim.x * kTopK.
+__global__ void softcap_topk_stage1(bf16* logits, int N, float cap, float* part_val, int* part_idx, long long ld) {
+    logits += blockIdx.y * ld;
+    part_val += static_cast<size_t>(blockIdx.y) * gridDim.x * kTopK;
+    part_idx += static_cast<size_t>(blockIdx.y) * gridDim.x * kTopK;
     float vals[kTopK];
     int idx[kTopK];
 #pragma unroll
@@ -283,6 +288,11 @@ __global__ void softcap_topk_stage1(bf16* logits, int N, float cap, float* part_
 // Stage 2: one block merges the per-block candidates (strided scan + shared-memory tree).
 __global__ void softcap_topk_stage2(const float* part_val, const int* part_idx, int nparts, uint32_t* out_idx,
                                     float* out_val) {
+    // one block per row (blockIdx.x); row r's result at out_* + kTopkRowStride r
+    part_val += static_cast<size_t>(blockIdx.x) * nparts * kTopK;
+    part_idx += static_cast<size_t>(blockIdx.x) * nparts * kTopK;
+    out_idx += blockIdx.x * kTopkRowStride;
+    out_val += blockIdx.x * kTopkRowStride;
     float vals[kTopK];
     int idx[kTopK];
 #pragma unroll
@@ -380,9 +390,23 @@ void launch_softcap_topk(bf16* logits, int N, float cap, float* scratch, int scr
     if (scratch_floats < nb * kTopK * 2) throw ArgError("softcap_topk: scratch too small");
     float* pv = scratch;
     int* pi = reinterpret_cast<int*>(scratch + nb * kTopK);
-    softcap_topk_stage1<<<nb, kTkThreads, 0, stream>>>(logits, N, cap, pv, pi);
+    softcap_topk_stage1<<<nb, kTkThreads, 0, stream>>>(logits, N, cap, pv, pi, 0);
     HYB_LAUNCH_CHECK("softcap_topk_stage1");
     softcap_topk_stage2<<<1, kTkThreads, 0, stream>>>(pv, pi, nb, out_idx, out_val);
+    HYB_LAUNCH_CHECK("softcap_topk_stage2");
+}
+
+void launch_softcap_topk_rows(bf16* logits, int rows, long long ld, int N, float cap, float* scratch,
+                              size_t scratch_floats, uint32_t* out_idx, float* out_val, cudaStream_t stream) {
+    if (rows <= 0) return;
+    const int nb = topk_blocks(N);
+    const size_t per = static_cast<size_t>(nb) * kTopK;
+    if (scratch_floats < per * 2 * rows) throw ArgError("softcap_topk: scratch too small");
+    float* pv = scratch;
+    int* pi = reinterpret_cast<int*>(scratch + per * rows);
+    softcap_topk_stage1<<<dim3(nb, rows), kTkThreads, 0, stream>>>(logits, N, cap, pv, pi, ld);
+    HYB_LAUNCH_CHECK("softcap_topk_stage1");
+    softcap_topk_stage2<<<rows, kTkThreads, 0, stream>>>(pv, pi, nb, out_idx, out_val);
     HYB_LAUNCH_CHECK("softcap_topk_stage2");
 }
 

@@ -155,6 +155,17 @@ __global__ void tp_candidates_kernel(const uint32_t* idx, const float* val, uint
     }
 }
 
+// Rows of a batch: (winner, runner-up) of row r with global vocabulary indices at cand + 4 r.
+__global__ void tp_candidates_rows_kernel(const uint32_t* idx, const float* val, int rows, uint32_t vocab0,
+                                          uint32_t* cand) {
+    for (int r = threadIdx.x; r < rows; r += blockDim.x) {
+        cand[4 * r + 0] = idx[kTopkRowStride * r] + vocab0;
+        cand[4 * r + 1] = __float_as_uint(val[kTopkRowStride * r]);
+        cand[4 * r + 2] = idx[kTopkRowStride * r + 1] + vocab0;
+        cand[4 * r + 3] = __float_as_uint(val[kTopkRowStride * r + 1]);
+    }
+}
+
 int grid_for(size_t n) { return static_cast<int>(std::min<size_t>((n + 255) / 256, 4096)); }
 
 // Rows [row0, row0 + rows) x columns [col0, col0 + K) of a synthetic [*, K_full] Q4
@@ -220,6 +231,10 @@ Model::~Model() {
     if (ws_.h_topk_val) cudaFreeHost(ws_.h_topk_val);
     if (ws_.h_cand) cudaFreeHost(ws_.h_cand);
     if (ws_.h_ids) cudaFreeHost(ws_.h_ids);
+    if (bws_.h_seqs) cudaFreeHost(bws_.h_seqs);
+    if (bws_.h_idx) cudaFreeHost(bws_.h_idx);
+    if (bws_.h_val) cudaFreeHost(bws_.h_val);
+    if (bws_.h_cand) cudaFreeHost(bws_.h_cand);
     if (stream_) cudaStreamDestroy(stream_);
 }
 
@@ -474,6 +489,46 @@ std::unique_ptr<KvState> Model::new_kv() const {
             kv->global.push_back(std::move(c));
         }
     }
+    HYB_CUDA(cudaStreamSynchronize(stream_));
+    return kv;
+}
+
+std::unique_ptr<KvState> Model::clone_kv(const KvState& src, uint32_t last_token) const {
+    auto kv = std::make_unique<KvState>();
+    for (const auto& s : src.local) {
+        LocalCache c;
+        c.nkv = s.nkv;
+        c.hd = s.hd;
+        c.cap = s.cap;
+        c.committed = s.committed;
+        const size_t n = static_cast<size_t>(c.cap) * c.nkv * c.hd;
+        c.k.reset(n);
+        c.v.reset(n);
+        HYB_CUDA(cudaMemcpyAsync(c.k.p, s.k.p, n * 2, cudaMemcpyDeviceToDevice, stream_));
+        HYB_CUDA(cudaMemcpyAsync(c.v.p, s.v.p, n * 2, cudaMemcpyDeviceToDevice, stream_));
+        encode_kv_tensor_map(&c.tk, c.k.p, static_cast<int>(c.cap), c.nkv, c.hd);
+        encode_kv_tensor_map(&c.tv, c.v.p, static_cast<int>(c.cap), c.nkv, c.hd);
+        kv->local.push_back(std::move(c));
+    }
+    for (const auto& s : src.global) {
+        GlobalCache c;
+        c.nkv = s.nkv;
+        c.hd = s.hd;
+        c.capacity = s.capacity;
+        c.committed = s.committed;
+        if (c.capacity > 0) {
+            const size_t n = static_cast<size_t>(c.capacity) * c.nkv * c.hd;
+            c.k.reset(n);
+            c.v.reset(n);
+            HYB_CUDA(cudaMemcpyAsync(c.k.p, s.k.p, n * 2, cudaMemcpyDeviceToDevice, stream_));
+            HYB_CUDA(cudaMemcpyAsync(c.v.p, s.v.p, n * 2, cudaMemcpyDeviceToDevice, stream_));
+            encode_kv_tensor_map(&c.tk, c.k.p, static_cast<int>(c.capacity), c.nkv, c.hd);
+            encode_kv_tensor_map(&c.tv, c.v.p, static_cast<int>(c.capacity), c.nkv, c.hd);
+        }
+        kv->global.push_back(std::move(c));
+    }
+    kv->offset = src.offset;
+    kv->last_token = last_token;
     HYB_CUDA(cudaStreamSynchronize(stream_));
     return kv;
 }
@@ -953,6 +1008,237 @@ StepOut Model::decode_step(KvState& kv, std::vector<uint16_t>* logits_out) {
     kv.offset += 1;
     kv.last_token = o.token;
     return o;
+}
+
+void Model::ensure_batch_workspace(int n) {
+    if (n <= bws_.cap) return;
+    const Geometry& g = geo_;
+    int max_k = static_cast<int>(g.hidden);
+    for (const auto& L : layers_) max_k = std::max({max_k, L.q_rows, L.down.K});
+    const size_t BP = static_cast<size_t>(qmv_batch_pad(n));
+    bws_.x16.reset(BP * max_k / 2);
+    bws_.logits.reset(static_cast<size_t>(n) * vocab_local_);
+    bws_.topk_scratch.reset(static_cast<size_t>(n) * softcap_topk_scratch_floats(vocab_local_));
+    bws_.topk_idx.reset(static_cast<size_t>(n) * kTopkRowStride);
+    bws_.topk_val.reset(static_cast<size_t>(n) * kTopkRowStride);
+    bws_.cand.reset(static_cast<size_t>(4) * n * (1 + tp_size_));
+    bws_.seqs.reset(sizeof(DecodeSeq) * layers_.size() * n);
+    if (bws_.h_seqs) cudaFreeHost(bws_.h_seqs);
+    if (bws_.h_idx) cudaFreeHost(bws_.h_idx);
+    if (bws_.h_val) cudaFreeHost(bws_.h_val);
+    if (bws_.h_cand) cudaFreeHost(bws_.h_cand);
+    HYB_CUDA(cudaMallocHost(&bws_.h_seqs, sizeof(DecodeSeq) * layers_.size() * n));
+    HYB_CUDA(cudaMallocHost(&bws_.h_idx, sizeof(uint32_t) * kTopkRowStride * n));
+    HYB_CUDA(cudaMallocHost(&bws_.h_val, sizeof(float) * kTopkRowStride * n));
+    HYB_CUDA(cudaMallocHost(&bws_.h_cand, sizeof(uint32_t) * 4 * n * tp_size_));
+    bws_.cap = n;
+}
+
+void Model::decode_batch(KvState* const* kvs, int B, StepOut* outs) {
+    if (B < 1 || B > kMaxDecodeBatch) throw ArgError("decode batch: 1 to 64 sequences");
+    const Geometry& g = geo_;
+    const int H = static_cast<int>(g.hidden), I = inter_local_;
+    const int nh = heads_local_;
+    cudaStream_t st = stream_;
+    uint32_t max_pos = 0;
+    for (int b = 0; b < B; ++b) {
+        for (int c = 0; c < b; ++c)
+            if (kvs[c] == kvs[b]) throw ArgError("decode batch: a state appears twice");
+        if (kvs[b]->offset + 1 > 32768) throw std::runtime_error("decode beyond 32768 tokens is not supported");
+        max_pos = std::max(max_pos, kvs[b]->offset);
+    }
+    ensure_workspace(B, std::min<uint32_t>(max_pos + 1, 32768));
+    ensure_batch_workspace(B);
+    for (int b = 0; b < B; ++b) {
+        reserve(*kvs[b], 1);
+        ws_.h_ids[b] = kvs[b]->last_token;
+    }
+    // every layer's attention descriptors, staged in one copy
+    DecodeSeq* hs = bws_.h_seqs;
+    const DecodeSeq* dseq = reinterpret_cast<const DecodeSeq*>(bws_.seqs.p);
+    std::vector<int> keys_max(g.n_layers, 0);
+    {
+        std::vector<size_t> li(B, 0), gi(B, 0);
+        for (uint32_t layer = 0; layer < g.n_layers; ++layer) {
+            const LayerW& W = layers_[layer];
+            const int qkv_ld = W.q_rows + W.k_rows + W.v_rows;
+            for (int b = 0; b < B; ++b) {
+                KvState& kv = *kvs[b];
+                DecodeSeq& d = hs[static_cast<size_t>(layer) * B + b];
+                const uint32_t pos = kv.offset;
+                d.qkv = ws_.qkv.p + static_cast<size_t>(b) * qkv_ld;
+                d.out = ws_.attn.p + static_cast<size_t>(b) * W.q_rows;
+                d.pos = static_cast<int>(pos);
+                if (W.kind == LayerKind::Sliding) {
+                    LocalCache& c = kv.local[li[b]++];
+                    d.tk = c.tk;
+                    d.tv = c.tv;
+                    d.k_cache = c.k.p;
+                    d.v_cache = c.v.p;
+                    d.cap = static_cast<int>(c.cap);
+                    d.n_keys = static_cast<int>(std::min(g.window, pos + 1));  // forward.cc:55-57
+                } else {
+                    GlobalCache& c = kv.global[gi[b]++];
+                    if (c.capacity < pos + 1) throw std::runtime_error("global cache not reserved");
+                    d.tk = c.tk;
+                    d.tv = c.tv;
+                    d.k_cache = c.k.p;
+                    d.v_cache = c.v.p;
+                    d.cap = static_cast<int>(c.capacity);
+                    d.n_keys = static_cast<int>(pos + 1);
+                }
+                keys_max[layer] = std::max(keys_max[layer], d.n_keys);
+            }
+        }
+    }
+    HYB_CUDA(cudaMemcpyAsync(bws_.seqs.p, hs, sizeof(DecodeSeq) * g.n_layers * B, cudaMemcpyHostToDevice, st));
+    HYB_CUDA(cudaMemcpyAsync(ws_.ids.p, ws_.h_ids, sizeof(uint32_t) * B, cudaMemcpyHostToDevice, st));
+
+    // one projection for the whole batch: activations to fp16 pairs, then the packed qmv
+    auto proj = [&](const bf16* x, int ldx, int K, const void* packed, int N, bf16* y, int ldy, bool geglu) {
+        launch_qmv_batched_x16(x, B, ldx, K, bws_.x16.p, st);
+        QmvBatchParams q;
+        q.x16 = bws_.x16.p;
+        q.packed = packed;
+        q.y = y;
+        q.K = K;
+        q.N = N;
+        q.B = B;
+        q.ldy = ldy;
+        q.geglu = geglu;
+        launch_qmv_batched(q, st);
+    };
+    bf16* h_cur = ws_.h_a.p;
+    bf16* h_alt = ws_.h_b.p;
+    launch_embed(ws_.ids.p, B, embed_.w.p, embed_.s.p, embed_.b.p, H, embed_scale_, h_cur, st);
+    launch_rms_norm(h_cur, layers_[0].in_ln.p, ws_.xn.p, B, H, g.eps, st);
+    for (uint32_t layer = 0; layer < g.n_layers; ++layer) {
+        LayerW& W = layers_[layer];
+        const int qkv_ld = W.q_rows + W.k_rows + W.v_rows;
+        proj(ws_.xn.p, H, H, W.qkv.packed.p, qkv_ld, ws_.qkv.p, qkv_ld, false);
+        // QK-norm + RoPE + cache append + attention of every sequence in one launch
+        DecodeFusedParams ap;
+        ap.v_from_k = W.v_rows == 0;
+        ap.q_norm = W.q_norm.p;
+        ap.k_norm = W.k_norm.p;
+        ap.inv_freq = W.inv_freq;
+        ap.eps = g.eps;
+        ap.n_heads = nh;
+        ap.n_kv = W.nkv;
+        ap.hd = W.hd;
+        ap.rounding = attn_rounding_;
+        ap.seqs = dseq + static_cast<size_t>(layer) * B;
+        ap.n_seq = B;
+        if (decode_attn_fused_fits(nh, W.nkv, W.hd, keys_max[layer])) {
+            launch_decode_attn_fused_batch(ap, keys_max[layer], st, false);
+        } else {
+            // contexts beyond one cluster's shared memory: per sequence, separate
+            // norm/RoPE/append and split-K attention
+            for (int b = 0; b < B; ++b) {
+                const DecodeSeq& d = hs[static_cast<size_t>(layer) * B + b];
+                QkvPostParams qp;
+                qp.qkv = d.qkv;
+                qp.L = 1;
+                qp.ld = qkv_ld;
+                qp.n_heads = nh;
+                qp.n_kv = W.nkv;
+                qp.hd = W.hd;
+                qp.v_from_k = ap.v_from_k;
+                qp.q_norm = W.q_norm.p;
+                qp.k_norm = W.k_norm.p;
+                qp.inv_freq = W.inv_freq;
+                qp.pos0 = d.pos;
+                qp.eps = g.eps;
+                qp.q_out = ws_.q.p;
+                qp.k_cache = d.k_cache;
+                qp.v_cache = d.v_cache;
+                qp.cache_cap = d.cap;
+                launch_qkv_post(qp, st);
+                DecodeAttnParams dp;
+                dp.q = ws_.q.p;
+                dp.k_cache = d.k_cache;
+                dp.v_cache = d.v_cache;
+                dp.out = d.out;
+                dp.n_heads = nh;
+                dp.n_kv = W.nkv;
+                dp.hd = W.hd;
+                dp.cap = d.cap;
+                dp.last_pos = d.pos;
+                dp.n_keys = d.n_keys;
+                dp.rounding = attn_rounding_;
+                dp.scratch = ws_.attn_scratch.p;
+                dp.scratch_bytes = ws_.attn_scratch_bytes;
+                launch_decode_attn(dp, st);
+            }
+        }
+        proj(ws_.attn.p, W.q_rows, W.o.K, W.o.packed.p, H, ws_.o.p, H, false);
+        tp_.all_reduce_sum_bf16(ws_.o.p, static_cast<size_t>(B) * H, st);  // row-parallel o_proj
+        launch_resid_norm(ws_.o.p, W.post_attn.p, h_cur, nullptr, h_alt, W.pre_ff.p, ws_.xn.p, B, H, g.eps, st);
+        proj(ws_.xn.p, H, H, W.gateup.packed.p, W.gateup.N, ws_.act.p, I, true);
+        proj(ws_.act.p, I, W.down.K, W.down.packed.p, H, ws_.dn.p, H, false);
+        tp_.all_reduce_sum_bf16(ws_.dn.p, static_cast<size_t>(B) * H, st);  // row-parallel down_proj
+        const bf16* next_w = (layer + 1 < g.n_layers) ? layers_[layer + 1].in_ln.p : final_norm_.p;
+        launch_resid_norm(ws_.dn.p, W.post_ff.p, h_alt, W.scalar.p, h_cur, next_w, ws_.xn.p, B, H, g.eps, st);
+    }
+    // lm_head over this rank's vocabulary rows, soft-cap and top-2 per sequence
+    proj(ws_.xn.p, H, H, lm_packed_.p, vocab_local_, bws_.logits.p, vocab_local_, false);
+    launch_softcap_topk_rows(bws_.logits.p, B, vocab_local_, vocab_local_, g.softcap, bws_.topk_scratch.p,
+                             bws_.topk_scratch.n, bws_.topk_idx.p, bws_.topk_val.p, st);
+    const int T = tp_size_;
+    if (T > 1) {
+        tp_candidates_rows_kernel<<<1, 64, 0, st>>>(bws_.topk_idx.p, bws_.topk_val.p, B, static_cast<uint32_t>(vocab0_),
+                                                     bws_.cand.p);
+        HYB_LAUNCH_CHECK("tp_candidates_rows_kernel");
+        tp_.all_gather_bytes(bws_.cand.p, bws_.cand.p + 4 * B, static_cast<size_t>(16) * B, st);
+        HYB_CUDA(cudaMemcpyAsync(bws_.h_cand, bws_.cand.p + 4 * B, static_cast<size_t>(16) * B * T,
+                                 cudaMemcpyDeviceToHost, st));
+    } else {
+        HYB_CUDA(cudaMemcpyAsync(bws_.h_idx, bws_.topk_idx.p, sizeof(uint32_t) * kTopkRowStride * B,
+                                 cudaMemcpyDeviceToHost, st));
+        HYB_CUDA(cudaMemcpyAsync(bws_.h_val, bws_.topk_val.p, sizeof(float) * kTopkRowStride * B,
+                                 cudaMemcpyDeviceToHost, st));
+    }
+    HYB_CUDA(cudaStreamSynchronize(st));
+    for (int b = 0; b < B; ++b) {
+        StepOut& out = outs[b];
+        out = StepOut{};
+        if (T > 1) {
+            // highest value first, lowest vocabulary index on ties (the TP = 1 order)
+            std::vector<std::pair<float, uint32_t>> c;
+            for (int r = 0; r < T; ++r)
+                for (int k = 0; k < 2; ++k) {
+                    const uint32_t* e = bws_.h_cand + (static_cast<size_t>(r) * B + b) * 4 + 2 * k;
+                    float v;
+                    std::memcpy(&v, e + 1, 4);
+                    c.emplace_back(v, e[0]);
+                }
+            std::sort(c.begin(), c.end(), [](const auto& x, const auto& y) {
+                return x.first > y.first || (x.first == y.first && x.second < y.second);
+            });
+            for (int i = 0; i < 2; ++i) {
+                out.topk_idx[i] = c[i].second;
+                out.topk_val[i] = c[i].first;
+            }
+        } else {
+            const int n = static_cast<int>(std::min<uint32_t>(2, g.vocab));
+            for (int i = 0; i < n; ++i) {
+                out.topk_idx[i] = bws_.h_idx[kTopkRowStride * b + i];
+                out.topk_val[i] = bws_.h_val[kTopkRowStride * b + i];
+            }
+            if (n < 2) out.topk_val[1] = -INFINITY;
+        }
+        out.token = out.topk_idx[0];
+        out.logit = out.topk_val[0];
+        out.near_tie = (out.logit - out.topk_val[1]) < 0.5f;
+        KvState& kv = *kvs[b];
+        size_t li = 0, gi = 0;
+        for (uint32_t layer = 0; layer < g.n_layers; ++layer) {
+            if (layers_[layer].kind == LayerKind::Sliding) kv.local[li++].committed = kv.offset + 1;
+            else kv.global[gi++].committed = kv.offset + 1;
+        }
+        kv.offset += 1;
+        kv.last_token = out.token;
+    }
 }
 
 }  // namespace hyb

@@ -124,6 +124,22 @@ struct Workspace {
     int h_ids_cap = 0;
 };
 
+// Buffers of a batched decode step (sized for the largest batch seen).
+struct BatchWorkspace {
+    int cap = 0;                       // sequences
+    DevPtr<uint32_t> x16;              // [pad(cap)][max K / 2] fp16 activation pairs
+    DevPtr<bf16> logits;               // [cap][vocab_local]
+    DevPtr<float> topk_scratch;
+    DevPtr<uint32_t> topk_idx;         // [cap][8]
+    DevPtr<float> topk_val;
+    DevPtr<uint32_t> cand;             // tensor parallel: [cap][4] own, then [TP][cap][4] gathered
+    DevPtr<unsigned char> seqs;        // [n_layers][cap] DecodeSeq of the attention launches
+    DecodeSeq* h_seqs = nullptr;       // pinned staging of `seqs`
+    uint32_t* h_idx = nullptr;         // pinned mirrors
+    float* h_val = nullptr;
+    uint32_t* h_cand = nullptr;
+};
+
 class Model {
   public:
     Model() = default;
@@ -141,6 +157,9 @@ class Model {
     int tp_size() const { return tp_size_; }
 
     std::unique_ptr<KvState> new_kv() const;
+    // A copy of `src` (every cache, cursor and commit count) whose next input token is
+    // `last_token`.
+    std::unique_ptr<KvState> clone_kv(const KvState& src, uint32_t last_token) const;
     // Grow global caches so that `n_tokens` more tokens fit (reference
     // plan_kv_growth / GlobalKvCache::append semantics: 256-token steps).
     void reserve(KvState& kv, uint32_t n_tokens) const;
@@ -149,6 +168,10 @@ class Model {
     StepOut prefill(KvState& kv, const uint32_t* tokens, uint32_t count, std::vector<uint16_t>* logits_out);
     // One decode step at kv.offset from kv.last_token.
     StepOut decode_step(KvState& kv, std::vector<uint16_t>* logits_out);
+    // One greedy decode step of `n` independent sequences together (each at its own
+    // offset, from its own last_token): one weight stream per projection for the whole
+    // batch. Writes outs[0..n); each state advances by one token.
+    void decode_batch(KvState* const* kvs, int n, StepOut* outs);
 
     // Attention rounding: 0 = MLX CPU-stream semantics (bf16 scores and
     // probabilities, the default), 1 = fp32 scores/probabilities (MLX's fused
@@ -188,6 +211,8 @@ class Model {
     bf16 embed_scale_{};
     int attn_rounding_ = 0;
     Workspace ws_;
+    BatchWorkspace bws_;
+    void ensure_batch_workspace(int n);
     // tensor parallelism (tp_size_ == 1: everything local)
     TpComm tp_;
     int tp_rank_ = 0, tp_size_ = 1;

@@ -56,6 +56,23 @@ void launch_qmv_pack(const uint32_t* w, const bf16* s, const bf16* b, int K, int
                      cudaStream_t stream);
 void launch_qmv_packed(const QmvParams& p, cudaStream_t stream, bool pdl = false);
 
+// Batched decode qmv (qmv_batched.cu): B <= kMaxDecodeBatch sequences over the packed
+// layout, one weight stream for the whole batch. x16 is the activation batch converted by
+// launch_qmv_batched_x16 ([qmv_batch_pad(B)][K/2] u32); y is [B][ldy] (N/2 columns with
+// the GeGLU epilogue over the interleaved gate/up matrix).
+constexpr int kMaxDecodeBatch = 64;
+struct QmvBatchParams {
+    const uint32_t* x16 = nullptr;
+    const void* packed = nullptr;
+    bf16* y = nullptr;
+    int K = 0, N = 0, B = 0, ldy = 0;
+    bool geglu = false;
+};
+int qmv_batch_pad(int B);
+void launch_qmv_batched_x16(const bf16* x, int B, int ldx, int K, uint32_t* x16, cudaStream_t stream);
+void launch_qmv_batched(const QmvBatchParams& p, cudaStream_t stream, bool pdl = false);
+int64_t read_qmvb_wait_timeouts();
+
 // Prefill GEMM for M >= 2 (tensor cores; fp16 operands, fp32 accumulation).
 // Prefill qmm on tcgen05 tensor cores with TMEM accumulators (qmm_tc.cu): 128x256 output
 // tiles, f16 operands dequantised in shared memory, fp32 accumulation.
@@ -122,6 +139,11 @@ void launch_gather_ring(const bf16* cache, int cap, int pos0, int n, int row_ele
 void launch_softcap_topk(bf16* logits, int N, float cap, float* scratch, int scratch_floats,
                          uint32_t* out_idx, float* out_val, cudaStream_t stream);
 int softcap_topk_scratch_floats(int N);
+// The same over `rows` rows of a [rows][ld] logits batch: the winner and runner-up of row r
+// at out_* + kTopkRowStride * r; scratch of rows * softcap_topk_scratch_floats(N) floats.
+constexpr int kTopkRowStride = 8;
+void launch_softcap_topk_rows(bf16* logits, int rows, long long ld, int N, float cap, float* scratch,
+                              size_t scratch_floats, uint32_t* out_idx, float* out_val, cudaStream_t stream);
 
 // ---------------------------------------------------------------- attention
 // Decode (one query token): q [H, hd]; caches [cap, Hkv, hd]; keys are the last
@@ -152,6 +174,17 @@ size_t decode_attn_noalloc_limit_bytes();
 // row qkv (q | k | v, or q | k with v_from_k) it normalises and rotates q and the new
 // k, normalises the new v, appends k/v at slot pos % cap, and attends over the
 // n_keys positions pos - n_keys + 1 .. pos. One thread-block cluster per KV head.
+// One sequence of a batched fused decode attention launch (device memory, 64-byte
+// aligned array; the tensor maps are read by TMA from there).
+struct alignas(64) DecodeSeq {
+    CUtensorMap tk, tv;       // encode_kv_tensor_map of k_cache / v_cache
+    const bf16* qkv = nullptr;  // this sequence's projection row
+    bf16* out = nullptr;        // [n_heads, hd]
+    bf16* k_cache = nullptr;
+    bf16* v_cache = nullptr;
+    int cap = 0, pos = 0, n_keys = 0, pad = 0;
+};
+
 struct DecodeFusedParams {
     const bf16* qkv = nullptr;
     bool v_from_k = false;
@@ -173,6 +206,10 @@ struct DecodeFusedParams {
     // encoded per launch when null.
     const CUtensorMap* tmap_k = nullptr;
     const CUtensorMap* tmap_v = nullptr;
+    // Batched launch (launch_decode_attn_fused_batch): per-sequence fields of n_seq
+    // sequences on the device; qkv/out/caches/cap/pos/n_keys/tensor maps above unused.
+    const DecodeSeq* seqs = nullptr;
+    int n_seq = 0;
 };
 // Tiled TMA tensor map (rank <= 5): dims innermost first, strides in bytes for dims
 // 1..rank-1, box in elements; no interleave, zero fill out of bounds (tma_host.cu).
@@ -186,6 +223,9 @@ void encode_kv_tensor_map(CUtensorMap* map, const bf16* cache, int cap, int n_kv
 void launch_decode_attn_fused(const DecodeFusedParams& p, cudaStream_t stream, bool pdl = false);
 // Whether the fused kernel's shared-memory plan holds n_keys scores (else use the
 // split-K path above).
+// Batched fused decode attention: one launch over `seqs` (device array of n_seq, built by
+// the caller) sharing layer weights and shapes; n_keys_max sizes the shared-memory plan.
+void launch_decode_attn_fused_batch(const DecodeFusedParams& p, int n_keys_max, cudaStream_t stream, bool pdl);
 bool decode_attn_fused_fits(int n_heads, int n_kv, int hd, int n_keys);
 
 // Bounded mbarrier waits that gave up on the current device (never expected):

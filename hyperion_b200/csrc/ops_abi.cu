@@ -140,6 +140,33 @@ HypStatus hyb_qmv_packed(const void* x, const void* packed, void* y, int64_t K, 
     });
 }
 
+HypStatus hyb_qmv_batched(const void* x, int32_t B, int64_t ldx, const void* packed, void* y, int64_t ldy, int64_t K,
+                          int64_t N, int32_t geglu, void* stream) {
+    if (!x || !packed || !y) return hyb::abi_fail(HYP_STATUS_INVALID_ARGUMENT, "null pointer argument");
+    if (B < 1 || B > hyb::kMaxDecodeBatch) return hyb::abi_fail(HYP_STATUS_INVALID_ARGUMENT, "qmv_batched: batch must be 1..64");
+    if (K <= 0 || K % 64 != 0 || N <= 0 || K > (1 << 20) || N > (1 << 30) || ldx < K || ldy < (geglu ? N / 2 : N))
+        return hyb::abi_fail(HYP_STATUS_INVALID_ARGUMENT, "qmv_batched: bad shape");
+    if (geglu && N % 32 != 0) return hyb::abi_fail(HYP_STATUS_INVALID_ARGUMENT, "qmv_batched: GeGLU rows must be a multiple of 32");
+    return run([&] {
+        cudaStream_t st = as_stream(stream);
+        void* x16 = nullptr;
+        HYB_CUDA(cudaMallocAsync(&x16, static_cast<size_t>(hyb::qmv_batch_pad(B)) * K * 2, st));
+        hyb::launch_qmv_batched_x16(static_cast<const hyb::bf16*>(x), B, static_cast<int>(ldx), static_cast<int>(K),
+                                    static_cast<uint32_t*>(x16), st);
+        hyb::QmvBatchParams q;
+        q.x16 = static_cast<const uint32_t*>(x16);
+        q.packed = packed;
+        q.y = static_cast<hyb::bf16*>(y);
+        q.K = static_cast<int>(K);
+        q.N = static_cast<int>(N);
+        q.B = B;
+        q.ldy = static_cast<int>(ldy);
+        q.geglu = geglu != 0;
+        hyb::launch_qmv_batched(q, st);
+        HYB_CUDA(cudaFreeAsync(x16, st));
+    });
+}
+
 size_t hyb_sdpa_decode_scratch_bytes(int32_t n_heads, int32_t n_kv, int32_t head_dim, int32_t max_keys) {
     if (n_heads <= 0 || n_kv <= 0 || head_dim <= 0 || max_keys <= 0) return 0;
     return hyb::decode_attn_scratch_bytes(n_heads, n_kv, head_dim, max_keys);
@@ -318,7 +345,10 @@ HypStatus hyb_qkv_post(const void* qkv, int32_t L, int32_t ld, int32_t n_heads, 
 
 HypStatus hyb_wait_timeouts(int64_t* count) {
     if (!count) return hyb::abi_fail(HYP_STATUS_INVALID_ARGUMENT, "count is null");
-    return run([&] { *count = hyb::read_qmv_wait_timeouts() + hyb::read_attn_wait_timeouts() + hyb::read_qmm_wait_timeouts(); });
+    return run([&] {
+        *count = hyb::read_qmv_wait_timeouts() + hyb::read_qmvb_wait_timeouts() + hyb::read_attn_wait_timeouts() +
+                 hyb::read_qmm_wait_timeouts();
+    });
 }
 
 }  // extern "C"

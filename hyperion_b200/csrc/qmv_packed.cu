@@ -19,6 +19,7 @@
 //   A warp's reads of one chunk index are 32 consecutive 16-byte words, so the
 //   shared-memory reads are conflict-free, and each item is a single bulk copy.
 #include "kernels.h"
+#include "qmv_pack.cuh"
 #include "tma.cuh"
 
 #include <algorithm>
@@ -37,28 +38,7 @@ constexpr int kWarps = 8;
 constexpr int kThreads = kWarps * 32;
 constexpr int kStages = 2;
 constexpr int kCtasPerSm = 2;
-constexpr int kItemMax = 32 * 144;  // 4608 bytes
 constexpr int kMaxPrologueK = 8192; // norm prologues hold K/8 16-byte chunks in registers
-
-struct PackGeo {
-    int K, N, G, nunits, nrb;
-    int gc_last, tv_last, item_last;  // last unit's group count, valid t count, bytes
-    long long rb_bytes;               // bytes of one 16-row block
-};
-
-__host__ __device__ inline PackGeo pack_geo(int K, int N) {
-    PackGeo p;
-    p.K = K;
-    p.N = N;
-    p.G = K / 64;
-    p.nunits = (p.G + 7) / 8;
-    p.nrb = (N + 15) / 16;
-    p.gc_last = p.G - 8 * (p.nunits - 1);
-    p.tv_last = (p.gc_last + 1) / 2;
-    p.item_last = 8 * p.tv_last * 144;
-    p.rb_bytes = static_cast<long long>(p.nunits - 1) * kItemMax + p.item_last;
-    return p;
-}
 
 // Bounded wait on an mbarrier phase: gives up (and records it) instead of hanging.
 __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t phase) {
@@ -75,20 +55,6 @@ __device__ __forceinline__ float block_sum(float v, float* tmp) {
     __syncthreads();
     float r = (lane < kWarps) ? tmp[lane] : 0.f;
     return warp_sum(r);
-}
-
-__device__ __forceinline__ float gelu_tanh_bf16ops(float x) {
-    const float kC = 0.044677734375f;  // bf16(0.044715)
-    const float kK = 0.796875f;        // bf16(sqrt(2/pi))
-    float x2 = rbf(x * x);
-    float x3 = rbf(x * x2);
-    float in = rbf(kC * x3);
-    in = rbf(in + x);
-    in = rbf(kK * in);
-    float th = rbf(tanhf(in));
-    float hx = rbf(0.5f * x);
-    float op = rbf(1.0f + th);
-    return rbf(hx * op);
 }
 
 // The input vector into shared memory: x (or its norm prologue) as the permuted
@@ -284,10 +250,6 @@ __device__ __forceinline__ void qmv_item(const unsigned char* st, const uint32_t
 // GEGLU: the interleaved gate/up matrix alternates 16-row gate blocks (even) and the
 // matching up blocks (odd); a CTA processes them as one pair so the epilogue can
 // combine them. BG = row blocks per work group.
-// Named barrier over `count` threads (a team of warps); id 0 is __syncthreads.
-__device__ __forceinline__ void team_sync(int id, int count) {
-    asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
-}
 
 // Work split: the CTA's 8 warps form teams of `team` warps (1, 2, 4 or 8). A team
 // owns whole work groups (one 16-row block, or a gate/up block pair for GEGLU) and

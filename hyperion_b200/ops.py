@@ -66,6 +66,16 @@ def qmv_packed(x, packed, K, N, prologue=0, epilogue=0, norm_w=None, resid=None,
     return out
 
 
+def qmv_batched(x, packed, K, N, geglu=False, out=None, stream=None):
+    """Batched decode qmv over packed weights: x [B, K] bf16 -> [B, N] (or [B, N/2] with GeGLU)."""
+    B = x.shape[0]
+    if out is None:
+        out = torch.empty((B, N // 2 if geglu else N), dtype=torch.bfloat16, device=x.device)
+    check(lib().hyb_qmv_batched(_p(x), B, x.stride(0), _p(packed), _p(out), out.stride(0), K, N, 1 if geglu else 0,
+                                _stream(stream)))
+    return out
+
+
 class DecodeScratch:
     """Device workspace for hyb_sdpa_decode (zeroed once)."""
 

@@ -223,6 +223,32 @@ HypStatus hyb_model_load_synthetic(HypModel model, const HypGeometryParams* geom
  */
 HypStatus hyb_model_set_attention_rounding(HypModel model, int32_t mode);
 
+/*
+ * Batched decode qmv: y[b] = x[b] · Wᵀ for b < B (1..64) over packed weights
+ * (hyb_qmv_pack), one weight stream for the batch. x is bf16 [B][ldx], y bf16 [B][ldy];
+ * geglu != 0 applies the GeGLU epilogue of the interleaved gate/up matrix (N/2 outputs).
+ * The codes are dequantised to fp16 (s·q + b, exact when b = −8s) and multiplied with
+ * fp16 activations on the tensor cores in fp32.
+ */
+HypStatus hyb_qmv_batched(const void* x, int32_t B, int64_t ldx, const void* packed, void* y, int64_t ldy, int64_t K,
+                          int64_t N, int32_t geglu, void* stream);
+
+/*
+ * A new KV state holding a copy of src (caches, position, commit counts) whose next
+ * input token is last_token (UINT32_MAX keeps src's). Free it with hyp_kvstate_free.
+ */
+HypStatus hyb_kvstate_clone(HypModel model, HypKvState src, uint32_t last_token, HypKvState* out);
+
+/*
+ * Batched decode: one greedy step of n (1..64) distinct, populated KV states of the same
+ * model in a single pass over the weights. Each state advances by one token from its own
+ * last token; tokens_out[i] (and, when logits_out is not NULL, logits_out[i], the
+ * post-softcap logit of that token) receive state i's result. Same validation as
+ * hyp_decode_block; a failure after the step starts poisons every state of the batch.
+ */
+HypStatus hyb_decode_batch(HypModel model, const HypKvState* kvstates, uint32_t n, uint32_t* tokens_out,
+                           float* logits_out);
+
 /* The CUDA stream the model's kernels run on (for event timing). */
 HypStatus hyb_model_stream(HypModel model, void** out_stream);
 

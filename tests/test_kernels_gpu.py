@@ -275,6 +275,37 @@ def test_qmv_packed_fused(built_lib, oracle_lib, K, N, prologue, epilogue, with_
     assert np.array_equal(host(h1), host(h2))
 
 
+@pytest.mark.parametrize("K,N,B,geglu", [
+    (256, 1024, 3, False), (3840, 8192, 9, False), (15360, 3840, 16, False), (3840, 30720, 5, True),
+    (576, 40, 33, False), (256, 2048, 64, True), (5376, 1024, 64, False), (128, 17, 1, False)])
+def test_qmv_batched(built_lib, oracle_lib, K, N, B, geglu):
+    """The batched decode qmv (fp16 dequantised codes x fp16 activations on the tensor
+    cores) against the oracle's exact sum, every row of the batch; ragged units and row
+    counts included. fp16 dequantisation is exact for these b = -8s weights."""
+    from hyperion_b200 import ops
+    from oracle import gemma_oracle as go
+    import torch
+    rng = np.random.default_rng(K + 5 * N + B)
+    w, s, b = random_q4(rng, N, K)
+    x = f32_to_bf16_bits(rng.standard_normal((B, K), dtype=np.float32))
+    packed = ops.qmv_pack(dev(w), dev(s), dev(b))
+    got = host(ops.qmv_batched(dev(x), packed, K, N, geglu=geglu))
+    torch.cuda.synchronize()
+    if not geglu:
+        want = go.qmm(x, w, s, b)
+    else:
+        t = np.arange(N // 32)
+        gate_rows = (32 * t[:, None] + np.arange(16)[None, :]).reshape(-1)
+        up_rows = gate_rows + 16
+        g = go.qmm(x, w[gate_rows], s[gate_rows], b[gate_rows])
+        u = go.qmm(x, w[up_rows], s[up_rows], b[up_rows])
+        want = go.bf(go.fl(go.gelu_tanh(g)) * go.fl(u))
+    assert got.shape == want.shape
+    for r in range(B):
+        assert rel_l2(got[r], want[r]) <= (REL_L2_QMM if want.shape[1] >= 256 else 1e-3), r
+        assert within_one_ulp(got[r], want[r]) >= 0.999, r
+
+
 @pytest.mark.parametrize("H,Hkv,hd,cap,pos,n_keys,v_from_k,proportional", [
     (16, 8, 256, 1032, 2999, 1024, False, False),   # cfg3 sliding, wrapped ring (8-CTA clusters)
     (16, 8, 256, 4352, 4099, 4100, True, True),     # cfg3 global
