@@ -6,7 +6,10 @@
 // RoPE, :459-468 cache append, :474-495 cache read, :498-504 SDPA).
 //
 // Each cluster of CS CTAs (CS <= 8, portable) owns one KV head and its REP query
-// heads; CTA rank c owns a contiguous slice of the n_keys cache positions. The
+// heads (of one sequence: a batched launch adds gridDim.z = sequences and reads each
+// sequence's caches, position and tensor maps from a DecodeSeq array; CS then shrinks
+// to keep about two CTAs per SM); CTA rank c owns a contiguous slice of the n_keys
+// cache positions. The
 // slice's K rows and then its V rows stream through a ring of shared-memory tiles
 // of 64 consecutive cache slots of this KV head: HD/64 tensor-map TMA boxes of
 // [64 slots][64 dims] with the 128-byte swizzle, so the tensor-core fragment loads
@@ -534,26 +537,32 @@ struct FusedPlan {
     size_t smem = 0;
 };
 
-FusedPlan plan_fused(int hd, int rep, int n_keys) {
-    FusedPlan f;
-    f.cs = std::min(kMaxCluster, std::max(1, (n_keys + 127) / 128));
-    f.chunk = (n_keys + f.cs - 1) / f.cs;
-    f.cs = (n_keys + f.chunk - 1) / f.chunk;
-    const int tile = kTileKeys * hd * 2;
-    // up to 128 KB of tiles in flight; +1 for a possible split at the ring wrap
-    const int items = 2 * ((f.chunk + kTileKeys - 1) / kTileKeys + 1);
-    for (int s = std::min({kMaxStages, items, kRingBytes / tile}); s >= 1; --s) {
-        f.stages = s;
-        f.smem = fused_layout(hd, rep, f.chunk, s).total + 1024;  // + alignment slack
-        if (f.smem <= kSmemLimit) return f;
+// `units` = independent (KV head, sequence) pairs of the launch. A cluster splits a
+// pair's keys over up to 8 CTAs (128 keys or more each) only while the launch has fewer
+// than two CTAs per SM; a batch of many sequences runs one CTA per pair. A plan whose
+// scores do not fit in shared memory takes more CTAs per cluster.
+FusedPlan plan_fused(int hd, int rep, int n_keys, int units) {
+    const int want = std::max(1, (2 * num_sms() + units - 1) / units);
+    int cs0 = std::min({kMaxCluster, std::max(1, (n_keys + 127) / 128), want});
+    for (int cs = cs0; cs <= kMaxCluster; ++cs) {
+        FusedPlan f;
+        f.chunk = (n_keys + cs - 1) / cs;
+        f.cs = (n_keys + f.chunk - 1) / f.chunk;
+        const int tile = kTileKeys * hd * 2;
+        // up to 128 KB of tiles in flight; +1 for a possible split at the ring wrap
+        const int items = 2 * ((f.chunk + kTileKeys - 1) / kTileKeys + 1);
+        for (int s = std::min({kMaxStages, items, kRingBytes / tile}); s >= 1; --s) {
+            f.stages = s;
+            f.smem = fused_layout(hd, rep, f.chunk, s).total + 1024;  // + alignment slack
+            if (f.smem <= kSmemLimit) return f;
+        }
     }
-    f.stages = 0;
-    return f;
+    return FusedPlan{};
 }
 
 template <int PER, int REP, int ROUND>
 void launch_fused_t(const DecodeFusedParams& p, cudaStream_t stream, bool pdl) {
-    const FusedPlan f = plan_fused(PER * 32, REP, p.n_keys);
+    const FusedPlan f = plan_fused(PER * 32, REP, p.n_keys, p.n_kv * (p.seqs ? p.n_seq : 1));
     if (f.stages == 0) throw ArgError("decode attention: too many keys for the shared-memory plan");
     auto kern = decode_attn_fused_kernel<PER, REP, ROUND>;
     static int attr_dev = -1;
@@ -625,7 +634,7 @@ bool decode_attn_fused_fits(int n_heads, int n_kv, int hd, int n_keys) {
     if (n_kv <= 0 || n_heads % n_kv != 0 || (hd != 64 && hd != 128 && hd != 256) || n_keys <= 0) return false;
     const int rep = n_heads / n_kv;
     if (rep != 1 && rep != 2 && rep != 4 && rep != 8) return false;
-    return plan_fused(hd, rep, n_keys).stages > 0;
+    return plan_fused(hd, rep, n_keys, n_kv).stages > 0;
 }
 
 void launch_decode_attn_fused(const DecodeFusedParams& p, cudaStream_t stream, bool pdl) {

@@ -96,6 +96,70 @@ __global__ void resid_norm_kernel(const bf16* __restrict__ x, const bf16* __rest
     }
 }
 
+// The same with every operand in registers: each thread issues its 16-byte loads of x,
+// resid, post_w and next_w at once (C chunks of 8 elements, D = 8 * chunks <= 2048 C),
+// so a row costs one memory round trip plus two block reductions. Same rounding points.
+template <int C>
+__global__ void __launch_bounds__(256) resid_norm_vec_kernel(const bf16* __restrict__ x, const bf16* __restrict__ post_w,
+                                                             const bf16* resid, const bf16* __restrict__ scalar,
+                                                             bf16* out_h, const bf16* __restrict__ next_w,
+                                                             bf16* __restrict__ out_n, int D, float eps) {
+    __shared__ float sh[32];
+    const size_t off = static_cast<size_t>(blockIdx.x) * D;
+    const int nch = D / 8;
+    const uint4 z = make_uint4(0, 0, 0, 0);
+    uint4 xv[C], rv[C], pv[C], nv[C];
+#pragma unroll
+    for (int c = 0; c < C; ++c) {
+        const int j = threadIdx.x + 256 * c;
+        const bool ok = j < nch;
+        xv[c] = ok ? reinterpret_cast<const uint4*>(x + off)[j] : z;
+        rv[c] = ok ? reinterpret_cast<const uint4*>(resid + off)[j] : z;
+        pv[c] = ok ? reinterpret_cast<const uint4*>(post_w)[j] : z;
+        nv[c] = (ok && next_w) ? reinterpret_cast<const uint4*>(next_w)[j] : z;
+    }
+    auto el = [](const uint4& v, int e) {  // element e (0..7) of a 16-byte chunk
+        const uint32_t w = e < 2 ? v.x : e < 4 ? v.y : e < 6 ? v.z : v.w;
+        return __uint_as_float((e & 1) ? (w & 0xFFFF0000u) : (w << 16));
+    };
+    float ss = 0.f;
+#pragma unroll
+    for (int c = 0; c < C; ++c)
+#pragma unroll
+        for (int e = 0; e < 8; ++e) ss += el(xv[c], e) * el(xv[c], e);
+    const float inv = 1.0f / sqrtf(block_reduce_sum(ss, sh) / static_cast<float>(D) + eps);
+    const float sc = scalar ? bf2f(scalar[0]) : 1.f;
+    float hv[C][8];
+    float ss2 = 0.f;
+#pragma unroll
+    for (int c = 0; c < C; ++c)
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+            const float n = rbf(rbf(el(xv[c], e) * inv) * el(pv[c], e));
+            float h = rbf(el(rv[c], e) + n);
+            if (scalar) h = rbf(h * sc);
+            hv[c][e] = h;
+            ss2 += h * h;
+        }
+    const float inv2 = 1.0f / sqrtf(block_reduce_sum(ss2, sh) / static_cast<float>(D) + eps);
+#pragma unroll
+    for (int c = 0; c < C; ++c) {
+        const int j = threadIdx.x + 256 * c;
+        if (j >= nch) continue;
+        uint4 ho, no;
+        uint32_t* hw = &ho.x;
+        uint32_t* nw = &no.x;
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+            hw[q] = pack_bf2(f2bf(hv[c][2 * q]), f2bf(hv[c][2 * q + 1]));
+            nw[q] = pack_bf2(f2bf(rbf(hv[c][2 * q] * inv2) * el(nv[c], 2 * q)),
+                             f2bf(rbf(hv[c][2 * q + 1] * inv2) * el(nv[c], 2 * q + 1)));
+        }
+        reinterpret_cast<uint4*>(out_h + off)[j] = ho;
+        if (next_w) reinterpret_cast<uint4*>(out_n + off)[j] = no;
+    }
+}
+
 // ------------------------------------------------------------------ GeGLU
 __device__ __forceinline__ float gelu_tanh_ops(float x) {
     const float kC = 0.044677734375f;  // bf16(0.044715)
@@ -351,6 +415,21 @@ void launch_rms_norm(const bf16* x, const bf16* w, bf16* out, int rows, int D, f
 void launch_resid_norm(const bf16* x, const bf16* post_w, const bf16* resid, const bf16* scalar, bf16* out_h,
                        const bf16* next_w, bf16* out_n, int rows, int D, float eps, cudaStream_t stream) {
     if (rows <= 0) return;
+    const bool vec = D % 8 == 0 && D <= 8 * 256 * 4 &&
+                     ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(post_w) |
+                       reinterpret_cast<uintptr_t>(resid) | reinterpret_cast<uintptr_t>(out_h) |
+                       reinterpret_cast<uintptr_t>(next_w) | reinterpret_cast<uintptr_t>(out_n)) & 15u) == 0;
+    if (vec) {
+        const int c = (D / 8 + 255) / 256;
+        switch (c) {
+            case 1: resid_norm_vec_kernel<1><<<rows, 256, 0, stream>>>(x, post_w, resid, scalar, out_h, next_w, out_n, D, eps); break;
+            case 2: resid_norm_vec_kernel<2><<<rows, 256, 0, stream>>>(x, post_w, resid, scalar, out_h, next_w, out_n, D, eps); break;
+            case 3: resid_norm_vec_kernel<3><<<rows, 256, 0, stream>>>(x, post_w, resid, scalar, out_h, next_w, out_n, D, eps); break;
+            default: resid_norm_vec_kernel<4><<<rows, 256, 0, stream>>>(x, post_w, resid, scalar, out_h, next_w, out_n, D, eps); break;
+        }
+        HYB_LAUNCH_CHECK("resid_norm_vec_kernel");
+        return;
+    }
     const size_t smem = static_cast<size_t>(D) * sizeof(float);
     if (smem > 48 * 1024) throw ArgError("resid_norm: hidden too large");
     resid_norm_kernel<<<rows, 256, smem, stream>>>(x, post_w, resid, scalar, out_h, next_w, out_n, D, eps);

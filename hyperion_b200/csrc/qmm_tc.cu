@@ -18,6 +18,9 @@
 //   warp 9       allocates 256 MT TMEM columns and issues, per stage, 4 MT
 //                tcgen05.mma.kind::f16 (M = 128, N = 256, K = 16) accumulating in
 //                TMEM; tcgen05.commit releases the stages and finally the accumulators.
+// Split-K (grid z): when the output tiles cannot fill the GPU (decode-sized M), slice z
+// takes k-blocks [z kper, (z + 1) kper) and writes fp32 partials, which a second kernel
+// sums in slice order (deterministic) into bf16.
 // Operand precision: f16 weights are exact for s*(q - 8) codes and within 2^-12
 // otherwise; bf16 weights would add ~2.3e-3 relative error, above the 2e-3 parity bound.
 // bf16 activations convert to f16 exactly inside f16's range (|x| < 65504).
@@ -117,7 +120,7 @@ template <int MT>
 __global__ void __launch_bounds__(kThreads, 1)
     qmm_tc_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_w,
                   const bf16* __restrict__ scales, const bf16* __restrict__ biases, bf16* __restrict__ y, int M,
-                  int K, int N) {
+                  int K, int N, int kper, float* __restrict__ part) {
     using P = Plan<MT>;
     constexpr int S = P::S;
     extern __shared__ unsigned char smem_dyn[];
@@ -125,7 +128,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t sbase = smem_u32(sm);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int m0 = blockIdx.x * kBM * MT, n0 = blockIdx.y * kBN;
-    const int nk = K / kBK;
+    const int k_first = static_cast<int>(blockIdx.z) * kper;       // this slice's k-blocks
+    const int nk = min(K / kBK - k_first, kper);                  // >= 1 by construction
     const int G = K / 64;
 
     const uint32_t tma_full = sbase + P::kOffBars;  // [S]: X blocks and W codes landed
@@ -166,9 +170,10 @@ __global__ void __launch_bounds__(kThreads, 1)
                 mbar_expect_tx(tma_full + 8 * s, MT * kXBytes + kWRawBytes);
 #pragma unroll
                 for (int mt = 0; mt < MT; ++mt)
-                    tma_load_2d(sbase + P::kOffA + (s * MT + mt) * kXBytes, &tm_x, kt * kBK, m0 + kBM * mt,
-                                tma_full + 8 * s);
-                tma_load_2d(sbase + P::kOffW + s * kWRawBytes, &tm_w, kt * (kBK / 8), n0, tma_full + 8 * s);
+                    tma_load_2d(sbase + P::kOffA + (s * MT + mt) * kXBytes, &tm_x, (k_first + kt) * kBK,
+                                m0 + kBM * mt, tma_full + 8 * s);
+                tma_load_2d(sbase + P::kOffW + s * kWRawBytes, &tm_w, (k_first + kt) * (kBK / 8), n0,
+                            tma_full + 8 * s);
             }
         }
     } else if (warp == kMmaWarp) {
@@ -197,8 +202,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int t = threadIdx.x;  // 0..255
         const int n = n0 + t;
         const bool row_ok = n < N;
-        const bf16* srow = scales + static_cast<size_t>(row_ok ? n : 0) * G;
-        const bf16* brow = biases + static_cast<size_t>(row_ok ? n : 0) * G;
+        const bf16* srow = scales + static_cast<size_t>(row_ok ? n : 0) * G + k_first;
+        const bf16* brow = biases + static_cast<size_t>(row_ok ? n : 0) * G + k_first;
         // scale/bias ring: slot (kt mod 4) holds stage kt, loaded three stages ahead
         float sr[4] = {0.f, 0.f, 0.f, 0.f}, br[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
@@ -255,7 +260,18 @@ __global__ void __launch_bounds__(kThreads, 1)
                                        static_cast<uint32_t>(kBN * mt + col),
                                    rr);
                 tmem_ld_wait();
-                if (m < M) {
+                if (m < M && part) {
+                    float* dst = part + (static_cast<size_t>(blockIdx.z) * M + m) * N + n0 + col;
+                    if (n0 + col + 32 <= N && (N % 4) == 0) {
+#pragma unroll
+                        for (int v = 0; v < 8; ++v)
+                            *reinterpret_cast<uint4*>(dst + 4 * v) =
+                                make_uint4(rr[4 * v], rr[4 * v + 1], rr[4 * v + 2], rr[4 * v + 3]);
+                    } else {
+                        for (int v = 0; v < 32; ++v)
+                            if (n0 + col + v < N) dst[v] = __uint_as_float(rr[v]);
+                    }
+                } else if (m < M) {
                     bf16* dst = y + static_cast<size_t>(m) * N + n0 + col;
                     if (n0 + col + 32 <= N && (N % 8) == 0) {
 #pragma unroll
@@ -288,9 +304,33 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
 }
 
+// y[m][n] = bf16(sum over slices z of part[z][m][n]), in slice order.
+__global__ void splitk_reduce_kernel(const float* __restrict__ part, int splits, size_t mn, bf16* __restrict__ y) {
+    for (size_t i = (blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x) * 4; i < mn;
+         i += static_cast<size_t>(gridDim.x) * blockDim.x * 4) {
+        if (i + 4 <= mn && (mn & 3) == 0) {  // every slice's row of 4 stays 16-byte aligned
+            float4 a = *reinterpret_cast<const float4*>(part + i);
+            for (int z = 1; z < splits; ++z) {
+                const float4 v = *reinterpret_cast<const float4*>(part + z * mn + i);
+                a.x += v.x;
+                a.y += v.y;
+                a.z += v.z;
+                a.w += v.w;
+            }
+            *reinterpret_cast<uint2*>(y + i) = make_uint2(pack_bf2(f2bf(a.x), f2bf(a.y)), pack_bf2(f2bf(a.z), f2bf(a.w)));
+        } else {
+            for (size_t j = i; j < mn && j < i + 4; ++j) {
+                float a = part[j];
+                for (int z = 1; z < splits; ++z) a += part[z * mn + j];
+                y[j] = f2bf(a);
+            }
+        }
+    }
+}
+
 template <int MT>
 void launch_tc(const CUtensorMap& tx, const CUtensorMap& tw, const bf16* s, const bf16* b, bf16* y, int M, int K,
-               int N, cudaStream_t stream) {
+               int N, int splits, int kper, float* part, cudaStream_t stream) {
     static int attr_dev = -1;
     int dev = 0;
     HYB_CUDA(cudaGetDevice(&dev));
@@ -298,8 +338,8 @@ void launch_tc(const CUtensorMap& tx, const CUtensorMap& tw, const bf16* s, cons
         HYB_CUDA(cudaFuncSetAttribute(qmm_tc_kernel<MT>, cudaFuncAttributeMaxDynamicSharedMemorySize, Plan<MT>::kSmem));
         attr_dev = dev;
     }
-    const dim3 grid((M + kBM * MT - 1) / (kBM * MT), (N + kBN - 1) / kBN);
-    qmm_tc_kernel<MT><<<grid, kThreads, Plan<MT>::kSmem, stream>>>(tx, tw, s, b, y, M, K, N);
+    const dim3 grid((M + kBM * MT - 1) / (kBM * MT), (N + kBN - 1) / kBN, splits);
+    qmm_tc_kernel<MT><<<grid, kThreads, Plan<MT>::kSmem, stream>>>(tx, tw, s, b, y, M, K, N, kper, part);
     HYB_LAUNCH_CHECK("qmm_tc_kernel");
 }
 
@@ -337,8 +377,27 @@ void launch_qmm_tc(const bf16* x, const uint32_t* w, const bf16* s, const bf16* 
     }
     // two 128-token blocks per CTA once there are enough tiles to fill the GPU
     const long long tiles2 = static_cast<long long>((M + 255) / 256) * ((N + kBN - 1) / kBN);
-    if (tiles2 >= num_sms()) launch_tc<2>(tx, tw, s, b, y, M, K, N, stream);
-    else launch_tc<1>(tx, tw, s, b, y, M, K, N, stream);
+    const long long tiles1 = static_cast<long long>((M + kBM - 1) / kBM) * ((N + kBN - 1) / kBN);
+    const int nk = K / kBK;
+    if (tiles2 >= num_sms()) {
+        launch_tc<2>(tx, tw, s, b, y, M, K, N, 1, nk, nullptr, stream);
+    } else if (tiles1 >= num_sms() || nk < 8) {
+        launch_tc<1>(tx, tw, s, b, y, M, K, N, 1, nk, nullptr, stream);
+    } else {
+        // split K so that about two CTAs per SM work, each slice at least 4 k-blocks
+        int splits = static_cast<int>(std::min<long long>(nk / 4, (2LL * num_sms() + tiles1 - 1) / tiles1));
+        splits = std::max(splits, 1);
+        const int kper = (nk + splits - 1) / splits;
+        splits = (nk + kper - 1) / kper;  // no empty slice
+        const size_t mn = static_cast<size_t>(M) * N;
+        float* part = nullptr;
+        HYB_CUDA(cudaMallocAsync(reinterpret_cast<void**>(&part), mn * splits * sizeof(float), stream));
+        launch_tc<1>(tx, tw, s, b, y, M, K, N, splits, kper, part, stream);
+        const int rgrid = static_cast<int>(std::min<size_t>((mn / 4 + 255) / 256 + 1, 8 * static_cast<size_t>(num_sms())));
+        splitk_reduce_kernel<<<rgrid, 256, 0, stream>>>(part, splits, mn, y);
+        HYB_LAUNCH_CHECK("splitk_reduce_kernel");
+        HYB_CUDA(cudaFreeAsync(part, stream));
+    }
     HYB_CUDA(cudaFreeAsync(xh, stream));
 }
 

@@ -59,8 +59,10 @@ def test_qmv_ragged_shapes(built_lib, oracle_lib, K, N):
     assert within_one_ulp(y, want) >= 0.999
 
 
+# small M x N tiles split K over grid z (fp32 partials summed in slice order): (17, 3840, 256),
+# (130, 15360, 128), (64, 4096, 200), (5, 1024, 1001) (ragged rows, scalar reduce), (64, 21504, 5376)
 @pytest.mark.parametrize("M,K,N", [(2, 256, 64), (17, 3840, 256), (130, 15360, 128), (512, 3840, 320),
-                                   (2048, 256, 384), (64, 4096, 200)])
+                                   (2048, 256, 384), (64, 4096, 200), (5, 1024, 1001), (64, 21504, 5376)])
 def test_qmm_prefill_shapes(built_lib, oracle_lib, M, K, N):
     y, want = _qmm_case(M, K, N, seed=M * 31 + K + N)
     assert rel_l2(y, want) <= REL_L2_QMM
