@@ -562,6 +562,16 @@ void launch_decode_attn_noalloc(DecodeAttnParams p, cudaStream_t stream) {
 void launch_prefill_attn(const PrefillAttnParams& p, cudaStream_t stream) {
     if (p.Lq <= 0) return;
     if (p.n_kv <= 0 || p.n_heads % p.n_kv != 0) throw ArgError("prefill attention: bad head counts");
+    if (prefill_attn_tc_supported(p)) {
+        launch_prefill_attn_tc(p, stream);
+        return;
+    }
+    launch_prefill_attn_mma(p, stream);
+}
+
+void launch_prefill_attn_mma(const PrefillAttnParams& p, cudaStream_t stream) {
+    if (p.Lq <= 0) return;
+    if (p.n_kv <= 0 || p.n_heads % p.n_kv != 0) throw ArgError("prefill attention: bad head counts");
     switch (p.hd) {
         case 64: launch_prefill_t<64>(p, stream); break;
         case 128: launch_prefill_t<128>(p, stream); break;

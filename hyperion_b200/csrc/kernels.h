@@ -247,5 +247,11 @@ struct PrefillAttnParams {
     int rounding = 0;
 };
 void launch_prefill_attn(const PrefillAttnParams& p, cudaStream_t stream);
+// The tcgen05 version (attention_tc.cu), which launch_prefill_attn uses when it applies
+// (head_dim 64/128/256, 16-byte aligned operands); the mma.sync kernel otherwise.
+bool prefill_attn_tc_supported(const PrefillAttnParams& p);
+void launch_prefill_attn_tc(const PrefillAttnParams& p, cudaStream_t stream);
+void launch_prefill_attn_mma(const PrefillAttnParams& p, cudaStream_t stream);
+int64_t read_attn_tc_wait_timeouts();
 
 }  // namespace hyb

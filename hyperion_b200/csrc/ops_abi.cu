@@ -347,7 +347,7 @@ HypStatus hyb_wait_timeouts(int64_t* count) {
     if (!count) return hyb::abi_fail(HYP_STATUS_INVALID_ARGUMENT, "count is null");
     return run([&] {
         *count = hyb::read_qmv_wait_timeouts() + hyb::read_qmvb_wait_timeouts() + hyb::read_attn_wait_timeouts() +
-                 hyb::read_qmm_wait_timeouts();
+                 hyb::read_attn_tc_wait_timeouts() + hyb::read_qmm_wait_timeouts();
     });
 }
 

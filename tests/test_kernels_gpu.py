@@ -123,6 +123,10 @@ def test_sdpa_decode(built_lib, oracle_lib, H, Hkv, hd, cap, last_pos, n_keys, s
     (200, 200, 32, 16, 128, 0, 0, 0, 1 / 11.3),  # cfg4 global
     (77, 77, 4, 1, 128, 0, 0, 0, 0.09),          # GQA 4, ragged
     (64, 64, 4, 2, 64, 0, 0, 8, 0.125),          # window 8
+    (1024, 1024, 16, 8, 256, 0, 0, 1024, 1 / 16.0),  # cfg2 local: 8 query tiles x 16 key blocks
+    (700, 700, 16, 8, 256, 0, 0, 0, 1 / 16.0),       # cfg2 global, ragged last tiles
+    (130, 2178, 8, 4, 128, 2048, 0, 0, 0.088),       # chunk after a 2048-token prefix (global)
+    (1, 1, 2, 1, 256, 0, 0, 0, 0.0625),              # one key: out = v
 ])
 def test_sdpa_prefill(built_lib, oracle_lib, Lq, Lk, H, Hkv, hd, q_pos0, k_pos0, window, scale):
     from hyperion_b200 import ops
