@@ -537,7 +537,7 @@ def run_sdpa_prefill(args, rank, world, local):
                       "config": {"workload": f"cfg2 causal SDPA at M = {args.qmm_m}"},
                       "roofline": {"bound": "tensor", "achieved": round(value, 1), "peak": tf_peak, "unit": "TFLOP/s",
                                    "frac": round(value / tf_peak, 4), "traffic": None, "peak_source": src,
-                                   "kernel": "prefill_attn_kernel"},
+                                   "kernel": "prefill_attn_tc_kernel"},
                       "per_case": rows}), flush=True)
 
 

@@ -104,6 +104,14 @@ __device__ __forceinline__ void tmem_ld_32x32b_x16(uint32_t taddr, uint32_t (&r)
         : "memory");
 }
 
+// 2^x, flushing denormal results to zero (one MUFU operation): masked scores of -FLT_MAX
+// come out as exactly 0.
+__device__ __forceinline__ float ex2_ftz(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
 __device__ __forceinline__ void team_sync_n(int id, int count) {
     asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
 }
@@ -126,7 +134,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     unsigned char* sm = smem_dyn + ((1024 - (smem_u32(smem_dyn) & 1023)) & 1023);
     const uint32_t sbase = smem_u32(sm);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int q0 = blockIdx.x * kQRows, h = blockIdx.y;
+    // causal tiles grow with the query index: every head's longest tiles run first
+    // (grid x = heads varies fastest, y = query tiles from the last), a shorter tail wave
+    const int q0 = (gridDim.y - 1 - blockIdx.y) * kQRows, h = blockIdx.x;
     const int hk = h / (a.n_heads / a.n_kv);
     const int qrows = min(kQRows, a.Lq - q0);
 
@@ -295,11 +305,11 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
                 for (int i = 0; i < kQCols; ++i) mx = fmaxf(mx, s[i]);
                 if (mx == -FLT_MAX) continue;
-                const float ms = mx * kLog2e;
+                const float ms = mx * kLog2e;  // finite: some key of this quarter is visible
                 float acc = 0.f;
 #pragma unroll
-                for (int i = 0; i < kQCols; ++i) acc += s[i] == -FLT_MAX ? 0.f : exp2f(fmaf(s[i], kLog2e, -ms));
-                l = (m == -FLT_MAX ? 0.f : l * exp2f(fmaf(m, kLog2e, -ms))) + acc;
+                for (int i = 0; i < kQCols; ++i) acc += ex2_ftz(fmaf(s[i], kLog2e, -ms));  // masked: 0
+                l = (m == -FLT_MAX ? 0.f : l * ex2_ftz(fmaf(m, kLog2e, -ms))) + acc;
                 m = mx;
             }
             // ---- merge the four quarters of each row (in quarter order: the same on all)
@@ -314,12 +324,13 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
             for (int u = 0; u < 4; ++u) {
                 const float mu = stat[(u * kQRows + r) * 2], lu = stat[(u * kQRows + r) * 2 + 1];
-                if (lu > 0.f) L += lu * exp2f((mu - M) * kLog2e);
+                if (lu > 0.f) L += lu * ex2_ftz((mu - M) * kLog2e);
             }
             team_sync_n(1, kSoftThreads);  // every thread has read the statistics
             m = M;
             const float il = L > 0.f ? 1.0f / L : 0.f;
-            const float ms = m * kLog2e;
+            // rows without a visible key (padding rows past Lq) get p = 0 and are not stored
+            const float ms = L > 0.f ? m * kLog2e : 0.f;
             // ---- pass 2: probabilities into the P operand (this quarter's 16 keys = 2 chunks)
             for (int c = 0; c < nb; ++c, ++b) {
                 float s[kQCols];
@@ -335,8 +346,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
                     for (int q = 0; q < 4; ++q) {
                         const float s0 = s[8 * h2 + 2 * q], s1 = s[8 * h2 + 2 * q + 1];
-                        const float p0 = s0 == -FLT_MAX ? 0.f : exp2f(fmaf(s0, kLog2e, -ms)) * il;
-                        const float p1 = s1 == -FLT_MAX ? 0.f : exp2f(fmaf(s1, kLog2e, -ms)) * il;
+                        const float p0 = ex2_ftz(fmaf(s0, kLog2e, -ms)) * il;  // masked: 0
+                        const float p1 = ex2_ftz(fmaf(s1, kLog2e, -ms)) * il;
                         w[q] = pack_bf2(f2bf(p0), f2bf(p1));
                     }
                     const int ch = 2 * qq + h2;
@@ -415,7 +426,7 @@ void launch_tc_t(const PrefillAttnParams& p, cudaStream_t stream) {
         encode_tma(&tv, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, p.v, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
     }
     TcArgs a{p.Lq, p.Lk, p.n_heads, p.n_kv, p.q_pos0, p.k_pos0, p.window, p.scale, p.softcap, p.rounding, p.out};
-    dim3 grid((p.Lq + kQRows - 1) / kQRows, p.n_heads);
+    dim3 grid(p.n_heads, (p.Lq + kQRows - 1) / kQRows);
     prefill_attn_tc_kernel<HD><<<grid, kThreads, P::kSmem, stream>>>(tq, tk, tv, a);
     HYB_LAUNCH_CHECK("prefill_attn_tc_kernel");
 }
