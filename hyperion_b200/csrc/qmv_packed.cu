@@ -31,13 +31,14 @@ __device__ int g_qmv_wait_timeouts = 0;  // set if an mbarrier wait gave up (nev
 
 namespace {
 
-// Two CTAs per SM (16 warps, <= 128 registers, <= ~113 KB shared memory each) so
-// that latency is hidden across warps and the next kernel's CTAs can become
-// resident during this one's tail (programmatic dependent launch).
-constexpr int kWarps = 8;
+// One CTA of 16 warps per SM (<= 128 registers, <= ~184 KB shared memory): the work
+// splits per SM, so row-block counts that do not divide evenly cost at most one group
+// per SM (two 8-warp CTAs per SM left some SMs with both CTAs busy and others with one),
+// and the norm prologue runs once per SM.
+constexpr int kWarps = 16;
 constexpr int kThreads = kWarps * 32;
 constexpr int kStages = 2;
-constexpr int kCtasPerSm = 2;
+constexpr int kCtasPerSm = 1;
 constexpr int kMaxPrologueK = 8192; // norm prologues hold K/8 16-byte chunks in registers
 
 // Bounded wait on an mbarrier phase: gives up (and records it) instead of hanging.
@@ -281,11 +282,16 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) qmv_packed_kernel(const 
 
     const int W = team;
     const int tw = warp / W, wt = warp % W;  // team within the CTA, warp within the team
-    const int team_id = static_cast<int>(blockIdx.x) * (kWarps / W) + tw;
-    const int n_teams = static_cast<int>(gridDim.x) * (kWarps / W);
+    // Groups are dealt round-robin over the CTAs (one per SM), so every SM gets the same
+    // count within one: CTA b owns groups b, b + grid, b + 2 grid, ..., and its team tw
+    // takes every tpc-th of them starting at the tw-th.
+    const int tpc = kWarps / W;
+    const int grid = static_cast<int>(gridDim.x), cta = static_cast<int>(blockIdx.x);
     const int n_groups = (pg.nrb + BG - 1) / BG;
+    const int cta_groups = cta < n_groups ? (n_groups - cta + grid - 1) / grid : 0;
+    auto group_of = [=](int gi) { return cta + (tw + gi * tpc) * grid; };
     const int my_units = (wt < pg.nunits) ? (pg.nunits - wt + W - 1) / W : 0;
-    const int my_groups = (team_id < n_groups) ? (n_groups - team_id + n_teams - 1) / n_teams : 0;
+    const int my_groups = cta_groups > tw ? (cta_groups - tw + tpc - 1) / tpc : 0;
     const int per_group = BG * my_units;
     const int n_items = my_groups * per_group;
 
@@ -302,7 +308,7 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) qmv_packed_kernel(const 
     // warp's item order; advanced like an odometer (no divisions per item).
     int ig = 0, ij = 0, iu = 0, n_issued = 0;
     auto issue_next = [&]() {
-        const int rb = (team_id + ig * n_teams) * BG + ij;
+        const int rb = group_of(ig) * BG + ij;
         const int unit = wt + iu * W;
         const int s = n_issued % kStages;
         const uint32_t bar = my_bar0 + 8 * s;
@@ -339,7 +345,7 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) qmv_packed_kernel(const 
     int buf = 0, it = 0;
     float gate0 = 0.f, gate1 = 0.f;  // team = 1 GEGLU: this lane's gate rows g, g + 8
     for (int gi = 0; gi < my_groups; ++gi) {
-        const int grp = team_id + gi * n_teams;
+        const int grp = group_of(gi);
         for (int j = 0; j < BG; ++j) {
             const int rb = grp * BG + j;
             float acc0 = 0.f, acc1 = 0.f;
@@ -500,18 +506,19 @@ int choose_team(const QmvParams& p, int max_ctas, int* grid_needed) {
     const PackGeo pg = pack_geo(p.K, p.N);
     const bool geglu = p.epilogue == QmvEpilogue::kGeglu;
     const int groups = geglu ? (pg.nrb + 1) / 2 : pg.nrb;
+    // one CTA per SM at most, each with ceil(groups / grid) groups at most (round-robin)
+    const int grid = std::max(1, std::min(groups, max_ctas));
+    const int per_cta = (groups + grid - 1) / grid;
     int team = kWarps, best = 1 << 30;
     for (int w = kWarps; w >= 1; w /= 2) {
         const int tpc_w = kWarps / w;
-        const int n_teams = std::min((groups + tpc_w - 1) / tpc_w, max_ctas) * tpc_w;
-        const int load = (groups + n_teams - 1) / n_teams * (geglu ? 2 : 1) * ((pg.nunits + w - 1) / w);
+        const int load = (per_cta + tpc_w - 1) / tpc_w * (geglu ? 2 : 1) * ((pg.nunits + w - 1) / w);
         if (load <= best) {
             best = load;
             team = w;
         }
     }
-    const int tpc = kWarps / team;
-    *grid_needed = std::max(1, std::min((groups + tpc - 1) / tpc, max_ctas));
+    *grid_needed = grid;
     return team;
 }
 
