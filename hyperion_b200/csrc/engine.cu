@@ -748,6 +748,10 @@ StepOut Model::epilogue(const bf16* final_row, bool fused_prologue, const bf16* 
         p.scalar = last.scalar.p;
         p.norm_w = final_norm_.p;
         p.h_out = ws_.h_a.p;
+        if (tp_.active() && tp_.fused_ready()) {  // the last down_proj's all-reduce
+            p.ar_mode = 2;
+            p.ar = last_ar_;
+        }
     } else {
         p.x = final_row;
     }
@@ -844,6 +848,11 @@ void Model::decode_layers(KvState& kv) {
     cudaStream_t st = stream_;
     const uint32_t pos = kv.offset;  // position of the token being decoded
     launch_embed(ws_.ids.p, 1, embed_.w.p, embed_.s.p, embed_.b.p, H, embed_scale_, ws_.h_e.p, st);
+    // Tensor parallel over mapped NVLink peers: the all-reduces after o_proj and down_proj
+    // run inside the qmvs (the row-parallel one stores its rows to every rank, the next
+    // one's residual+norm prologue sums them); otherwise a separate all-reduce.
+    const bool fused_ar = tp_.active() && tp_.fused_ready();
+    QmvTpFuse dn_ar;  // the previous layer's down_proj all-reduce, consumed by the next qkv
     // qkv projection of `layer` with its input norm (and the previous layer's
     // post-MLP residual/scalar) fused into its prologue
     auto qkv_params = [&](uint32_t layer) {
@@ -869,6 +878,10 @@ void Model::decode_layers(KvState& kv) {
             p.post_w = P.post_ff.p;
             p.scalar = P.scalar.p;
             p.h_out = ws_.h_a.p;
+            if (fused_ar) {
+                p.ar_mode = 2;
+                p.ar = dn_ar;
+            }
         }
         return p;
     };
@@ -989,11 +1002,25 @@ void Model::decode_layers(KvState& kv) {
         pd.y = ws_.dn.p;
         pd.K = W.down.K;
         pd.N = H;
-        launch_qmv(po, st, true);
-        tp_.all_reduce_small_bf16(ws_.o.p, static_cast<size_t>(H), st, true);  // row-parallel o_proj
-        launch_qmv(pg, st, true);
-        launch_qmv(pd, st, true);
-        tp_.all_reduce_small_bf16(ws_.dn.p, static_cast<size_t>(H), st, true);  // row-parallel down_proj
+        if (fused_ar) {
+            po.ar_mode = 1;
+            po.ar = tp_.next_fused_ar(qmv_packed_grid(po));
+            pg.ar_mode = 2;
+            pg.ar = po.ar;
+            pd.ar_mode = 1;
+            launch_qmv(po, st, true);
+            launch_qmv(pg, st, true);
+            pd.ar = tp_.next_fused_ar(qmv_packed_grid(pd));
+            launch_qmv(pd, st, true);
+            dn_ar = pd.ar;
+            last_ar_ = pd.ar;
+        } else {
+            launch_qmv(po, st, true);
+            tp_.all_reduce_small_bf16(ws_.o.p, static_cast<size_t>(H), st, true);  // row-parallel o_proj
+            launch_qmv(pg, st, true);
+            launch_qmv(pd, st, true);
+            tp_.all_reduce_small_bf16(ws_.dn.p, static_cast<size_t>(H), st, true);  // row-parallel down_proj
+        }
     }
 }
 

@@ -222,6 +222,7 @@ class Model {
     int vocab_local_ = 0;   // lm_head rows on this rank, starting at vocab0_
     int vocab0_ = 0;
     DevPtr<unsigned char> lm_packed_;  // packed lm_head rows of this rank
+    QmvTpFuse last_ar_;                // the last decode layer's down_proj all-reduce (lm_head input)
 };
 
 }  // namespace hyb

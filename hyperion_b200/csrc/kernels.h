@@ -27,6 +27,23 @@ enum class QmvEpilogue : int {
     kGeglu = 1,   // rows are (gate, up) interleaved by 16-row tiles: y[n] = bf16(gelu(g) * u)
 };
 
+// Tensor-parallel all-reduce fused into the decode qmvs over NVLink peer memory. Every
+// rank's receive buffer (IPC-mapped into every process, own included): [2 sets][T
+// sources][max_count] bf16, then per-source arrival counters (u32). A row-parallel qmv
+// (ar_mode 1) stores its bf16 output rows into slot (set, me) of every rank and each CTA
+// adds 1 to counter[me] on every rank (release at system scope); the next qmv (ar_mode 2)
+// waits (bounded) until counter[src] >= target for every source, then uses
+// x = bf16(sum over sources in rank order) as its input: the same bits on every rank.
+struct QmvTpFuse {
+    unsigned char* peer[8] = {};
+    int T = 0, me = 0;
+    int set = 0;                // receive set of this all-reduce
+    unsigned target = 0;        // producer CTAs per source counted after this all-reduce
+    size_t max_count = 0;       // elements per (set, source) slot
+    size_t counters_off = 0;    // byte offset of the counters in a buffer
+    size_t err_off = 0;         // byte offset of the wait-error counter
+};
+
 struct QmvParams {
     const bf16* x = nullptr;          // [K] activation (or the branch output for kResidNorm)
     const uint32_t* w = nullptr;      // [N, K/8]
@@ -45,7 +62,13 @@ struct QmvParams {
     bf16* h_out = nullptr;            // [K] new residual, written by CTA 0
     float eps = 1e-6f;
     const void* packed = nullptr;     // packed resident layout (launch_qmv_packed); w/s/b unused then
+    // fused tensor-parallel all-reduce: 0 none, 1 produce (store rows to every rank),
+    // 2 consume (x = the all-reduced rows); packed path, K and N <= ar.max_count
+    int ar_mode = 0;
+    QmvTpFuse ar;
 };
+// CTAs launch_qmv_packed uses for `p` (the producer count of a fused all-reduce).
+int qmv_packed_grid(const QmvParams& p);
 
 void launch_qmv(const QmvParams& p, cudaStream_t stream, bool pdl = false);
 

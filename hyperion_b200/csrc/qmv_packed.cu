@@ -58,6 +58,76 @@ __device__ __forceinline__ float block_sum(float v, float* tmp) {
     return warp_sum(r);
 }
 
+// ---- fused tensor-parallel all-reduce (QmvTpFuse)
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
+    uint32_t v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+// Producer: output row `row` into slot (set, me) of every rank.
+__device__ __forceinline__ void ar_store(const QmvParams& p, int row, bf16 v) {
+    if (p.ar_mode != 1) return;
+    const size_t off = ((static_cast<size_t>(p.ar.set) * p.ar.T + p.ar.me) * p.ar.max_count + row) * 2;
+    for (int r = 0; r < p.ar.T; ++r) *reinterpret_cast<bf16*>(p.ar.peer[r] + off) = v;
+}
+
+// Producer, end of the CTA: its rows are stored; count it on every rank.
+__device__ __forceinline__ void ar_publish(const QmvParams& p) {
+    if (p.ar_mode != 1) return;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        __threadfence_system();
+        for (int r = 0; r < p.ar.T; ++r)
+            asm volatile("red.release.sys.global.add.u32 [%0], 1;" ::"l"(p.ar.peer[r] + p.ar.counters_off + 4 * p.ar.me)
+                         : "memory");
+    }
+}
+
+// Consumer: wait (bounded) until every source's producer CTAs have published.
+__device__ __forceinline__ void ar_wait(const QmvParams& p) {
+    if (threadIdx.x == 0) {
+        const unsigned char* mine = p.ar.peer[p.ar.me];
+        for (int src = 0; src < p.ar.T; ++src) {
+            const uint32_t* c = reinterpret_cast<const uint32_t*>(mine + p.ar.counters_off + 4 * src);
+            bool ok = false;
+            for (int it = 0; it < (1 << 22); ++it) {
+                if (static_cast<int32_t>(ld_acquire_sys(c) - p.ar.target) >= 0) {
+                    ok = true;
+                    break;
+                }
+                if (it > 32) __nanosleep(64);
+            }
+            if (!ok) atomicAdd(reinterpret_cast<int*>(p.ar.peer[p.ar.me] + p.ar.err_off), 1);
+        }
+    }
+    __syncthreads();
+}
+
+// Consumer: chunk j (8 elements) of the all-reduced vector, summed over sources in rank
+// order in fp32 and rounded to bf16 (read through L2: the peers wrote it over NVLink).
+__device__ __forceinline__ uint4 ar_chunk(const QmvParams& p, int j) {
+    const unsigned char* mine = p.ar.peer[p.ar.me];
+    float a[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    for (int src = 0; src < p.ar.T; ++src) {
+        const uint4 v = __ldcg(reinterpret_cast<const uint4*>(
+                                   mine + (static_cast<size_t>(p.ar.set) * p.ar.T + src) * p.ar.max_count * 2) +
+                               j);
+        const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+            a[2 * q] += __uint_as_float(w[q] << 16);
+            a[2 * q + 1] += __uint_as_float(w[q] & 0xFFFF0000u);
+        }
+    }
+    uint4 o;
+    o.x = pack_bf2(f2bf(a[0]), f2bf(a[1]));
+    o.y = pack_bf2(f2bf(a[2]), f2bf(a[3]));
+    o.z = pack_bf2(f2bf(a[4]), f2bf(a[5]));
+    o.w = pack_bf2(f2bf(a[6]), f2bf(a[7]));
+    return o;
+}
+
 // The input vector into shared memory: x (or its norm prologue) as the permuted
 // bf16 pairs the MMA B fragments read, and the per-group sums of x.
 __device__ __forceinline__ void stage_input(const QmvParams& p, uint32_t* xp, float* xsum, float* tmp) {
@@ -100,12 +170,14 @@ __device__ __forceinline__ void stage_input(const QmvParams& p, uint32_t* xp, fl
         const uint4* n4 = reinterpret_cast<const uint4*>(p.norm_w);
         const bool resid = p.prologue == QmvPrologue::kResidNorm;
         const uint64_t keep = l2_evict_last();  // norm weights: re-read every token
+        const bool ar = p.ar_mode == 2;
+        if (ar) ar_wait(p);
         uint4 xv[kMaxC], nv4[kMaxC], rv[kMaxC], pv[kMaxC];
 #pragma unroll
         for (int c = 0; c < kMaxC; ++c) {
             const int j = static_cast<int>(threadIdx.x) + c * kThreads;
             const uint4 z = make_uint4(0, 0, 0, 0);
-            xv[c] = j < nch ? ld(x4 + j) : z;
+            xv[c] = j < nch ? (ar ? ar_chunk(p, j) : ld(x4 + j)) : z;
             nv4[c] = j < nch ? ld_v4_hint(n4 + j, keep) : z;
             rv[c] = (resid && j < nch) ? ld(reinterpret_cast<const uint4*>(p.resid) + j) : z;
             pv[c] = (resid && j < nch) ? ld_v4_hint(reinterpret_cast<const uint4*>(p.post_w) + j, keep) : z;
@@ -377,8 +449,14 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) qmv_packed_kernel(const 
                 // the warp holds the whole sums: lane (g, 0) has rows g and g + 8
                 if (t == 0) {
                     if (!GEGLU) {
-                        if (rb * 16 + g < pg.N) p.y[rb * 16 + g] = f2bf(acc0);
-                        if (rb * 16 + g + 8 < pg.N) p.y[rb * 16 + g + 8] = f2bf(acc1);
+                        if (rb * 16 + g < pg.N) {
+                            p.y[rb * 16 + g] = f2bf(acc0);
+                            ar_store(p, rb * 16 + g, f2bf(acc0));
+                        }
+                        if (rb * 16 + g + 8 < pg.N) {
+                            p.y[rb * 16 + g + 8] = f2bf(acc1);
+                            ar_store(p, rb * 16 + g + 8, f2bf(acc1));
+                        }
                     } else if (j == 0) {
                         gate0 = acc0;
                         gate1 = acc1;
@@ -401,7 +479,10 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) qmv_packed_kernel(const 
                 float* pb = pairbuf + tw * 32;
                 if (!GEGLU) {
                     const int row = rb * 16 + lane;
-                    if (row < pg.N) p.y[row] = f2bf(v);
+                    if (row < pg.N) {
+                        p.y[row] = f2bf(v);
+                        ar_store(p, row, f2bf(v));
+                    }
                 } else {
                     pb[j * 16 + lane] = v;  // j = 0 gate rows, j = 1 up rows
                     if (j == 1) {
@@ -414,6 +495,7 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) qmv_packed_kernel(const 
             buf ^= 1;
         }
     }
+    ar_publish(p);
 }
 
 __global__ void qmv_pack_kernel(const uint32_t* __restrict__ w, const bf16* __restrict__ s,
@@ -524,8 +606,22 @@ int choose_team(const QmvParams& p, int max_ctas, int* grid_needed) {
 
 }  // namespace
 
+int qmv_packed_grid(const QmvParams& p) {
+    int grid = 1;
+    choose_team(p, kCtasPerSm * num_sms(), &grid);
+    return grid;
+}
+
 void launch_qmv_packed(const QmvParams& p, cudaStream_t stream, bool pdl) {
     check_packed_stage(p);
+    if (p.ar_mode != 0) {
+        const bool ok_mode = (p.ar_mode == 1 && p.epilogue == QmvEpilogue::kStore &&
+                              static_cast<size_t>(p.N) <= p.ar.max_count) ||
+                             (p.ar_mode == 2 && p.prologue == QmvPrologue::kResidNorm &&
+                              static_cast<size_t>(p.K) <= p.ar.max_count);
+        if (!ok_mode || p.ar.T < 2 || p.ar.T > 8 || p.ar.me < 0 || p.ar.me >= p.ar.T)
+            throw ArgError("qmv_packed: unsupported fused all-reduce");
+    }
     const size_t smem = packed_smem_bytes(p.K, p.prologue != QmvPrologue::kNone);
     int dev = 0;
     HYB_CUDA(cudaGetDevice(&dev));

@@ -5,6 +5,7 @@
 #pragma once
 
 #include "common.cuh"
+#include "kernels.h"
 
 #include <nccl.h>
 
@@ -40,6 +41,12 @@ class TpComm {
     // Number of flag waits that gave up since the last call (then resets it); a wait that
     // gives up leaves that step's result undefined but never hangs the GPU.
     int take_wait_errors(cudaStream_t stream);
+    // Fused all-reduce in the decode qmvs (QmvTpFuse): available once setup_p2p mapped the
+    // peers' buffers. next_fused_ar(ctas) describes the next all-reduce of up to the
+    // set-up count, produced by a qmv of `ctas` CTAs (every rank calls it in the same order
+    // with the same counts, so the receive set and the cumulative target agree).
+    bool fused_ready() const { return p2p_local_ != nullptr; }
+    QmvTpFuse next_fused_ar(int producer_ctas);
     // Rank r's `bytes` land at recv + r * bytes on every rank.
     void all_gather_bytes(const void* send, void* recv, size_t bytes, cudaStream_t stream);
 
@@ -51,6 +58,8 @@ class TpComm {
     void* p2p_peer_[8] = {};
     size_t p2p_max_ = 0;
     uint32_t epoch_ = 0;
+    uint32_t ar_seq_ = 0, ar_total_ = 0;  // fused all-reduces issued, producer CTAs counted
+    size_t counters_off() const { return (2 * static_cast<size_t>(size_) * p2p_max_ * 2 + 4 * static_cast<size_t>(size_) + 4 + 15) / 16 * 16; }
 };
 
 }  // namespace hyb
