@@ -130,6 +130,7 @@ __device__ __forceinline__ uint4 ar_chunk(const QmvParams& p, int j) {
 
 // The input vector into shared memory: x (or its norm prologue) as the permuted
 // bf16 pairs the MMA B fragments read, and the per-group sums of x.
+template <bool AR>
 __device__ __forceinline__ void stage_input(const QmvParams& p, uint32_t* xp, float* xsum, float* tmp) {
     auto ld = [](const uint4* a) { return *a; };
     const int K = p.K;
@@ -170,7 +171,7 @@ __device__ __forceinline__ void stage_input(const QmvParams& p, uint32_t* xp, fl
         const uint4* n4 = reinterpret_cast<const uint4*>(p.norm_w);
         const bool resid = p.prologue == QmvPrologue::kResidNorm;
         const uint64_t keep = l2_evict_last();  // norm weights: re-read every token
-        const bool ar = p.ar_mode == 2;
+        const bool ar = AR && p.ar_mode == 2;
         if (ar) ar_wait(p);
         uint4 xv[kMaxC], nv4[kMaxC], rv[kMaxC], pv[kMaxC];
 #pragma unroll
@@ -329,7 +330,8 @@ __device__ __forceinline__ void qmv_item(const unsigned char* st, const uint32_t
 // splits their K units among its warps; only the team synchronises, on its own
 // named barrier, to sum the warps' partials. With team = 1 warps run fully
 // independently, which keeps their bulk-copy rings streaming on large N.
-template <bool GEGLU>
+// AR: the fused tensor-parallel all-reduce paths are compiled in (tensor-parallel launches only).
+template <bool GEGLU, bool AR>
 __global__ void __launch_bounds__(kThreads, kCtasPerSm) qmv_packed_kernel(const QmvParams p, int team) {
     constexpr int BG = GEGLU ? 2 : 1;
     extern __shared__ __align__(128) unsigned char smem_raw[];
@@ -410,7 +412,7 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) qmv_packed_kernel(const 
 
     pdl_wait();
     if (threadIdx.x < 32) zero_page[threadIdx.x] = 0u;
-    stage_input(p, xp, xsum, tmp);
+    stage_input<AR>(p, xp, xsum, tmp);
     __syncthreads();
 
     uint32_t phase_bits = 0;  // one parity bit per stage
@@ -451,11 +453,11 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) qmv_packed_kernel(const 
                     if (!GEGLU) {
                         if (rb * 16 + g < pg.N) {
                             p.y[rb * 16 + g] = f2bf(acc0);
-                            ar_store(p, rb * 16 + g, f2bf(acc0));
+                            if (AR) ar_store(p, rb * 16 + g, f2bf(acc0));
                         }
                         if (rb * 16 + g + 8 < pg.N) {
                             p.y[rb * 16 + g + 8] = f2bf(acc1);
-                            ar_store(p, rb * 16 + g + 8, f2bf(acc1));
+                            if (AR) ar_store(p, rb * 16 + g + 8, f2bf(acc1));
                         }
                     } else if (j == 0) {
                         gate0 = acc0;
@@ -481,7 +483,7 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) qmv_packed_kernel(const 
                     const int row = rb * 16 + lane;
                     if (row < pg.N) {
                         p.y[row] = f2bf(v);
-                        ar_store(p, row, f2bf(v));
+                        if (AR) ar_store(p, row, f2bf(v));
                     }
                 } else {
                     pb[j * 16 + lane] = v;  // j = 0 gate rows, j = 1 up rows
@@ -495,7 +497,7 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) qmv_packed_kernel(const 
             buf ^= 1;
         }
     }
-    ar_publish(p);
+    if (AR) ar_publish(p);
 }
 
 __global__ void qmv_pack_kernel(const uint32_t* __restrict__ w, const bf16* __restrict__ s,
@@ -627,8 +629,10 @@ void launch_qmv_packed(const QmvParams& p, cudaStream_t stream, bool pdl) {
     HYB_CUDA(cudaGetDevice(&dev));
     static int attr_dev = -1;
     if (attr_dev != dev) {
-        HYB_CUDA(cudaFuncSetAttribute(qmv_packed_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024));
-        HYB_CUDA(cudaFuncSetAttribute(qmv_packed_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024));
+        HYB_CUDA(cudaFuncSetAttribute(qmv_packed_kernel<false, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024));
+        HYB_CUDA(cudaFuncSetAttribute(qmv_packed_kernel<true, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024));
+        HYB_CUDA(cudaFuncSetAttribute(qmv_packed_kernel<false, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024));
+        HYB_CUDA(cudaFuncSetAttribute(qmv_packed_kernel<true, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024));
         attr_dev = dev;
     }
     int grid = 1;
@@ -643,8 +647,11 @@ void launch_qmv_packed(const QmvParams& p, cudaStream_t stream, bool pdl) {
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = pdl ? 1 : 0;
-    if (p.epilogue == QmvEpilogue::kGeglu) HYB_CUDA(cudaLaunchKernelEx(&cfg, qmv_packed_kernel<true>, p, team));
-    else HYB_CUDA(cudaLaunchKernelEx(&cfg, qmv_packed_kernel<false>, p, team));
+    const bool geglu = p.epilogue == QmvEpilogue::kGeglu, ar = p.ar_mode != 0;
+    if (geglu && ar) HYB_CUDA(cudaLaunchKernelEx(&cfg, qmv_packed_kernel<true, true>, p, team));
+    else if (geglu) HYB_CUDA(cudaLaunchKernelEx(&cfg, qmv_packed_kernel<true, false>, p, team));
+    else if (ar) HYB_CUDA(cudaLaunchKernelEx(&cfg, qmv_packed_kernel<false, true>, p, team));
+    else HYB_CUDA(cudaLaunchKernelEx(&cfg, qmv_packed_kernel<false, false>, p, team));
 }
 
 int64_t read_qmv_wait_timeouts() {
