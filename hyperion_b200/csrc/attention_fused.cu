@@ -30,8 +30,9 @@
 //            tile; s = bf16(s * scale) into shared memory; each warp reduces
 //            (max, sum of exp) over its own keys; the CTA's pair is pushed into every
 //            CTA of the cluster (remote stores);
-//   cluster barrier; each warp forms the row's (M, L) from the pushed pairs in rank
-//            order and turns its own scores into p = bf16(exp(s - M) / L);
+//   cluster barrier; each warp merges the pushed pairs into the row's (M, L) with a
+//            fixed shuffle tree (the same on every CTA) and turns its own scores into
+//            p = bf16(exp(s - M) / L);
 //   phase 2  O = P V with mma.sync: warp w owns head_dim columns [w HD/8, (w+1) HD/8)
 //            over all keys (bf16 p is exact in rounding mode 0; mode 1 adds the
 //            bf16 residual p - bf16(p) as a second product); each output element's
@@ -92,6 +93,24 @@ __device__ __forceinline__ void dsmem_st(uint32_t addr, float v) {
 
 __device__ __forceinline__ void dsmem_st2(uint32_t addr, float a, float b) {
     asm volatile("st.shared::cluster.v2.f32 [%0], {%1, %2};" ::"r"(addr), "f"(a), "f"(b) : "memory");
+}
+
+// e^x as one MUFU operation on log2(e)-scaled arguments, flushing denormal results to zero.
+__device__ __forceinline__ float exp_fast(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x * 1.4426950408889634f));
+    return y;
+}
+
+// (max, sum of exp relative to the max) over the lanes of one 8-lane group: `m` and `l` are
+// one entry per lane (l = 0: empty); every lane of the group gets the merged pair.
+__device__ __forceinline__ void merge8(float m, float l, float& M, float& L) {
+    M = l > 0.f ? m : -FLT_MAX;
+#pragma unroll
+    for (int o = 1; o < 8; o <<= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
+    L = l > 0.f ? l * exp_fast(m - M) : 0.f;
+#pragma unroll
+    for (int o = 1; o < 8; o <<= 1) L += __shfl_xor_sync(0xffffffffu, L, o);
 }
 
 __device__ __forceinline__ float score_round(float dot, float scale, float cap, int rounding) {
@@ -197,7 +216,7 @@ __device__ __forceinline__ uint32_t tile_off(int r, int c) {
 }
 
 template <int PER, int REP, int ROUND>
-__global__ void __launch_bounds__(kThreads) decode_attn_fused_kernel(const DecodeFusedParams p, int chunk,
+__global__ void __launch_bounds__(kThreads, 1) decode_attn_fused_kernel(const DecodeFusedParams p, int chunk,
                                                                      int stages,
                                                                      const __grid_constant__ CUtensorMap tmk,
                                                                      const __grid_constant__ CUtensorMap tmv) {
@@ -401,7 +420,7 @@ __global__ void __launch_bounds__(kThreads) decode_attn_fused_kernel(const Decod
         float l = 0.f;
         for (int i = lane; i < my_count; i += 32) {
             const int k = my_key(i);
-            if (k >= 0) l += expf(s_sc[h * chunk + k] - m);
+            if (k >= 0) l += exp_fast(s_sc[h * chunk + k] - m);
         }
         l = warp_sum(l);
         if (lane == 0) {
@@ -412,40 +431,29 @@ __global__ void __launch_bounds__(kThreads) decode_attn_fused_kernel(const Decod
     __syncthreads();
     // every CTA of the cluster has started: its shared memory may now be written
     cluster_wait();
-    if (static_cast<int>(threadIdx.x) < CS * REP) {
-        const int c = threadIdx.x / REP, h = threadIdx.x % REP;
-        float M = -FLT_MAX;
-        for (int w = 0; w < kWarps; ++w)
-            if (wml[(w * REP + h) * 2 + 1] > 0.f) M = fmaxf(M, wml[(w * REP + h) * 2]);
-        float L = 0.f;
-        for (int w = 0; w < kWarps; ++w) {
-            const float lw = wml[(w * REP + h) * 2 + 1];
-            if (lw > 0.f) L += lw * expf(wml[(w * REP + h) * 2] - M);
-        }
-        dsmem_st2(dsmem_addr(&allml[(rank * REP + h) * 2], c), M, L);
+    // warp h merges head h's (max, sum) over the 8 warps (lanes 0..7, shuffle tree) and
+    // lanes c < CS push the CTA's pair into CTA c
+    if (warp < REP) {
+        const int h = warp, w = lane & 7;
+        float M, L;
+        merge8(wml[(w * REP + h) * 2], wml[(w * REP + h) * 2 + 1], M, L);
+        if (lane < CS) dsmem_st2(dsmem_addr(&allml[(rank * REP + h) * 2], lane), M, L);
     }
     cluster_sync();
     // ---- row statistics (lane h < REP), then p in place over this warp's keys
     {
-        float Ml = 0.f, iLl = 0.f;
-        if (lane < REP) {
-            float M = -FLT_MAX;
-            for (int c = 0; c < CS; ++c) M = fmaxf(M, allml[(c * REP + lane) * 2]);
-            float L = 0.f;
-            for (int c = 0; c < CS; ++c) {
-                const float lc = allml[(c * REP + lane) * 2 + 1];
-                if (lc > 0.f) L += lc * expf(allml[(c * REP + lane) * 2] - M);
-            }
-            Ml = M;
-            iLl = 1.0f / L;
-        }
 #pragma unroll
         for (int h = 0; h < REP; ++h) {
-            const float M = __shfl_sync(0xffffffffu, Ml, h), iL = __shfl_sync(0xffffffffu, iLl, h);
+            // lane c (< CS) holds CTA c's pair for head h; the shuffle tree merges them
+            const int c = lane & 7;
+            const bool has = c < CS;
+            float M, L;
+            merge8(has ? allml[(c * REP + h) * 2] : -FLT_MAX, has ? allml[(c * REP + h) * 2 + 1] : 0.f, M, L);
+            const float iL = 1.0f / L;
             for (int i = lane; i < my_count; i += 32) {
                 const int k = my_key(i);
                 if (k >= 0) {
-                    const float e = expf(s_sc[h * chunk + k] - M) * iL;
+                    const float e = exp_fast(s_sc[h * chunk + k] - M) * iL;
                     s_sc[h * chunk + k] = (ROUND == 0) ? rbf(e) : e;
                 }
             }
