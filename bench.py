@@ -13,7 +13,8 @@ time (GB/s). Per-shape figures are timed separately over >= 48 distinct copies.
 `--workload decode` times the engine's full 12B-shaped decode (config 3) through
 hyp_decode_block after a 4096-token prefill: tokens/s. `--workload attn-decode` times
 the fused decode attention alone over the model's 48 layer caches; `--workload
-qmv-shape` one qmv shape (both for profiling).
+qmv-shape` one qmv shape (both for profiling). `--workload spec-verify` times greedy
+speculative verify passes (hyb_verify) of 1/3/7 drafts beside a plain decode step.
 
 `--impl reference` times the CPU restatement of the same qmv (the reference's
 own path is MLX, unavailable here) on the host cores.
@@ -651,6 +652,72 @@ def run_decode(args, rank, world, local):
     print(json.dumps(line), flush=True)
 
 
+# ------------------------------------------------------------------ speculative verify
+def run_spec_verify(args, rank, world, local):
+    """Greedy speculative verify on the 12B-shaped model after a --ctx prefill: one pass
+    checks D draft tokens (D = 1, 3, 7 by default, --drafts) by running D + 1 rows through
+    the chunked forward and sampling every row (hyb_verify). Each pass is timed with CUDA
+    events on the engine stream beside a plain decode step of the same state; value = rows
+    per second of the largest D (the tokens/s speculative decoding reaches when every draft
+    is accepted)."""
+    import numpy as np
+    import torch
+    import hyperion_b200 as hb
+    from hyperion_b200.synth import config3
+    geo = config3()
+    eng = hb.Engine(geo, synthetic_seed=1 + rank)
+    ctx = args.ctx
+    rng = np.random.default_rng(5)
+    prompt = rng.integers(0, geo.vocab_size, ctx).tolist()
+    kv = eng.new_kv()
+    kv.prefill(prompt)
+    stream = torch.cuda.ExternalStream(eng.stream())
+    drafts = [int(d) for d in args.drafts.split(",")]
+
+    def timed(fn):
+        for _ in range(args.warmup):
+            fn()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
+        w0 = time.perf_counter()
+        e0.record(stream)
+        for _ in range(args.steps):
+            fn()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / args.steps, (time.perf_counter() - w0) * 1e3 / args.steps
+
+    with ClockSampler(local) as clk:
+        dec_ms, _ = timed(lambda: kv.decode(1))
+        per, wall = {}, {}
+        for d in drafts:
+            draws = [rng.integers(0, geo.vocab_size, d).tolist() for _ in range(args.warmup + args.steps)]
+            it = iter(draws)
+            per[d], wall[d] = timed(lambda: kv.verify(next(it)))
+    if rank != 0:
+        return
+    d = max(drafts)
+    rows_s = (d + 1) / (per[d] * 1e-3)
+    w_bytes = 48 * sum(qmv_bytes(K, N) for _, K, N in PROJ) + qmv_bytes(3840, 262144)
+    hbm, _, src = peaks()
+    print(json.dumps({
+        "metric": "speculative verify rows/s (12B-shaped, all drafts accepted)", "value": round(rows_s, 1),
+        "unit": "tok/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(per[d], 4),
+        "higher_is_better": True, "vs_baseline": None, "dtype": "u4/bf16->f32", "data": "synthetic",
+        "config": {"workload": f"cfg3 12B-shaped verify of {drafts} drafts at ctx ~{ctx}, batch 1",
+                   "decode_ms": round(dec_ms, 4),
+                   "verify_ms": {str(k): round(v, 4) for k, v in per.items()},
+                   "verify_wall_ms": {str(k): round(v, 4) for k, v in wall.items()},
+                   "speedup_at_full_acceptance": {str(k): round((k + 1) * dec_ms / v, 2) for k, v in per.items()},
+                   "l2": "inputs larger than L2"},
+        "roofline": {"bound": "hbm", "achieved": round(w_bytes / (per[d] * 1e-3) / 1e9, 1), "peak": hbm,
+                     "unit": "GB/s", "frac": round(w_bytes / (per[d] * 1e-3) / 1e9 / hbm, 4), "traffic": None,
+                     "peak_source": src, "kernel": "whole verify pass (weight bytes per pass)"},
+        "e2e": {"value": round((d + 1) / (wall[d] * 1e-3), 1), "unit": "tok/s", "h2d_bytes_per_step": 4 * d,
+                "d2h_bytes_per_step": 8 * (d + 1), "path": "hyb_verify via ctypes, host wall clock"},
+        "clocks": clk.summary()}), flush=True)
+
+
 # ------------------------------------------------------------------ decode attention alone (profiling)
 def run_attn_decode(args, rank, world, local):
     """The fused decode attention over the 48 layers of the 12B-shaped model at --ctx:
@@ -802,7 +869,9 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--workload", default="qmv",
-                    choices=["qmv", "decode", "qmv-shape", "attn-decode", "qmm", "tp-decode", "sdpa-prefill"])
+                    choices=["qmv", "decode", "qmv-shape", "attn-decode", "qmm", "tp-decode", "sdpa-prefill",
+                             "spec-verify"])
+    ap.add_argument("--drafts", default="1,3,7", help="draft lengths for --workload spec-verify (1..8)")
     ap.add_argument("--qmm-m", default="512,2048,8192", help="token counts for --workload qmm")
     ap.add_argument("--shape", default="3840,262144", help="K,N for --workload qmv-shape")
     ap.add_argument("--layout", default="packed", choices=["packed", "mlx"], help="weights for qmv-shape")
@@ -834,6 +903,8 @@ def main():
             run_attn_decode(args, rank, world, local)
         elif args.workload == "qmv-shape":
             run_qmv_shape(args, rank, world, local)
+        elif args.workload == "spec-verify":
+            run_spec_verify(args, rank, world, local)
         else:
             run_decode(args, rank, world, local)
     finally:

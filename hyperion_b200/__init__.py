@@ -106,6 +106,7 @@ EXT_FUNCTIONS = [
     "hyb_sdpa_decode_fused", "hyb_wait_timeouts", "hyb_nccl_unique_id", "hyb_model_set_tensor_parallel",
     "hyb_sdpa_prefill", "hyb_rms_norm", "hyb_qkv_post", "hyb_model_load_synthetic",
     "hyb_model_set_attention_rounding", "hyb_model_stream", "hyb_decode_batch", "hyb_kvstate_clone", "hyb_qmv_batched",
+    "hyb_verify",
     "hyb_kv_copy_layer", "hyb_kv_cursor", "hyb_prefill_logits", "hyb_decode_logits", "hyb_decode_forced",
     "hyb_test_arm_post_append_fault",
 ]
@@ -163,6 +164,8 @@ def lib() -> ctypes.CDLL:
         "hyb_kvstate_clone": [P, P, c.c_uint32, ctypes.POINTER(P)],
         "hyb_qmv_batched": [P, c.c_int32, c.c_int64, P, P, c.c_int64, c.c_int64, c.c_int64, c.c_int32, P],
         "hyb_decode_batch": [P, ctypes.POINTER(P), c.c_uint32, ctypes.POINTER(c.c_uint32), ctypes.POINTER(c.c_float)],
+        "hyb_verify": [P, P, ctypes.POINTER(c.c_uint32), c.c_uint32, ctypes.POINTER(c.c_uint32),
+                       ctypes.POINTER(c.c_float), ctypes.POINTER(c.c_uint32)],
         "hyb_model_stream": [P, ctypes.POINTER(P)],
         "hyb_kv_copy_layer": [P, P, c.c_uint32, c.c_int32, P, ctypes.POINTER(c.c_uint32)],
         "hyb_kv_cursor": [P, ctypes.POINTER(c.c_uint32), ctypes.POINTER(c.c_uint32)],
@@ -339,6 +342,18 @@ class KvState:
         check(lib().hyb_kvstate_clone(self.eng.handle, self._kv, 0xFFFFFFFF if last_token is None else last_token,
                                       ctypes.byref(k._kv)))
         return k
+
+    def verify(self, draft: Sequence[int]):
+        """Greedy speculative verify of `draft` (1..8 tokens, hyb_verify): returns
+        (accepted, tokens, post-softcap logits) with len(draft) + 1 greedy samples; the
+        state advances by accepted + 1 tokens."""
+        n = len(draft)
+        d = (ctypes.c_uint32 * max(n, 1))(*draft)
+        toks = (ctypes.c_uint32 * (n + 1))()
+        logs = (ctypes.c_float * (n + 1))()
+        acc = ctypes.c_uint32()
+        check(lib().hyb_verify(self.eng.handle, self._kv, d, n, toks, logs, ctypes.byref(acc)))
+        return acc.value, list(toks), list(logs)
 
     def close(self):
         if self._kv:

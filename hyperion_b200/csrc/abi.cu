@@ -668,6 +668,43 @@ HypStatus hyb_decode_batch(HypModel model, const HypKvState* kvstates, uint32_t 
     });
 }
 
+HypStatus hyb_verify(HypModel model, HypKvState kv, const uint32_t* draft, uint32_t n_draft, uint32_t* tokens_out,
+                     float* logits_out, uint32_t* n_accepted) {
+    HypStatus st = validate_model(model);
+    if (st != HYP_STATUS_OK) return st;
+    st = validate_kv(kv);
+    if (st != HYP_STATUS_OK) return st;
+    if (!model->loaded) return fail(HYP_STATUS_INVALID_ARGUMENT, "model is not loaded");
+    if (kv->owner != model) return fail(HYP_STATUS_INVALID_ARGUMENT, "kvstate belongs to another model");
+    if (draft == nullptr || tokens_out == nullptr || n_accepted == nullptr)
+        return fail(HYP_STATUS_INVALID_ARGUMENT, "null argument");
+    if (n_draft == 0 || n_draft > static_cast<uint32_t>(hyb::kSpecMax))
+        return fail(HYP_STATUS_INVALID_ARGUMENT, "verify takes 1 to 8 draft tokens");
+    if (kv->kv->offset == 0) return fail(HYP_STATUS_INVALID_ARGUMENT, "decode requires a populated KV state (prefill first)");
+    hyb::Model& m = *model->model;
+    for (uint32_t i = 0; i < n_draft; ++i)
+        if (draft[i] >= m.geometry().vocab) return fail(HYP_STATUS_INVALID_ARGUMENT, "token id is outside the vocabulary");
+    return guarded("hyb_verify", [&]() -> HypStatus {
+        DeviceGuard dg(m.device());
+        std::string why;
+        if (!admit(m, *kv->kv, n_draft + 1, why)) return fail(HYP_STATUS_OOM_GOVERNOR, why);
+        std::vector<hyb::StepOut> outs(n_draft + 1);
+        int a = 0;
+        try {
+            a = m.verify(*kv->kv, draft, static_cast<int>(n_draft), outs.data());
+        } catch (...) {
+            kv->kv->poisoned = true;  // a failed step consumes the state, as a failed decode does
+            throw;
+        }
+        for (uint32_t i = 0; i <= n_draft; ++i) {
+            tokens_out[i] = outs[i].token;
+            if (logits_out) logits_out[i] = outs[i].logit;
+        }
+        *n_accepted = static_cast<uint32_t>(a);
+        return ok();
+    });
+}
+
 HypStatus hyb_nccl_unique_id(void* out128) {
     if (out128 == nullptr) return fail(HYP_STATUS_INVALID_ARGUMENT, "output buffer is null");
     return guarded("hyb_nccl_unique_id", [&]() -> HypStatus {

@@ -182,7 +182,8 @@ __global__ void __launch_bounds__(kDecThreads) decode_pv_kernel(DecodeAttnParams
     const int hd = p.hd;
     const int j0 = split * chunk, j1 = min(p.n_keys, j0 + chunk);
     __shared__ float s_M[REP], s_invL[REP];
-    constexpr int kAcc = (REP * PER * 32 <= 1024) ? REP * PER * 32 : 32;  // per-warp REP * hd floats
+    static_assert(REP * PER * 32 <= 1024, "GQA group x head_dim above 1024");
+    constexpr int kAcc = REP * PER * 32;  // per-warp REP * hd floats
     __shared__ float s_acc[8][kAcc];
     __shared__ unsigned s_ticket;
     pdl_wait();
@@ -282,6 +283,10 @@ void decode_plan(int n_kv, int n_keys, int& n_splits, int& chunk) {
 
 template <int PER, int REP>
 void launch_decode_t(const DecodeAttnParams& p, const DecodeScratch& sc, cudaStream_t stream) {
+    if constexpr (REP * PER * 32 > 1024) {
+        // GQA group x head_dim above 1024 (rejected by the caller): not instantiated.
+        throw ArgError("decode attention: GQA group x head_dim > 1024");
+    } else {
     int n_splits, chunk;
     decode_plan(p.n_kv, p.n_keys, n_splits, chunk);
     if (chunk > 512) throw ArgError("decode attention: too many keys for the split plan");
@@ -290,6 +295,7 @@ void launch_decode_t(const DecodeAttnParams& p, const DecodeScratch& sc, cudaStr
     HYB_LAUNCH_CHECK("decode_scores_kernel");
     decode_pv_kernel<PER, REP><<<grid, kDecThreads, 0, stream>>>(p, sc, n_splits, chunk);
     HYB_LAUNCH_CHECK("decode_pv_kernel");
+    }
 }
 
 template <int PER>

@@ -259,7 +259,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_attn_fused_kernel(const De
     const int j0 = static_cast<int>(rank) * chunk;
     const int j1 = min(n_keys, j0 + chunk);
     const int n = max(0, j1 - j0);
-    const bool owns_newest = (j1 == n_keys) && n > 0;
+    const bool owns_newest = !p.kv_ready && (j1 == n_keys) && n > 0;
     const int newest = n_keys - 1;
     const int first_pos = pos - n_keys + 1;
     // tiles: segment A = keys before the ring wraps to slot 0, segment B = the rest
@@ -646,6 +646,7 @@ bool decode_attn_fused_fits(int n_heads, int n_kv, int hd, int n_keys) {
 }
 
 void launch_decode_attn_fused(const DecodeFusedParams& p, cudaStream_t stream, bool pdl) {
+    if (p.kv_ready && pdl) throw ArgError("decode attention: kv_ready launches cannot use PDL");
     if (p.n_keys <= 0 || p.n_kv <= 0 || p.n_heads % p.n_kv != 0 || p.pos < p.n_keys - 1 || p.cap < p.n_keys)
         throw ArgError("decode attention: bad shape");
     if ((p.n_heads / p.n_kv) * p.hd > 1024) throw ArgError("decode attention: GQA group x head_dim > 1024");
@@ -665,6 +666,8 @@ void launch_decode_attn_fused_batch(const DecodeFusedParams& p, int n_keys_max, 
     if (n_keys_max <= 0 || p.n_kv <= 0 || p.n_heads % p.n_kv != 0)
         throw ArgError("decode attention batch: bad shape");
     if ((p.n_heads / p.n_kv) * p.hd > 1024) throw ArgError("decode attention: GQA group x head_dim > 1024");
+    // cache tiles are requested before the dependency wait: appended K/V must be complete
+    if (p.kv_ready && pdl) throw ArgError("decode attention batch: kv_ready launches cannot use PDL");
     DecodeFusedParams q = p;
     q.n_keys = n_keys_max;  // the shared-memory plan covers the longest sequence
     switch (p.hd) {

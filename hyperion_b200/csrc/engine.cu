@@ -841,6 +841,33 @@ StepOut Model::prefill(KvState& kv, const uint32_t* tokens, uint32_t count, std:
     throw std::logic_error("prefill: empty prompt");
 }
 
+int Model::verify(KvState& kv, const uint32_t* draft, int n, StepOut* outs) {
+    if (n < 1 || n > kSpecMax) throw ArgError("verify: 1 to 8 draft tokens");
+    if (kv.offset == 0) throw ArgError("verify requires a populated KV state (prefill first)");
+    const int L = n + 1;
+    if (kv.offset + L > 32768) throw std::runtime_error("decode beyond 32768 tokens is not supported");
+    ensure_workspace(L, kv.offset + L);
+    ensure_batch_workspace(L);
+    reserve(kv, static_cast<uint32_t>(L));
+    ws_.h_ids[0] = kv.last_token;
+    std::memcpy(ws_.h_ids + 1, draft, static_cast<size_t>(n) * sizeof(uint32_t));
+    // the L rows run through the batched decode stack as consecutive positions of this
+    // state; all L positions are written to the caches (a rejected tail lands in the ring
+    // slack / past the committed global length and is overwritten later)
+    std::vector<KvState*> rows(L, &kv);
+    const std::vector<int> keys_max = stage_rows(rows.data(), L, 1);
+    rows_forward(L, keys_max, &kv);
+    lm_head_rows(L, outs);
+    int a = 0;
+    while (a < n && outs[a].token == draft[a]) ++a;
+    const uint32_t committed = kv.offset + static_cast<uint32_t>(a) + 1;
+    for (auto& c : kv.local) c.committed = committed;
+    for (auto& c : kv.global) c.committed = committed;
+    kv.offset = committed;
+    kv.last_token = outs[a].token;
+    return a;
+}
+
 void Model::decode_layers(KvState& kv) {
     const Geometry& g = geo_;
     const int H = static_cast<int>(g.hidden);
@@ -1064,66 +1091,96 @@ void Model::ensure_batch_workspace(int n) {
 // Batches up to this size project through qmv_batched; larger ones through the tcgen05 GEMM.
 constexpr int kBatchQmvMax = 16;
 
-void Model::decode_batch(KvState* const* kvs, int B, StepOut* outs) {
-    if (B < 1 || B > kMaxDecodeBatch) throw ArgError("decode batch: 1 to 64 sequences");
+// lm_head over this rank's vocabulary rows for the B final-normed rows in ws_.xn, then
+// soft-cap and top-2 per row (forward.cc:137-189); with tensor parallelism every rank's
+// (winner, runner-up) pair is all-gathered and merged. Writes outs[0..B).
+void Model::lm_head_rows(int B, StepOut* outs) {
+    const Geometry& g = geo_;
+    const int H = static_cast<int>(g.hidden);
+    cudaStream_t st = stream_;
+    if (B > kBatchQmvMax) {
+        launch_quantized_matmul(ws_.xn.p, embed_.w.p + static_cast<size_t>(vocab0_) * (H / 8),
+                                embed_.s.p + static_cast<size_t>(vocab0_) * (H / 64),
+                                embed_.b.p + static_cast<size_t>(vocab0_) * (H / 64), bws_.logits.p, B, H,
+                                vocab_local_, st);
+    } else {
+        launch_qmv_batched_x16(ws_.xn.p, B, H, H, bws_.x16.p, st);
+        QmvBatchParams q;
+        q.x16 = bws_.x16.p;
+        q.packed = lm_packed_.p;
+        q.y = bws_.logits.p;
+        q.K = H;
+        q.N = vocab_local_;
+        q.B = B;
+        q.ldy = vocab_local_;
+        q.geglu = false;
+        launch_qmv_batched(q, st);
+    }
+    launch_softcap_topk_rows(bws_.logits.p, B, vocab_local_, vocab_local_, g.softcap, bws_.topk_scratch.p,
+                             bws_.topk_scratch.n, bws_.topk_idx.p, bws_.topk_val.p, st);
+    const int T = tp_size_;
+    if (T > 1) {
+        tp_candidates_rows_kernel<<<1, 64, 0, st>>>(bws_.topk_idx.p, bws_.topk_val.p, B, static_cast<uint32_t>(vocab0_),
+                                                     bws_.cand.p);
+        HYB_LAUNCH_CHECK("tp_candidates_rows_kernel");
+        tp_.all_gather_bytes(bws_.cand.p, bws_.cand.p + 4 * B, static_cast<size_t>(16) * B, st);
+        HYB_CUDA(cudaMemcpyAsync(bws_.h_cand, bws_.cand.p + 4 * B, static_cast<size_t>(16) * B * T,
+                                 cudaMemcpyDeviceToHost, st));
+    } else {
+        HYB_CUDA(cudaMemcpyAsync(bws_.h_idx, bws_.topk_idx.p, sizeof(uint32_t) * kTopkRowStride * B,
+                                 cudaMemcpyDeviceToHost, st));
+        HYB_CUDA(cudaMemcpyAsync(bws_.h_val, bws_.topk_val.p, sizeof(float) * kTopkRowStride * B,
+                                 cudaMemcpyDeviceToHost, st));
+    }
+    HYB_CUDA(cudaStreamSynchronize(st));
+    if (T > 1 && tp_.take_wait_errors(st))
+        throw CudaError("tensor-parallel all-reduce: a wait for a peer's flag gave up");
+    for (int b = 0; b < B; ++b) {
+        StepOut& out = outs[b];
+        out = StepOut{};
+        if (T > 1) {
+            // highest value first, lowest vocabulary index on ties (the TP = 1 order)
+            std::vector<std::pair<float, uint32_t>> c;
+            for (int r = 0; r < T; ++r)
+                for (int k = 0; k < 2; ++k) {
+                    const uint32_t* e = bws_.h_cand + (static_cast<size_t>(r) * B + b) * 4 + 2 * k;
+                    float v;
+                    std::memcpy(&v, e + 1, 4);
+                    c.emplace_back(v, e[0]);
+                }
+            std::sort(c.begin(), c.end(), [](const auto& x, const auto& y) {
+                return x.first > y.first || (x.first == y.first && x.second < y.second);
+            });
+            for (int i = 0; i < 2; ++i) {
+                out.topk_idx[i] = c[i].second;
+                out.topk_val[i] = c[i].first;
+            }
+        } else {
+            const int n = static_cast<int>(std::min<uint32_t>(2, g.vocab));
+            for (int i = 0; i < n; ++i) {
+                out.topk_idx[i] = bws_.h_idx[kTopkRowStride * b + i];
+                out.topk_val[i] = bws_.h_val[kTopkRowStride * b + i];
+            }
+            if (n < 2) out.topk_val[1] = -INFINITY;
+        }
+        out.token = out.topk_idx[0];
+        out.logit = out.topk_val[0];
+        out.near_tie = (out.logit - out.topk_val[1]) < 0.5f;
+    }
+}
+
+// The layer stack for B rows whose inputs are in ws_.ids: row b's attention is described by
+// entry [layer][b] of the DecodeSeq arrays (host copy bws_.h_seqs, device copy bws_.seqs),
+// keys_max[layer] is its longest key range. Rows are independent sequences (batched
+// decode), or, with one_seq, consecutive positions of that one sequence (verify). Leaves the
+// final-normed rows in ws_.xn.
+void Model::rows_forward(int B, const std::vector<int>& keys_max, const KvState* one_seq) {
     const Geometry& g = geo_;
     const int H = static_cast<int>(g.hidden), I = inter_local_;
     const int nh = heads_local_;
     cudaStream_t st = stream_;
-    uint32_t max_pos = 0;
-    for (int b = 0; b < B; ++b) {
-        for (int c = 0; c < b; ++c)
-            if (kvs[c] == kvs[b]) throw ArgError("decode batch: a state appears twice");
-        if (kvs[b]->offset + 1 > 32768) throw std::runtime_error("decode beyond 32768 tokens is not supported");
-        max_pos = std::max(max_pos, kvs[b]->offset);
-    }
-    ensure_workspace(B, std::min<uint32_t>(max_pos + 1, 32768));
-    ensure_batch_workspace(B);
-    for (int b = 0; b < B; ++b) {
-        reserve(*kvs[b], 1);
-        ws_.h_ids[b] = kvs[b]->last_token;
-    }
-    // every layer's attention descriptors, staged in one copy
-    DecodeSeq* hs = bws_.h_seqs;
+    const DecodeSeq* hs = bws_.h_seqs;
     const DecodeSeq* dseq = reinterpret_cast<const DecodeSeq*>(bws_.seqs.p);
-    std::vector<int> keys_max(g.n_layers, 0);
-    {
-        std::vector<size_t> li(B, 0), gi(B, 0);
-        for (uint32_t layer = 0; layer < g.n_layers; ++layer) {
-            const LayerW& W = layers_[layer];
-            const int qkv_ld = W.q_rows + W.k_rows + W.v_rows;
-            for (int b = 0; b < B; ++b) {
-                KvState& kv = *kvs[b];
-                DecodeSeq& d = hs[static_cast<size_t>(layer) * B + b];
-                const uint32_t pos = kv.offset;
-                d.qkv = ws_.qkv.p + static_cast<size_t>(b) * qkv_ld;
-                d.out = ws_.attn.p + static_cast<size_t>(b) * W.q_rows;
-                d.pos = static_cast<int>(pos);
-                if (W.kind == LayerKind::Sliding) {
-                    LocalCache& c = kv.local[li[b]++];
-                    d.tk = c.tk;
-                    d.tv = c.tv;
-                    d.k_cache = c.k.p;
-                    d.v_cache = c.v.p;
-                    d.cap = static_cast<int>(c.cap);
-                    d.n_keys = static_cast<int>(std::min(g.window, pos + 1));  // forward.cc:55-57
-                } else {
-                    GlobalCache& c = kv.global[gi[b]++];
-                    if (c.capacity < pos + 1) throw std::runtime_error("global cache not reserved");
-                    d.tk = c.tk;
-                    d.tv = c.tv;
-                    d.k_cache = c.k.p;
-                    d.v_cache = c.v.p;
-                    d.cap = static_cast<int>(c.capacity);
-                    d.n_keys = static_cast<int>(pos + 1);
-                }
-                keys_max[layer] = std::max(keys_max[layer], d.n_keys);
-            }
-        }
-    }
-    HYB_CUDA(cudaMemcpyAsync(bws_.seqs.p, hs, sizeof(DecodeSeq) * g.n_layers * B, cudaMemcpyHostToDevice, st));
-    HYB_CUDA(cudaMemcpyAsync(ws_.ids.p, ws_.h_ids, sizeof(uint32_t) * B, cudaMemcpyHostToDevice, st));
-
     // one projection for the whole batch: activations to fp16 pairs, then the packed qmv
     auto proj = [&](const bf16* x, int ldx, int K, const void* packed, int N, bf16* y, int ldy, bool geglu) {
         launch_qmv_batched_x16(x, B, ldx, K, bws_.x16.p, st);
@@ -1163,6 +1220,30 @@ void Model::decode_batch(KvState* const* kvs, int B, StepOut* outs) {
         const int qkv_ld = W.q_rows + W.k_rows + W.v_rows;
         if (tc) proj_tc(ws_.xn.p, H, W.qkv.w.p, W.qkv.s.p, W.qkv.b.p, qkv_ld, ws_.qkv.p, false);
         else proj(ws_.xn.p, H, H, W.qkv.packed.p, qkv_ld, ws_.qkv.p, qkv_ld, false);
+        if (one_seq) {
+            // rows of one sequence: every row's K/V goes into the caches first (one launch),
+            // so that row r's attention sees rows 0..r; the attention launch then only
+            // reads the caches
+            const DecodeSeq& d0 = hs[static_cast<size_t>(layer) * B];
+            QkvPostParams qp;
+            qp.qkv = ws_.qkv.p;
+            qp.L = B;
+            qp.ld = qkv_ld;
+            qp.n_heads = nh;
+            qp.n_kv = W.nkv;
+            qp.hd = W.hd;
+            qp.v_from_k = W.v_rows == 0;
+            qp.q_norm = W.q_norm.p;
+            qp.k_norm = W.k_norm.p;
+            qp.inv_freq = W.inv_freq;
+            qp.pos0 = d0.pos;
+            qp.eps = g.eps;
+            qp.q_out = ws_.q.p;
+            qp.k_cache = d0.k_cache;
+            qp.v_cache = d0.v_cache;
+            qp.cache_cap = d0.cap;
+            launch_qkv_post(qp, st);
+        }
         // QK-norm + RoPE + cache append + attention of every sequence in one launch
         DecodeFusedParams ap;
         ap.v_from_k = W.v_rows == 0;
@@ -1176,6 +1257,7 @@ void Model::decode_batch(KvState* const* kvs, int B, StepOut* outs) {
         ap.rounding = attn_rounding_;
         ap.seqs = dseq + static_cast<size_t>(layer) * B;
         ap.n_seq = B;
+        ap.kv_ready = one_seq != nullptr;
         if (decode_attn_fused_fits(nh, W.nkv, W.hd, keys_max[layer])) {
             launch_decode_attn_fused_batch(ap, keys_max[layer], st, false);
         } else {
@@ -1183,6 +1265,24 @@ void Model::decode_batch(KvState* const* kvs, int B, StepOut* outs) {
             // norm/RoPE/append and split-K attention
             for (int b = 0; b < B; ++b) {
                 const DecodeSeq& d = hs[static_cast<size_t>(layer) * B + b];
+                if (one_seq) {  // K/V already appended; q of row b from the append launch
+                    DecodeAttnParams dp;
+                    dp.q = ws_.q.p + static_cast<size_t>(b) * W.q_rows;
+                    dp.k_cache = d.k_cache;
+                    dp.v_cache = d.v_cache;
+                    dp.out = d.out;
+                    dp.n_heads = nh;
+                    dp.n_kv = W.nkv;
+                    dp.hd = W.hd;
+                    dp.cap = d.cap;
+                    dp.last_pos = d.pos;
+                    dp.n_keys = d.n_keys;
+                    dp.rounding = attn_rounding_;
+                    dp.scratch = ws_.attn_scratch.p;
+                    dp.scratch_bytes = ws_.attn_scratch_bytes;
+                    launch_decode_attn(dp, st);
+                    continue;
+                }
                 QkvPostParams qp;
                 qp.qkv = d.qkv;
                 qp.L = 1;
@@ -1233,61 +1333,77 @@ void Model::decode_batch(KvState* const* kvs, int B, StepOut* outs) {
         const bf16* next_w = (layer + 1 < g.n_layers) ? layers_[layer + 1].in_ln.p : final_norm_.p;
         launch_resid_norm(ws_.dn.p, W.post_ff.p, h_alt, W.scalar.p, h_cur, next_w, ws_.xn.p, B, H, g.eps, st);
     }
-    // lm_head over this rank's vocabulary rows, soft-cap and top-2 per sequence
-    if (tc)
-        proj_tc(ws_.xn.p, H, embed_.w.p + static_cast<size_t>(vocab0_) * (H / 8),
-                embed_.s.p + static_cast<size_t>(vocab0_) * (H / 64), embed_.b.p + static_cast<size_t>(vocab0_) * (H / 64),
-                vocab_local_, bws_.logits.p, false);
-    else
-        proj(ws_.xn.p, H, H, lm_packed_.p, vocab_local_, bws_.logits.p, vocab_local_, false);
-    launch_softcap_topk_rows(bws_.logits.p, B, vocab_local_, vocab_local_, g.softcap, bws_.topk_scratch.p,
-                             bws_.topk_scratch.n, bws_.topk_idx.p, bws_.topk_val.p, st);
-    const int T = tp_size_;
-    if (T > 1) {
-        tp_candidates_rows_kernel<<<1, 64, 0, st>>>(bws_.topk_idx.p, bws_.topk_val.p, B, static_cast<uint32_t>(vocab0_),
-                                                     bws_.cand.p);
-        HYB_LAUNCH_CHECK("tp_candidates_rows_kernel");
-        tp_.all_gather_bytes(bws_.cand.p, bws_.cand.p + 4 * B, static_cast<size_t>(16) * B, st);
-        HYB_CUDA(cudaMemcpyAsync(bws_.h_cand, bws_.cand.p + 4 * B, static_cast<size_t>(16) * B * T,
-                                 cudaMemcpyDeviceToHost, st));
-    } else {
-        HYB_CUDA(cudaMemcpyAsync(bws_.h_idx, bws_.topk_idx.p, sizeof(uint32_t) * kTopkRowStride * B,
-                                 cudaMemcpyDeviceToHost, st));
-        HYB_CUDA(cudaMemcpyAsync(bws_.h_val, bws_.topk_val.p, sizeof(float) * kTopkRowStride * B,
-                                 cudaMemcpyDeviceToHost, st));
-    }
-    HYB_CUDA(cudaStreamSynchronize(st));
-    for (int b = 0; b < B; ++b) {
-        StepOut& out = outs[b];
-        out = StepOut{};
-        if (T > 1) {
-            // highest value first, lowest vocabulary index on ties (the TP = 1 order)
-            std::vector<std::pair<float, uint32_t>> c;
-            for (int r = 0; r < T; ++r)
-                for (int k = 0; k < 2; ++k) {
-                    const uint32_t* e = bws_.h_cand + (static_cast<size_t>(r) * B + b) * 4 + 2 * k;
-                    float v;
-                    std::memcpy(&v, e + 1, 4);
-                    c.emplace_back(v, e[0]);
+}
+
+// Attention descriptors of B rows for every layer, staged to the device with the rows'
+// input tokens (ws_.h_ids): row b is state kvs[b] at position kvs[b]->offset + b * pos_step
+// (pos_step 0: one step of B sequences; 1: consecutive rows of one sequence). Returns each
+// layer's longest key range.
+std::vector<int> Model::stage_rows(KvState* const* kvs, int B, uint32_t pos_step) {
+    const Geometry& g = geo_;
+    cudaStream_t st = stream_;
+    DecodeSeq* hs = bws_.h_seqs;
+    std::vector<int> keys_max(g.n_layers, 0);
+    {
+        std::vector<size_t> li(B, 0), gi(B, 0);
+        for (uint32_t layer = 0; layer < g.n_layers; ++layer) {
+            const LayerW& W = layers_[layer];
+            const int qkv_ld = W.q_rows + W.k_rows + W.v_rows;
+            for (int b = 0; b < B; ++b) {
+                KvState& kv = *kvs[b];
+                DecodeSeq& d = hs[static_cast<size_t>(layer) * B + b];
+                const uint32_t pos = kv.offset + static_cast<uint32_t>(b) * pos_step;
+                d.qkv = ws_.qkv.p + static_cast<size_t>(b) * qkv_ld;
+                d.out = ws_.attn.p + static_cast<size_t>(b) * W.q_rows;
+                d.pos = static_cast<int>(pos);
+                if (W.kind == LayerKind::Sliding) {
+                    LocalCache& c = kv.local[li[b]++];
+                    d.tk = c.tk;
+                    d.tv = c.tv;
+                    d.k_cache = c.k.p;
+                    d.v_cache = c.v.p;
+                    d.cap = static_cast<int>(c.cap);
+                    d.n_keys = static_cast<int>(std::min(g.window, pos + 1));  // forward.cc:55-57
+                } else {
+                    GlobalCache& c = kv.global[gi[b]++];
+                    if (c.capacity < pos + 1) throw std::runtime_error("global cache not reserved");
+                    d.tk = c.tk;
+                    d.tv = c.tv;
+                    d.k_cache = c.k.p;
+                    d.v_cache = c.v.p;
+                    d.cap = static_cast<int>(c.capacity);
+                    d.n_keys = static_cast<int>(pos + 1);
                 }
-            std::sort(c.begin(), c.end(), [](const auto& x, const auto& y) {
-                return x.first > y.first || (x.first == y.first && x.second < y.second);
-            });
-            for (int i = 0; i < 2; ++i) {
-                out.topk_idx[i] = c[i].second;
-                out.topk_val[i] = c[i].first;
+                keys_max[layer] = std::max(keys_max[layer], d.n_keys);
             }
-        } else {
-            const int n = static_cast<int>(std::min<uint32_t>(2, g.vocab));
-            for (int i = 0; i < n; ++i) {
-                out.topk_idx[i] = bws_.h_idx[kTopkRowStride * b + i];
-                out.topk_val[i] = bws_.h_val[kTopkRowStride * b + i];
-            }
-            if (n < 2) out.topk_val[1] = -INFINITY;
         }
-        out.token = out.topk_idx[0];
-        out.logit = out.topk_val[0];
-        out.near_tie = (out.logit - out.topk_val[1]) < 0.5f;
+    }
+    HYB_CUDA(cudaMemcpyAsync(bws_.seqs.p, hs, sizeof(DecodeSeq) * g.n_layers * B, cudaMemcpyHostToDevice, st));
+    HYB_CUDA(cudaMemcpyAsync(ws_.ids.p, ws_.h_ids, sizeof(uint32_t) * B, cudaMemcpyHostToDevice, st));
+    return keys_max;
+}
+
+void Model::decode_batch(KvState* const* kvs, int B, StepOut* outs) {
+    if (B < 1 || B > kMaxDecodeBatch) throw ArgError("decode batch: 1 to 64 sequences");
+    const Geometry& g = geo_;
+    uint32_t max_pos = 0;
+    for (int b = 0; b < B; ++b) {
+        for (int c = 0; c < b; ++c)
+            if (kvs[c] == kvs[b]) throw ArgError("decode batch: a state appears twice");
+        if (kvs[b]->offset + 1 > 32768) throw std::runtime_error("decode beyond 32768 tokens is not supported");
+        max_pos = std::max(max_pos, kvs[b]->offset);
+    }
+    ensure_workspace(B, std::min<uint32_t>(max_pos + 1, 32768));
+    ensure_batch_workspace(B);
+    for (int b = 0; b < B; ++b) {
+        reserve(*kvs[b], 1);
+        ws_.h_ids[b] = kvs[b]->last_token;
+    }
+    const std::vector<int> keys_max = stage_rows(kvs, B, 0);
+    rows_forward(B, keys_max, nullptr);
+    lm_head_rows(B, outs);
+    for (int b = 0; b < B; ++b) {
+        const StepOut& out = outs[b];
         KvState& kv = *kvs[b];
         size_t li = 0, gi = 0;
         for (uint32_t layer = 0; layer < g.n_layers; ++layer) {

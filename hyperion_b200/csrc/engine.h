@@ -98,6 +98,12 @@ struct KvState {
     bool poisoned = false;
 };
 
+// Draft tokens one verify pass may check: the speculative slack of the local rings
+// (capacity window + 8). Writing positions offset..offset+8 overwrites only ring slots
+// of positions at least window + 8 back, so after any acceptance every position the next
+// step attends to is intact (kv.h:7-18).
+constexpr int kSpecMax = 8;
+
 struct StepOut {
     uint32_t token = 0;
     float logit = 0.f;
@@ -172,6 +178,13 @@ class Model {
     // offset, from its own last_token): one weight stream per projection for the whole
     // batch. Writes outs[0..n); each state advances by one token.
     void decode_batch(KvState* const* kvs, int n, StepOut* outs);
+    // Greedy speculative verify: one pass over [kv.last_token, draft[0..n)] at positions
+    // kv.offset.. (1 <= n <= kSpecMax), through the batched decode stack with the rows as
+    // consecutive positions of this state. outs[i] is the greedy sample after input i. The
+    // longest prefix of draft that matches outs is accepted: the state commits
+    // last_token and those `accepted` drafts, and its next input is outs[accepted].token,
+    // so the result equals `accepted + 1` greedy decode steps. Returns `accepted`.
+    int verify(KvState& kv, const uint32_t* draft, int n, StepOut* outs);
 
     // Attention rounding: 0 = MLX CPU-stream semantics (bf16 scores and
     // probabilities, the default), 1 = fp32 scores/probabilities (MLX's fused
@@ -197,6 +210,9 @@ class Model {
     void ensure_workspace(int tokens, uint32_t max_keys);
     void forward_chunk(KvState& kv, int L, uint32_t offset);  // ids already in ws_.ids
     void decode_layers(KvState& kv);
+    void lm_head_rows(int B, StepOut* outs);  // B final-normed rows in ws_.xn -> greedy samples
+    std::vector<int> stage_rows(KvState* const* kvs, int B, uint32_t pos_step);
+    void rows_forward(int B, const std::vector<int>& keys_max, const KvState* one_seq);
     StepOut epilogue(const bf16* final_row, bool fused_prologue, const bf16* dn, const bf16* resid,
                      std::vector<uint16_t>* logits_out);
 

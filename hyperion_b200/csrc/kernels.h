@@ -233,6 +233,10 @@ struct DecodeFusedParams {
     // sequences on the device; qkv/out/caches/cap/pos/n_keys/tensor maps above unused.
     const DecodeSeq* seqs = nullptr;
     int n_seq = 0;
+    // The newest position's K/V are already in the caches (appended by an earlier launch,
+    // e.g. rows of one sequence at consecutive positions): the kernel neither computes nor
+    // appends them and reads every key from the caches. Such a launch must not use PDL.
+    bool kv_ready = false;
 };
 // Tiled TMA tensor map (rank <= 5): dims innermost first, strides in bytes for dims
 // 1..rank-1, box in elements; no interleave, zero fill out of bounds (tma_host.cu).

@@ -249,6 +249,20 @@ HypStatus hyb_kvstate_clone(HypModel model, HypKvState src, uint32_t last_token,
 HypStatus hyb_decode_batch(HypModel model, const HypKvState* kvstates, uint32_t n, uint32_t* tokens_out,
                            float* logits_out);
 
+/*
+ * Greedy speculative verify of n_draft (1..8) draft tokens on a populated KV state: one
+ * forward pass over [the state's last token, draft[0..n_draft)] at consecutive positions.
+ * tokens_out[i] (n_draft + 1 entries) receives the greedy sample after input i, and
+ * logits_out[i] (when not NULL) its post-softcap logit. The longest prefix of draft that
+ * equals tokens_out is accepted (*n_accepted): the state advances by n_accepted + 1
+ * tokens and its next input is tokens_out[n_accepted], so the outcome equals that many
+ * greedy hyp_decode_block steps. The rejected tail stays in the local rings' speculative
+ * slack (capacity window + 8) and is overwritten later; committed tokens are never
+ * touched (kv.h:7-18). A failure after the pass starts poisons the state.
+ */
+HypStatus hyb_verify(HypModel model, HypKvState kv, const uint32_t* draft, uint32_t n_draft, uint32_t* tokens_out,
+                     float* logits_out, uint32_t* n_accepted);
+
 /* The CUDA stream the model's kernels run on (for event timing). */
 HypStatus hyb_model_stream(HypModel model, void** out_stream);
 
