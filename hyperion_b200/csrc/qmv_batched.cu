@@ -97,11 +97,14 @@ __global__ void __launch_bounds__(kThreads) qmv_batched_kernel(const QmvBatchPar
 
     const int W = team;
     const int tw = warp / W, wt = warp % W;
-    const int team_id = static_cast<int>(blockIdx.x) * (kWarps / W) + tw;
-    const int n_teams = static_cast<int>(gridDim.x) * (kWarps / W);
+    // row-block groups are dealt round-robin over the CTAs first, then over the CTA's teams:
+    // group_of(i) = cta + (tw + i * tpc) * grid, so every SM holds the same count within one
+    const int tpc = kWarps / W, grid = static_cast<int>(gridDim.x), cta = static_cast<int>(blockIdx.x);
+    auto group_of = [=](int i) { return cta + (tw + i * tpc) * grid; };
     const int n_groups = (pg.nrb + BG - 1) / BG;
     const int my_units = (wt < pg.nunits) ? (pg.nunits - wt + W - 1) / W : 0;
-    const int my_groups = (team_id < n_groups) ? (n_groups - team_id + n_teams - 1) / n_teams : 0;
+    const int first = group_of(0);
+    const int my_groups = (first < n_groups) ? (n_groups - 1 - first) / (tpc * grid) + 1 : 0;
     const int n_items = my_groups * BG * my_units;
 
     pdl_launch_dependents();
@@ -113,7 +116,7 @@ __global__ void __launch_bounds__(kThreads) qmv_batched_kernel(const QmvBatchPar
 
     int ig = 0, ij = 0, iu = 0, n_issued = 0;
     auto issue_next = [&]() {
-        const int rb = (team_id + ig * n_teams) * BG + ij;
+        const int rb = group_of(ig) * BG + ij;
         const int unit = wt + iu * W;
         const int s = n_issued % kStages;
         const uint32_t bar = my_bar0 + 8 * s;
@@ -144,7 +147,7 @@ __global__ void __launch_bounds__(kThreads) qmv_batched_kernel(const QmvBatchPar
     uint32_t phase_bits = 0;
     int it = 0;
     for (int gi = 0; gi < my_groups; ++gi) {
-        const int grp = team_id + gi * n_teams;
+        const int grp = group_of(gi);
         for (int j = 0; j < BG; ++j) {
             const int rb = grp * BG + j;
             float acc[NB8][4];
@@ -344,18 +347,18 @@ void launch_qmv_batched(const QmvBatchParams& p, cudaStream_t stream, bool pdl) 
     const int per_sm = smem <= 110 * 1024 ? 2 : 1;
     const int max_ctas = per_sm * num_sms();
     // team size: fewest items on the busiest warp, the smallest team on ties
+    // (groups go round-robin over the CTAs, so the busiest CTA holds ceil(groups / grid))
+    const int grid = std::max(1, std::min(groups, max_ctas));
+    const int per_cta = (groups + grid - 1) / grid;
     int team = kWarps, best = 1 << 30;
     for (int w = kWarps; w >= 1; w /= 2) {
         const int tpc_w = kWarps / w;
-        const int n_teams = std::min((groups + tpc_w - 1) / tpc_w, max_ctas) * tpc_w;
-        const int load = (groups + n_teams - 1) / n_teams * (p.geglu ? 2 : 1) * ((pg.nunits + w - 1) / w);
+        const int load = (per_cta + tpc_w - 1) / tpc_w * (p.geglu ? 2 : 1) * ((pg.nunits + w - 1) / w);
         if (load <= best) {
             best = load;
             team = w;
         }
     }
-    const int tpc = kWarps / team;
-    const int grid = std::max(1, std::min((groups + tpc - 1) / tpc, max_ctas));
     switch (BP) {
         case 8: p.geglu ? launch_t<true, 1>(p, team, grid, smem, stream, pdl) : launch_t<false, 1>(p, team, grid, smem, stream, pdl); break;
         case 16: p.geglu ? launch_t<true, 2>(p, team, grid, smem, stream, pdl) : launch_t<false, 2>(p, team, grid, smem, stream, pdl); break;
