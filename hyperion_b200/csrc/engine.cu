@@ -1069,8 +1069,7 @@ void Model::ensure_batch_workspace(int n) {
     const Geometry& g = geo_;
     int max_k = static_cast<int>(g.hidden);
     for (const auto& L : layers_) max_k = std::max({max_k, L.q_rows, L.down.K});
-    const size_t BP = static_cast<size_t>(qmv_batch_pad(n));
-    bws_.x16.reset(BP * max_k / 2);
+    bws_.x16.reset(qmv_batch_x16_words(n, max_k));
     bws_.logits.reset(static_cast<size_t>(n) * vocab_local_);
     bws_.topk_scratch.reset(static_cast<size_t>(n) * softcap_topk_scratch_floats(vocab_local_));
     bws_.topk_idx.reset(static_cast<size_t>(n) * kTopkRowStride);

@@ -81,8 +81,8 @@ void launch_qmv_packed(const QmvParams& p, cudaStream_t stream, bool pdl = false
 
 // Batched decode qmv (qmv_batched.cu): B <= kMaxDecodeBatch sequences over the packed
 // layout, one weight stream for the whole batch. x16 is the activation batch converted by
-// launch_qmv_batched_x16 ([qmv_batch_pad(B)][K/2] u32); y is [B][ldy] (N/2 columns with
-// the GeGLU epilogue over the interleaved gate/up matrix).
+// launch_qmv_batched_x16 (qmv_batch_x16_words(B, K) u32, tiled per 512-code unit); y is
+// [B][ldy] (N/2 columns with the GeGLU epilogue over the interleaved gate/up matrix).
 constexpr int kMaxDecodeBatch = 64;
 struct QmvBatchParams {
     const uint32_t* x16 = nullptr;
@@ -92,6 +92,7 @@ struct QmvBatchParams {
     bool geglu = false;
 };
 int qmv_batch_pad(int B);
+size_t qmv_batch_x16_words(int B, int K);
 void launch_qmv_batched_x16(const bf16* x, int B, int ldx, int K, uint32_t* x16, cudaStream_t stream);
 void launch_qmv_batched(const QmvBatchParams& p, cudaStream_t stream, bool pdl = false);
 int64_t read_qmvb_wait_timeouts();

@@ -150,7 +150,7 @@ HypStatus hyb_qmv_batched(const void* x, int32_t B, int64_t ldx, const void* pac
     return run([&] {
         cudaStream_t st = as_stream(stream);
         void* x16 = nullptr;
-        HYB_CUDA(cudaMallocAsync(&x16, static_cast<size_t>(hyb::qmv_batch_pad(B)) * K * 2, st));
+        HYB_CUDA(cudaMallocAsync(&x16, hyb::qmv_batch_x16_words(B, static_cast<int>(K)) * 4, st));
         hyb::launch_qmv_batched_x16(static_cast<const hyb::bf16*>(x), B, static_cast<int>(ldx), static_cast<int>(K),
                                     static_cast<uint32_t*>(x16), st);
         hyb::QmvBatchParams q;

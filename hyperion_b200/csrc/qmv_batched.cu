@@ -14,9 +14,12 @@
 // weights carry their scales, so that is fine, and lane (n, t) loads the activations of
 // sequence n at exactly the code positions lane (·, t) supplies.
 //
-// x arrives pre-converted (launch_qmv_batched_x16): x16[b][4j + p] = fp16 pair
-// (x[b][8j + p], x[b][8j + p + 4]), the nibble pairing of the packed words, rows >= B
-// zero. Work split, rings and teams as in the batch-1 kernel; a team sums its warps'
+// x arrives pre-converted (launch_qmv_batched_x16) into fp16 pairs (x[b][8j + p],
+// x[b][8j + p + 4]), the nibble pairing of the packed words, tiled so that every warp-wide
+// activation load is one contiguous 512-byte run: the 16-byte chunk (pairs p = 0..3 of
+// 8-code chunk j = 8G + w, group G = 8u + 2t + sel of unit u, sequence b = 8o + g) sits at
+// chunk index ((((u·2 + sel)·8 + w)·NB8 + o)·8 + g)·4 + t, exactly where lane (g, t) of
+// MMA column group o reads it; sequences >= B and groups past K are zero. Work split, rings and teams as in the batch-1 kernel; a team sums its warps'
 // partials in shared memory in a fixed order.
 #include "kernels.h"
 #include "qmv_pack.cuh"
@@ -143,7 +146,7 @@ __global__ void __launch_bounds__(kThreads) qmv_batched_kernel(const QmvBatchPar
     while (n_issued < kStages && n_issued < n_items) issue_next();
     pdl_wait();
 
-    const size_t xrow = static_cast<size_t>(p.K) / 2;  // u32 per x16 row
+    const uint4* x16q = reinterpret_cast<const uint4*>(p.x16);
     uint32_t phase_bits = 0;
     int it = 0;
     for (int gi = 0; gi < my_groups; ++gi) {
@@ -193,7 +196,7 @@ __global__ void __launch_bounds__(kThreads) qmv_batched_kernel(const QmvBatchPar
                     const float fb0 = __uint_as_float(static_cast<uint32_t>(b0) << 16);
                     const float fb1 = __uint_as_float(static_cast<uint32_t>(b1) << 16);
                     const bool slow = !__all_sync(0xffffffffu, exact || !gvalid);
-                    const uint32_t* xg = p.x16 + static_cast<size_t>(G) * 32;  // this group's 32 pair words
+                    const uint4* xg = x16q + static_cast<size_t>((unit * 2 + sel) * 8) * NB8 * 32 + lane;
 #pragma unroll
                     for (int w = 0; w < 8; ++w) {
                         const uint4 c0 = wv[2 * sel + (w >> 2)], c1 = wv[4 + 2 * sel + (w >> 2)];
@@ -217,7 +220,7 @@ __global__ void __launch_bounds__(kThreads) qmv_batched_kernel(const QmvBatchPar
 #pragma unroll
                         for (int o = 0; o < NB8; ++o) {
                             uint4 xv = make_uint4(0, 0, 0, 0);
-                            if (gvalid) xv = *reinterpret_cast<const uint4*>(xg + static_cast<size_t>(8 * o + g) * xrow + 4 * w);
+                            if (gvalid) xv = xg[(w * NB8 + o) * 32];
                             // k-steps: pairs (0, 1) then (2, 3) of word w
                             mma_f16_16816(acc[o], a[0][0], a[0][1], a[1][0], a[1][1], xv.x, xv.y);
                             mma_f16_16816(acc[o], a[2][0], a[2][1], a[3][0], a[3][1], xv.z, xv.w);
@@ -258,30 +261,36 @@ __global__ void __launch_bounds__(kThreads) qmv_batched_kernel(const QmvBatchPar
     }
 }
 
-// x [B][ldx] bf16 -> x16 [BP][K/2] fp16 pairs (x[8j + p], x[8j + p + 4]) at 4j + p; rows >= B zero.
-__global__ void x16_kernel(const bf16* __restrict__ x, int B, int ldx, int K, int BP, uint32_t* __restrict__ x16) {
-    const int nch = K / 8;
-    const long long total = static_cast<long long>(BP) * nch;
+// x [B][ldx] bf16 -> the tiled fp16-pair chunks read by qmv_batched_kernel (one thread per
+// 16-byte chunk, padding chunks zero).
+__global__ void x16_kernel(const bf16* __restrict__ x, int B, int ldx, int K, int NB8, uint4* __restrict__ x16) {
+    const int n_groups = K / 64;
+    const long long total = static_cast<long long>((n_groups + 7) / 8) * 512 * NB8;
     for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < total;
          i += static_cast<long long>(gridDim.x) * blockDim.x) {
-        const int b = static_cast<int>(i / nch), j = static_cast<int>(i % nch);
-        uint4 o = make_uint4(0, 0, 0, 0);
-        if (b < B) {
-            const uint4 v = *reinterpret_cast<const uint4*>(x + static_cast<size_t>(b) * ldx + 8 * j);
-            const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+        const int t = static_cast<int>(i & 3), g = static_cast<int>((i >> 2) & 7);
+        long long r = i >> 5;
+        const int o = static_cast<int>(r % NB8);
+        r /= NB8;
+        const int w = static_cast<int>(r & 7), sel = static_cast<int>((r >> 3) & 1), u = static_cast<int>(r >> 4);
+        const int b = 8 * o + g, G = 8 * u + 2 * t + sel;
+        uint4 out = make_uint4(0, 0, 0, 0);
+        if (b < B && G < n_groups) {
+            const uint4 v = *reinterpret_cast<const uint4*>(x + static_cast<size_t>(b) * ldx + 8 * (8 * G + w));
+            const uint32_t wd[4] = {v.x, v.y, v.z, v.w};
             float f[8];
 #pragma unroll
             for (int q = 0; q < 4; ++q) {
-                f[2 * q] = __uint_as_float(w[q] << 16);
-                f[2 * q + 1] = __uint_as_float(w[q] & 0xFFFF0000u);
+                f[2 * q] = __uint_as_float(wd[q] << 16);
+                f[2 * q + 1] = __uint_as_float(wd[q] & 0xFFFF0000u);
             }
             auto h = [](float a) { return static_cast<uint32_t>(__half_as_ushort(__float2half_rn(a))); };
-            o.x = h(f[0]) | (h(f[4]) << 16);
-            o.y = h(f[1]) | (h(f[5]) << 16);
-            o.z = h(f[2]) | (h(f[6]) << 16);
-            o.w = h(f[3]) | (h(f[7]) << 16);
+            out.x = h(f[0]) | (h(f[4]) << 16);
+            out.y = h(f[1]) | (h(f[5]) << 16);
+            out.z = h(f[2]) | (h(f[6]) << 16);
+            out.w = h(f[3]) | (h(f[7]) << 16);
         }
-        reinterpret_cast<uint4*>(x16 + static_cast<size_t>(b) * (K / 2))[j] = o;
+        x16[i] = out;
     }
 }
 
@@ -310,6 +319,10 @@ void launch_t(const QmvBatchParams& p, int team, int grid, size_t smem, cudaStre
 
 }  // namespace
 
+size_t qmv_batch_x16_words(int B, int K) {
+    return static_cast<size_t>((K / 64 + 7) / 8) * 256 * qmv_batch_pad(B);
+}
+
 int qmv_batch_pad(int B) {
     if (B <= 8) return 8;
     if (B <= 16) return 16;
@@ -322,10 +335,10 @@ void launch_qmv_batched_x16(const bf16* x, int B, int ldx, int K, uint32_t* x16,
         throw ArgError("qmv batched: bad activation shape");
     if ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(x16)) & 15u)
         throw ArgError("qmv batched: activations must be 16-byte aligned");
-    const int BP = qmv_batch_pad(B);
-    const long long total = static_cast<long long>(BP) * (K / 8);
+    const int NB8 = qmv_batch_pad(B) / 8;
+    const long long total = static_cast<long long>((K / 64 + 7) / 8) * 512 * NB8;
     const int grid = static_cast<int>(std::min<long long>((total + 255) / 256, 4 * num_sms()));
-    x16_kernel<<<grid, 256, 0, stream>>>(x, B, ldx, K, BP, x16);
+    x16_kernel<<<grid, 256, 0, stream>>>(x, B, ldx, K, NB8, reinterpret_cast<uint4*>(x16));
     HYB_LAUNCH_CHECK("x16_kernel");
 }
 
