@@ -120,6 +120,53 @@ def test_verify_rejected_tail_is_invisible(built_lib):
     assert np.mean(agree) >= 11 / 12
 
 
+@pytest.mark.parametrize("name,geo,seed,plen,passes", [
+    ("cfg0", config0(), 7, 32, 10),
+    ("tiny_ring_wraps", tiny_fixture_geometry(), 11, 20, 12),
+])
+def test_verify_matches_oracle(built_lib, oracle_lib, tmp_path, name, geo, seed, plen, passes):
+    """Every row of every verify pass against the CPU oracle teacher-forced through the
+    same inputs from its own committed state (a copy per pass); the oracle then commits
+    the same accepted rows. Drafts follow the oracle's own greedy continuation up to a
+    random point, so acceptance varies. Greedy tokens >= 99%; post-softcap top logits
+    within 5e-2 relative (the bound of the decode-vs-oracle tests)."""
+    import copy
+    from oracle import gemma_oracle as go
+    from hyperion_b200.synth import bf16_bits_to_f32, write_checkpoint
+    t = write_checkpoint(geo, str(tmp_path / "w"), seed=seed)
+    eng, orc = hb.Engine(geo, weights_dir=str(tmp_path / "w")), go.OracleModel(geo, t)
+    rng = np.random.default_rng(seed)
+    prompt = rng.integers(0, geo.vocab_size, plen).tolist()
+    kv, okv = eng.new_kv(), orc.new_kv()
+    kv.prefill(prompt)
+    orc.prefill(okv, prompt)
+    agree, rel, accepted = [], [], []
+    for _ in range(passes):
+        n = int(rng.integers(1, 9))
+        _, last = kv.cursor()
+        probe = copy.deepcopy(okv)
+        seq, inp = [], last
+        for _ in range(n):  # the oracle's own greedy continuation from `last`
+            (tok, _, _, _), = orc.decode(probe, 1, forced=[inp])
+            seq.append(tok)
+            inp = tok
+        keep = int(rng.integers(0, n + 1))
+        draft = seq[:keep] + rng.integers(0, geo.vocab_size, n - keep).tolist()
+        a, toks, logs = kv.verify(draft)
+        ref = orc.decode(copy.deepcopy(okv), n + 1, forced=[last] + draft)
+        for i in range(n + 1):
+            agree.append(toks[i] == ref[i][0])
+            if toks[i] == ref[i][0]:
+                want = float(bf16_bits_to_f32(np.asarray([ref[i][3][toks[i]]], dtype=np.uint16))[0])
+                rel.append(abs(logs[i] - want) / max(1.0, abs(want)))
+        orc.decode(okv, a + 1, forced=[last] + draft[:a])  # commit what the engine committed
+        assert kv.cursor()[0] == okv["offset"]
+        accepted.append(a)
+    assert np.mean(agree) >= 0.99, agree
+    assert max(rel) <= 5e-2, max(rel)
+    assert max(accepted) > 0
+
+
 def test_verify_errors(built_lib):
     geo = config0()
     eng = hb.Engine(geo, synthetic_seed=2)
