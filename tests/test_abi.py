@@ -83,6 +83,15 @@ def test_handle_lifecycle_and_errors_without_gpu(built_lib):
     assert L.hyp_step_result_fields(r, ctypes.byref(f)) == hb.OK
     assert L.hyp_step_result_fields(r, None) == hb.INVALID_ARGUMENT
     assert L.hyp_decode_block(m, None, 1, r) == hb.INVALID_ARGUMENT
+    # batched decode, clone and speculative verify validate before any device work
+    tok = (ctypes.c_uint32 * 9)()
+    acc = ctypes.c_uint32()
+    assert L.hyb_verify(m, None, tok, 2, tok, None, ctypes.byref(acc)) == hb.INVALID_ARGUMENT
+    assert L.hyb_verify(None, None, tok, 2, tok, None, ctypes.byref(acc)) == hb.INVALID_ARGUMENT
+    assert L.hyb_decode_batch(m, None, 1, tok, None) == hb.INVALID_ARGUMENT
+    assert "not loaded" in hb.last_error()
+    out = ctypes.c_void_p()
+    assert L.hyb_kvstate_clone(m, None, 0, ctypes.byref(out)) == hb.INVALID_ARGUMENT and not out.value
     assert L.hyp_step_result_free(ctypes.byref(r)) == hb.OK and not r.value
     assert L.hyp_step_result_free(ctypes.byref(r)) == hb.OK
     assert L.hyp_model_free(ctypes.byref(m)) == hb.OK and not m.value
