@@ -1196,7 +1196,7 @@ void Model::rows_forward(int B, const std::vector<int>& keys_max, const KvState*
     };
     // the same through the tcgen05 GEMM over the MLX layout (split-K when its tiles cannot
     // fill the GPU); GeGLU then runs on the interleaved gate/up output. Measured on the
-    // 27B shape: the batched qmv wins at 8 sequences (392 vs 286 tok/s), the GEMM at 64
+    // 27B shape: the batched qmv wins at 8 sequences (402 vs 286 tok/s), the GEMM at 64
     // (1045 vs 628 tok/s), where the qmv's eight MMA column groups per k-step bind it.
     auto proj_tc = [&](const bf16* x, int K, const uint32_t* w, const bf16* s, const bf16* b, int N, bf16* y,
                        bool geglu) {
