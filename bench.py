@@ -1,23 +1,28 @@
 #!/usr/bin/env python3
 """Benchmark of the Hyperion hot path on B200 (one JSON line on rank 0).
 
-Default workload (the metric's configuration): the batch-1
-affine Q4/g64 qmv sweep over the Gemma-12B layer shapes, in the proportions one
-decode token uses them: 48 layers x {q 3840x4096, k 3840x2048, v 3840x2048,
-o 4096x3840, gate 3840x15360, up 3840x15360, down 15360x3840} + the tied lm_head
-3840x262144. Every projection has its own weights (6.62 GB per step, far above
-the 126 MB L2, so nothing is re-read from L2 between steps). One step = the 337
-qmv launches of one token, captured in a CUDA graph; value = algorithmic bytes /
-time (GB/s). Per-shape figures are timed separately over >= 48 distinct copies.
+Default workload (the metric's "12B-shaped decode tok/s at 1/2/4/8
+GPUs"): the 48-layer Gemma-12B-shaped Q4/g64 decoder (seeded synthetic weights) prefills
+a 4096-token context and then decodes greedily, one token per step, through the
+reference-facing ABI call hyp_decode_block. With N GPUs the model is tensor-parallel
+over the N ranks (column/row-parallel projections, KV heads sharded, vocab-parallel
+lm_head, all-reduces over NVLink), so `value` is whole-job tokens/s at a fixed model
+(strong scaling). The line also carries:
+  * roofline: the decode projections' kernel (qmv_packed_kernel) over this rank's
+    shapes, timed live with CUDA events on graphs of back-to-back launches over distinct
+    weight copies (inputs larger than L2), mix-weighted by one token's launches;
+  * qmv_sweep (N = 1): the config-1 qmv shapes, the metric's first half;
+  * parity (N > 1): 16 greedy steps of the tensor-parallel run teacher-forced against
+    the same model at TP = 1 on rank 0;
+  * cpu_baseline (N = 1): a full 48-layer decode token on the host cores (the oracle's
+    multithreaded C kernels; the reference's own CPU path is MLX, unavailable here).
 
-`--workload decode` times the engine's full 12B-shaped decode (config 3) through
-hyp_decode_block after a 4096-token prefill: tokens/s. `--workload attn-decode` times
-the fused decode attention alone over the model's 48 layer caches; `--workload
-qmv-shape` one qmv shape (both for profiling). `--workload spec-verify` times greedy
-speculative verify passes (hyb_verify) of 1/3/7 drafts beside a plain decode step.
+Other workloads (profiling and config 2/4 measurements): `--workload qmv` (the config-1
+sweep in 12B decode-token proportions, GB/s), `qmv-shape`, `attn-decode`, `qmm`,
+`sdpa-prefill`, `spec-verify`, `tp-decode` (27B-shaped, config 4).
 
-`--impl reference` times the CPU restatement of the same qmv (the reference's
-own path is MLX, unavailable here) on the host cores.
+`--impl reference` times the CPU restatement of the default workload (full decode
+tokens on all host cores) on rank 0.
 """
 from __future__ import annotations
 
@@ -68,7 +73,7 @@ class ClockSampler:
              "clocks_event_reasons.sw_power_cap")
         try:
             self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.idx), f"--query-gpu={q}",
-                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                          "--format=csv,noheader,nounits", "-lms", "100"],
                                          stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
         except Exception:
             self.proc = None
@@ -153,7 +158,7 @@ def cpu_qmv_baseline(budget_s: float = 10.0):
         b = f32_to_bf16_bits(-8 * (s.astype(np.uint32) << 16).view(np.float32))
         x = f32_to_bf16_bits(rng.standard_normal(K, dtype=np.float32))
         data.append((K, N, x, w, s, b))
-    threads = go.lib().orc_max_threads()
+    threads = go.host_threads()
     for K, N, x, w, s, b in data:  # warm-up pass
         go.qmv_fast(x, w, s, b, threads)
     total_bytes, t0, passes = 0, time.perf_counter(), 0
@@ -170,96 +175,140 @@ def cpu_qmv_baseline(budget_s: float = 10.0):
                       f"oracle/hyp_oracle.c orc_qmv_fast, OpenMP {threads} threads"}
 
 
+class CpuDecode:
+    """Full 12B-shaped decode tokens on the host cores: the reference's CPU path restated
+    with the oracle's multithreaded C kernels (orc_qmv_fast: fp32 group dots, the way a
+    tuned CPU quantized matmul accumulates; orc_sdpa: fp32-or-better attention).
+
+    Every step runs all 48 layers: input norm, the fused q/k/v projection, QK-norm, RoPE,
+    cache append, attention over 1024 ring keys (sliding) or every cached key (global),
+    o_proj, residual and norms, gate/up, GeGLU, down_proj, layer scalar, then the final
+    norm, the 262144-row lm_head, the soft-cap and the greedy scan. Weights are the
+    seeded synthetic model; the caches hold random keys for a `ctx`-token context. The
+    ring is read in slot order rather than position order (same cost, no gather), so
+    this is a timing port, not a parity path (parity lives in tests/)."""
+
+    def __init__(self, ctx: int, threads: int, extra_steps: int = 256, seed: int = 1):
+        import numpy as np
+        from oracle import gemma_oracle as go
+        from hyperion_b200.synth import config3
+        self.go, self.np = go, np
+        self.geo = geo = config3()
+        self.threads = threads
+        ztab = go.normal_table()
+        H, I, nh, hd = geo.hidden_size, geo.intermediate_size, geo.num_attention_heads, geo.head_dim_local
+        rng = np.random.default_rng(seed)
+        tag = [seed * 1000003]
+
+        def nxt():
+            tag[0] += 1
+            return tag[0]
+
+        self.lm = go.synth_q4(nxt(), geo.vocab_size, H, ztab=ztab, nthreads=threads)
+        self.final_norm = go.synth_norm(nxt(), H, ztab)
+        self.layers = []
+        for i, kind in enumerate(geo.layer_types):
+            nkv = geo.n_kv(i)
+            rows = nh * hd + (1 if kind == 1 else 2) * nkv * hd
+            cap = geo.sliding_window + 8 if kind == 0 else ctx + extra_steps
+            lay = {"kind": kind, "qkv": go.synth_q4(nxt(), rows, H, ztab=ztab, nthreads=threads),
+                   "o": go.synth_q4(nxt(), H, nh * hd, ztab=ztab, nthreads=threads),
+                   "gate": go.synth_q4(nxt(), I, H, ztab=ztab, nthreads=threads),
+                   "up": go.synth_q4(nxt(), I, H, ztab=ztab, nthreads=threads),
+                   "down": go.synth_q4(nxt(), H, I, ztab=ztab, nthreads=threads),
+                   "norms": [go.synth_norm(nxt(), n, ztab) for n in (hd, hd, H, H, H, H, 1)],
+                   "k": rng.integers(0x3800, 0x3F00, size=(cap, nkv, hd), dtype=np.uint16),
+                   "v": rng.integers(0x3800, 0x3F00, size=(cap, nkv, hd), dtype=np.uint16)}
+            self.layers.append(lay)
+        self.inv_l = go.rope_inv_freq(hd, geo.rope_theta_local, False, 0.0)
+        self.inv_g = go.rope_inv_freq(geo.head_dim_global, geo.rope_theta_global, True,
+                                      geo.partial_rotary_factor_global)
+        self.pos = ctx
+        self.token = 7
+
+    def step(self) -> int:
+        go, np, geo, nt = self.go, self.np, self.geo, self.threads
+        H, nh, eps = geo.hidden_size, geo.num_attention_heads, geo.rms_norm_eps
+        w, s, b = self.lm
+        codes = np.zeros(H, dtype=np.float32)
+        for i in range(8):
+            codes[i::8] = ((w[self.token] >> np.uint32(4 * i)) & np.uint32(15)).astype(np.float32)
+        g = codes.reshape(-1, 64) * go.fl(s[self.token])[:, None] + go.fl(b[self.token])[:, None]
+        h = go.bf(go.fl(go.bf(g.reshape(-1))) * 62.0)
+        pos = self.pos
+        for lay in self.layers:
+            qn, kn, in_ln, post_attn, pre_ff, post_ff, scal = lay["norms"]
+            kind = lay["kind"]
+            k_c, v_c = lay["k"], lay["v"]
+            nkv, hd = k_c.shape[1], k_c.shape[2]
+            xn = go.rms_norm(h.reshape(1, H), in_ln, eps)
+            qkv = go.qmv_fast(xn, *lay["qkv"], nt)
+            q = go.rope(go.rms_norm(qkv[:nh * hd].reshape(1, nh, hd), qn, eps), pos, self.inv_l if kind == 0 else self.inv_g)
+            kr = qkv[nh * hd:(nh + nkv) * hd].reshape(1, nkv, hd)
+            k = go.rope(go.rms_norm(kr, kn, eps), pos, self.inv_l if kind == 0 else self.inv_g)
+            v = go.rms_norm(kr if kind == 1 else qkv[(nh + nkv) * hd:].reshape(1, nkv, hd), None, eps)
+            slot = pos % k_c.shape[0]
+            k_c[slot], v_c[slot] = k[0], v[0]
+            n = min(geo.sliding_window, pos + 1) if kind == 0 else pos + 1
+            att = go.sdpa(q, k_c[:n], v_c[:n], pos, pos - n + 1, 0, nthreads=nt)
+            o = go.qmv_fast(att.reshape(-1), *lay["o"], nt)
+            h1 = go.bf(go.fl(h) + go.fl(go.rms_norm(o.reshape(1, H), post_attn, eps)).reshape(-1))
+            xin = go.rms_norm(h1.reshape(1, H), pre_ff, eps)
+            act = go.bf(go.fl(go.gelu_tanh(go.qmv_fast(xin, *lay["gate"], nt))) * go.fl(go.qmv_fast(xin, *lay["up"], nt)))
+            dn = go.qmv_fast(act, *lay["down"], nt)
+            h2 = go.bf(go.fl(h1) + go.fl(go.rms_norm(dn.reshape(1, H), post_ff, eps)).reshape(-1))
+            h = go.bf(go.fl(h2) * go.fl(scal)[0])
+        logits = go.softcap(go.qmv_fast(go.rms_norm(h.reshape(1, H), self.final_norm, eps), *self.lm, nt),
+                            geo.final_logit_softcapping)
+        self.token = go.greedy(logits)[0]
+        self.pos += 1
+        return self.token
+
+
 def cpu_decode_baseline(ctx: int, budget_s: float = 10.0):
-    """CPU tokens/s of the 12B-shaped decode step, from a bounded sample.
-
-    One decoder layer's four fused projections (qkv 3840x8192, o 4096x3840, gate/up
-    3840x30720, down 15360x3840), the lm_head (3840x262144), one sliding-window and
-    one global attention at `ctx` are each timed with the oracle's multithreaded C
-    kernels; a token costs 48 x projections + lm_head + 40 x local + 8 x global
-    attention (norms and elementwise work are left out, which favours the CPU).
-    """
-    import numpy as np
+    """CPU tokens/s of full 12B-shaped decode tokens (CpuDecode) for about budget_s."""
     from oracle import gemma_oracle as go
-    from hyperion_b200.synth import f32_to_bf16_bits
-    rng = np.random.default_rng(0)
-    threads = go.lib().orc_max_threads()
-
-    def q4(N, K):
-        w = rng.integers(0, 2 ** 32, size=(N, K // 8), dtype=np.uint32)
-        s = f32_to_bf16_bits(np.abs(rng.standard_normal((N, K // 64), dtype=np.float32)) * 0.02)
-        b = f32_to_bf16_bits(-8 * (s.astype(np.uint32) << 16).view(np.float32))
-        return w, s, b
-
-    projs = [(3840, 8192), (4096, 3840), (3840, 30720), (15360, 3840)]
-    layer = [(K, q4(N, K), f32_to_bf16_bits(rng.standard_normal(K, dtype=np.float32))) for K, N in projs]
-    lm = (3840, q4(262144, 3840), f32_to_bf16_bits(rng.standard_normal(3840, dtype=np.float32)))
-    H, Hkv, D = 16, 8, 256
-    q = f32_to_bf16_bits(rng.standard_normal((1, H, D), dtype=np.float32))
-    kv = {n: (f32_to_bf16_bits(rng.standard_normal((n, Hkv, D), dtype=np.float32)),
-              f32_to_bf16_bits(rng.standard_normal((n, Hkv, D), dtype=np.float32))) for n in (1024, ctx)}
-
-    def timed(fn, share):
-        fn()  # warm-up
-        t0, n = time.perf_counter(), 0
-        while True:
-            fn()
-            n += 1
-            if time.perf_counter() - t0 >= share:
-                return (time.perf_counter() - t0) / n
-
-    t_layer = timed(lambda: [go.qmv_fast(x, *wsb, threads) for _, wsb, x in layer], 0.4 * budget_s)
-    t_lm = timed(lambda: go.qmv_fast(lm[2], *lm[1], threads), 0.3 * budget_s)
-    t_loc = timed(lambda: go.sdpa(q, *kv[1024], ctx - 1, ctx - 1024, 0, nthreads=threads), 0.15 * budget_s)
-    t_glb = timed(lambda: go.sdpa(q, *kv[ctx], ctx - 1, 0, 0, nthreads=threads), 0.15 * budget_s)
-    t_tok = 48 * t_layer + t_lm + 40 * t_loc + 8 * t_glb
-    return {"value": round(1.0 / t_tok, 3), "unit": "tok/s", "cores": threads, "kind": "port",
-            "sample": f"one layer's 4 projections ({t_layer * 1e3:.1f} ms), lm_head ({t_lm * 1e3:.1f} ms), "
-                      f"1024-key and {ctx}-key attention ({t_loc * 1e3:.2f} / {t_glb * 1e3:.2f} ms) timed with "
-                      f"oracle/hyp_oracle.c (OpenMP {threads} threads) for ~{budget_s:.0f} s, "
-                      "scaled to 48 layers (40 local, 8 global)"}
+    threads = go.host_threads()
+    cpu = CpuDecode(ctx, threads)
+    cpu.step()  # warm-up (first touch of the caches, thread pool start)
+    t0, n = time.perf_counter(), 0
+    while True:
+        cpu.step()
+        n += 1
+        if time.perf_counter() - t0 >= budget_s:
+            break
+    el = time.perf_counter() - t0
+    return {"value": round(n / el, 3), "unit": "tok/s", "cores": threads, "kind": "port",
+            "sample": f"{n} full cfg3 decode tokens (48 layers + lm_head) at ctx {ctx} in {el:.1f} s, oracle C "
+                      f"kernels (orc_qmv_fast, orc_sdpa) on {threads} host threads"}
 
 
 def run_reference(args):
+    """The reference arm: the default workload's CPU restatement (full 12B-shaped decode
+    tokens, all host cores) on rank 0; other ranks exit at once."""
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
-    import numpy as np
     from oracle import gemma_oracle as go
-    from hyperion_b200.synth import f32_to_bf16_bits
-    rng = np.random.default_rng(0)
-    shapes = [(3840, 4096), (3840, 2048), (4096, 3840), (3840, 15360), (15360, 3840), (3840, 262144)]
-    data = []
-    for K, N in shapes:
-        w = rng.integers(0, 2 ** 32, size=(N, K // 8), dtype=np.uint32)
-        s = f32_to_bf16_bits(np.abs(rng.standard_normal((N, K // 64), dtype=np.float32)) * 0.02)
-        b = f32_to_bf16_bits(-8 * (s.astype(np.uint32) << 16).view(np.float32))
-        x = f32_to_bf16_bits(rng.standard_normal(K, dtype=np.float32))
-        data.append((K, N, x, w, s, b))
-    threads = go.lib().orc_max_threads()
-    step_bytes = sum(qmv_bytes(K, N) for K, N, *_ in data)
-
-    def step():
-        for K, N, x, w, s, b in data:
-            go.qmv_fast(x, w, s, b, threads)
-
+    threads = go.host_threads()
+    cpu = CpuDecode(args.ctx, threads, extra_steps=args.warmup + args.steps + 8)
     for _ in range(args.warmup):
-        step()
+        cpu.step()
     t0 = time.perf_counter()
     for _ in range(args.steps):
-        step()
+        cpu.step()
     el = time.perf_counter() - t0
-    v = step_bytes * args.steps / el / 1e9
-    line = {"impl": "reference", "metric": METRIC, "value": round(v, 2), "unit": "GB/s", "n_gpus": args.gpus,
+    v = args.steps / el
+    line = {"impl": "reference", "metric": METRIC, "value": round(v, 3), "unit": "tok/s", "n_gpus": args.gpus,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(el / args.steps * 1e3, 3),
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "u4/bf16->f32",
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "u4/bf16->f32",
             "data": "synthetic",
-            "config": {"workload": "cfg1 qmv sweep: the six Gemma-12B qmv shapes once per step (655 MB)",
-                       "l2": "inputs larger than L2"},
-            "cpu_baseline": {"value": round(v, 2), "unit": "GB/s", "cores": threads, "kind": "port",
-                             "sample": f"{args.steps} steps of the six cfg-1 shapes, orc_qmv_fast "
-                                       f"(the reference's MLX CPU path is not installable here)"},
-            "e2e": {"value": round(v, 2), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+            "config": {"workload": f"cfg3 12B-shaped decode, ctx {args.ctx}, batch 1", "l2": "inputs larger than L2"},
+            "cpu_baseline": {"value": round(v, 3), "unit": "tok/s", "cores": threads, "kind": "port",
+                             "sample": f"{args.steps} full decode tokens (48 layers + lm_head) at ctx {args.ctx}, "
+                                       f"oracle C kernels on {threads} host threads (the reference's MLX CPU path "
+                                       f"is not installable here)"},
+            "e2e": {"value": round(v, 3), "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
 
 
@@ -273,6 +322,8 @@ def make_q4(N, K, gen, device):
 
 
 def run_qmv(args, rank, world, local):
+    """`--workload qmv`: the config-1 sweep as one graph of 337 launches per step (every
+    projection of a 12B decode token with its own weights), replicated per rank."""
     import torch
     import ctypes
     import hyperion_b200 as hb
@@ -417,7 +468,8 @@ def run_qmv(args, rank, world, local):
         with open(tp) as f:
             traffic = json.load(f).get("dram_bytes_per_launch_mix")
     line = {
-        "metric": METRIC, "value": round(value, 1), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+        "metric": "cfg1 Q4/g64 qmv HBM GB/s (12B decode-token mix)", "value": round(value, 1), "unit": "GB/s",
+        "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(ms_max, 4), "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "u4/bf16->f32", "data": "synthetic",
         "config": {"workload": "cfg1 qmv sweep in 12B decode-token proportions: 48 x {q,k,v,o,gate,up,down} "
@@ -588,29 +640,136 @@ def run_qmv_shape(args, rank, world, local):
                           "GB/s": round(nbytes / (us * 1e-6) / 1e9, 1), "bytes_per_launch": nbytes}), flush=True)
 
 
-# ------------------------------------------------------------------ 12B decode (ours)
+# ------------------------------------------------------------------ 12B decode (ours, default)
+L2_BYTES = 126 * 2 ** 20
+
+
+def time_qmv_shapes(shapes, dev, stream, rounds=5):
+    """Per-launch time of qmv_packed_kernel for each (name, K, N, prologue, epilogue):
+    a CUDA graph of back-to-back launches over distinct packed weight copies (together
+    more than 2x L2, so every launch streams its weights from HBM), timed with CUDA events
+    on the launching stream after a warm-up replay. Returns {name: microseconds}."""
+    import torch
+    from hyperion_b200 import ops
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(4321)
+    out = {}
+    for name, K, N, prologue, epilogue in shapes:
+        copies = max(2, -(-2 * L2_BYTES // qmv_bytes(K, N)))
+        bufs = []
+        for _ in range(copies):
+            w, sc, bi = make_q4(N, K, gen, dev)
+            pk = ops.qmv_pack(w, sc, bi)
+            del w, sc, bi
+            x = torch.randn(K, device=dev, generator=gen).to(torch.bfloat16)
+            y = torch.empty(N // 2 if epilogue else N, dtype=torch.bfloat16, device=dev)
+            nw = (1 + 0.02 * torch.randn(K, device=dev, generator=gen)).to(torch.bfloat16)
+            rs = torch.randn(K, device=dev, generator=gen).to(torch.bfloat16)
+            ho = torch.empty(K, dtype=torch.bfloat16, device=dev)
+            bufs.append((pk, x, y, nw, rs, ho))
+
+        def launch_all():
+            for pk, x, y, nw, rs, ho in bufs:
+                if prologue == 2:
+                    ops.qmv_packed(x, pk, K, N, prologue=2, epilogue=epilogue, norm_w=nw, resid=rs, post_w=nw,
+                                   h_out=ho, out=y, stream=stream)
+                else:
+                    ops.qmv_packed(x, pk, K, N, prologue=prologue, epilogue=epilogue, norm_w=nw, out=y,
+                                   stream=stream)
+
+        torch.cuda.synchronize()
+        with torch.cuda.stream(stream):
+            launch_all()
+        torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=stream):
+            launch_all()
+        with torch.cuda.stream(stream):
+            g.replay()
+            torch.cuda.synchronize()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            for _ in range(rounds):
+                g.replay()
+            e1.record(stream)
+            torch.cuda.synchronize()
+        out[name] = e0.elapsed_time(e1) * 1e3 / (rounds * copies)
+        del g, bufs
+    torch.cuda.empty_cache()
+    return out
+
+
+def decode_shapes(T: int):
+    """The decode projections of the 12B-shaped model on one of T tensor-parallel ranks,
+    as the engine launches them: (name, K, N, prologue, epilogue, launches per token).
+    Prologue 1 = norm, 2 = residual + norm; epilogue 1 = GeGLU over interleaved rows."""
+    return [("qkv_sliding", 3840, 8192 // T, 2, 0, 40), ("qkv_global", 3840, 6144 // T, 2, 0, 8),
+            ("o", 4096 // T, 3840, 0, 0, 48), ("gate_up", 3840, 30720 // T, 2, 1, 48),
+            ("down", 15360 // T, 3840, 0, 0, 48), ("lm_head", 3840, 262144 // T, 2, 0, 1)]
+
+
 def run_decode(args, rank, world, local):
+    """The default workload: cfg3 decode through hyp_decode_block, tensor-parallel over
+    the job's ranks (see the module docstring)."""
     import torch
     import hyperion_b200 as hb
     from hyperion_b200.synth import config3
     geo = config3()
-    eng = hb.Engine(geo, synthetic_seed=1 + rank)
+    why = hb.tp_shard_check(geo, world)
+    if why:
+        raise SystemExit(f"config 3 does not split over {world} ranks: {why}")
+    tp = None
+    if world > 1:
+        import torch.distributed as dist
+        obj = [hb.nccl_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(obj, src=0)
+        tp = (rank, world, obj[0])
+    dev = torch.device("cuda", local)
+    seed = 1
+    t0 = time.perf_counter()
+    eng = hb.Engine(geo, synthetic_seed=seed, tp=tp)
+    load_s = max_over_ranks(time.perf_counter() - t0, world)
     ctx = args.ctx
     prompt = [int(t) for t in torch.randint(0, geo.vocab_size, (ctx,), generator=torch.Generator().manual_seed(5))]
-    warm = eng.new_kv()  # first prefill pays one-time costs (module load, pools, tensor maps)
+    warm = eng.new_kv()  # the first prefill pays one-time costs (module load, pools, tensor maps)
     warm.prefill(prompt)
-    del warm
+    warm.close()
     kv = eng.new_kv()
+    barrier(world)
     torch.cuda.synchronize()
     t0 = time.perf_counter()
-    kv.prefill(prompt)
-    prefill_s = time.perf_counter() - t0
+    f0, _ = kv.prefill(prompt)
+    prefill_s = max_over_ranks(time.perf_counter() - t0, world)
+
+    # parity of the tensor-parallel run: 16 greedy steps, teacher-forced against TP = 1
+    parity = None
+    if world > 1:
+        toks = [f0.token_id]
+        for _ in range(16):
+            f, _ = kv.decode(1)
+            toks.append(f.token_id)
+        barrier(world)
+        if rank == 0:
+            ref = hb.Engine(geo, synthetic_seed=seed)
+            rkv = ref.new_kv()
+            rf, _ = rkv.prefill(prompt)
+            agree = [rf.token_id == toks[0]]
+            for i in range(16):
+                f, _ = rkv.decode(1, forced=toks[i])
+                agree.append(f.token_id == toks[i + 1])
+            rkv.close()
+            ref.close()
+            torch.cuda.empty_cache()
+            parity = {"vs": "same model at TP 1 on rank 0, teacher-forced", "steps": 17,
+                      "greedy_agreement": round(sum(agree) / len(agree), 4)}
+        barrier(world)
+
     stream = torch.cuda.ExternalStream(eng.stream())
-    for _ in range(args.warmup):
-        kv.decode(1)
-    barrier(world)
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(local) as clk:
+        for _ in range(args.warmup):
+            kv.decode(1)
+        barrier(world)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         torch.cuda.synchronize()
         w0 = time.perf_counter()
         e0.record(stream)
@@ -619,34 +778,73 @@ def run_decode(args, rank, world, local):
         e1.record(stream)
         torch.cuda.synchronize()
         wall_ms = (time.perf_counter() - w0) * 1e3 / args.steps
-    ms = max_over_ranks(e0.elapsed_time(e1) / args.steps, world)
-    wall_ms = max_over_ranks(wall_ms, world)
-    tok_s = world / (ms * 1e-3)
+        ms = max_over_ranks(e0.elapsed_time(e1) / args.steps, world)
+        wall_ms = max_over_ranks(wall_ms, world)
+        # the dominant kernel, live: the decode projections at this rank's shapes
+        qstream = torch.cuda.Stream(device=dev)
+        shapes = decode_shapes(world)
+        per = time_qmv_shapes([sh[:5] for sh in shapes], dev, qstream)
+        sweep = None
+        if world == 1 and not args.no_sweep:
+            cfg1 = PROJ + [LM_HEAD]
+            sp = time_qmv_shapes([(nm, K, N, 0, 0) for nm, K, N in cfg1], dev, qstream)
+            sb = 48 * sum(qmv_bytes(K, N) for _, K, N in PROJ) + qmv_bytes(LM_HEAD[1], LM_HEAD[2])
+            st = 48 * sum(sp[nm] for nm, _, _ in PROJ) + sp[LM_HEAD[0]]
+            sweep = {"workload": "cfg1 shapes in 12B decode-token proportions (48 x q,k,v,o,gate,up,down + "
+                                 "lm_head), no prologue",
+                     "value": round(sb / (st * 1e-6) / 1e9, 1), "unit": "GB/s",
+                     "frac": round(sb / (st * 1e-6) / 1e9 / peaks()[0], 4),
+                     "per_shape": [{"shape": f"{nm} K={K} N={N}", "us": round(sp[nm], 2),
+                                    "frac": round(qmv_bytes(K, N) / (sp[nm] * 1e-6) / 1e9 / peaks()[0], 3)}
+                                   for nm, K, N in cfg1]}
+    tok_s = 1e3 / ms
     if rank != 0:
         return
-    # kernels per token: embed, 5 per layer (qkv, fused attention, o, gate/up+GeGLU, down),
-    # lm_head and the two soft-cap/top-k stages
-    launches_per_step = 1 + 5 * len(geo.layer_types) + 3
-    w_bytes = 48 * sum(qmv_bytes(K, N) for _, K, N in PROJ) + qmv_bytes(3840, 262144)
+    hbm, _, src = peaks()
+    mix_bytes = sum(c * qmv_bytes(K, N) for _, K, N, _, _, c in shapes)
+    mix_us = sum(c * per[nm] for nm, _, _, _, _, c in shapes)
+    achieved = mix_bytes / (mix_us * 1e-6) / 1e9
+    # whole-step bytes per token on this rank: its weight shard + its KV heads
     kv_bytes = 0
     for i, kind in enumerate(geo.layer_types):
         n = min(geo.sliding_window, ctx + args.warmup) if kind == 0 else ctx + args.warmup
-        kv_bytes += 2 * n * geo.n_kv(i) * geo.head_dim(i) * 2
-    hbm, _, src = peaks()
-    bytes_tok = w_bytes + kv_bytes
+        kv_bytes += 2 * n * geo.n_kv(i) * geo.head_dim(i) * 2 // world
+    step_bytes = mix_bytes + kv_bytes
+    traffic = None
+    tp_path = os.path.join(REPO, "profiles", "qmv_traffic.json")
+    if os.path.exists(tp_path) and world == 1:
+        with open(tp_path) as f:
+            traffic = json.load(f).get("dram_bytes_per_launch_decode_mix")
+    # our kernels per token: embed, 5 per layer (qkv, fused attention, o, gate/up, down),
+    # lm_head, soft-cap/top-k stages 1 and 2, and with TP the candidate kernel
+    launches_per_step = 1 + 5 * len(geo.layer_types) + 3 + (1 if world > 1 else 0)
     line = {"metric": METRIC, "value": round(tok_s, 2), "unit": "tok/s", "n_gpus": world, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "weak",
+            "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "strong",
             "vs_baseline": None, "dtype": "u4/bf16->f32", "data": "synthetic",
-            "config": {"workload": f"cfg3 12B-shaped decode, ctx {ctx}, batch 1", "prefill_s": round(prefill_s, 3),
-                       "prefill_tok_s": round(ctx / prefill_s, 1),
-                       "l2": "inputs larger than L2"},
-            "roofline": {"bound": "hbm", "achieved": round(bytes_tok / (ms * 1e-3) / 1e9, 1), "peak": hbm,
-                         "unit": "GB/s", "frac": round(bytes_tok / (ms * 1e-3) / 1e9 / hbm, 4), "traffic": None,
-                         "peak_source": src, "kernel": "whole decode step (weights + KV bytes per token)"},
+            "config": {"workload": f"cfg3 12B-shaped decode, ctx {ctx}, batch 1", "parallelism": f"tp{world}",
+                       "load_s": round(load_s, 2), "prefill_s": round(prefill_s, 3),
+                       "prefill_tok_s": round(ctx / prefill_s, 1), "l2": "inputs larger than L2 (6.6 GB of "
+                       "weights per token; roofline copies > 2x L2)"},
+            "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s",
+                         "frac": round(achieved / hbm, 4), "traffic": traffic, "peak_source": src,
+                         "kernel": "qmv_packed_kernel, mix-weighted over one token's decode projections at this "
+                                   "rank's shapes (CUDA events, back-to-back graph launches)"},
+            "per_shape": [{"shape": f"{nm} K={K} N={N}", "launches_per_token": c, "us": round(per[nm], 2),
+                           "frac": round(qmv_bytes(K, N) / (per[nm] * 1e-6) / 1e9 / hbm, 3)}
+                          for nm, K, N, _, _, c in shapes],
+            "step_roofline": {"bytes_per_token_per_rank": step_bytes,
+                              "achieved": round(step_bytes / (ms * 1e-3) / 1e9, 1),
+                              "frac": round(step_bytes / (ms * 1e-3) / 1e9 / hbm, 4)},
             "gpu_launches": launches_per_step * args.steps,
-            "e2e": {"value": round(world / (wall_ms * 1e-3), 2), "unit": "tok/s", "h2d_bytes_per_step": 4,
-                    "d2h_bytes_per_step": 64, "path": "hyp_decode_block(n_tokens=1) via ctypes, host wall clock"},
+            "e2e": {"value": round(1e3 / wall_ms, 2), "unit": "tok/s", "h2d_bytes_per_step": 4,
+                    "d2h_bytes_per_step": 64 if world == 1 else 16 * world,
+                    "path": "hyp_decode_block(n_tokens=1) via ctypes on every rank (token id in, greedy result "
+                            "out each step), host wall clock, max over ranks"},
             "clocks": clk.summary()}
+    if parity is not None:
+        line["parity"] = parity
+    if sweep is not None:
+        line["qmv_sweep"] = sweep
     if world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_decode_baseline(ctx, args.cpu_seconds)
     print(json.dumps(line), flush=True)
@@ -868,7 +1066,7 @@ def main():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="qmv",
+    ap.add_argument("--workload", default="decode",
                     choices=["qmv", "decode", "qmv-shape", "attn-decode", "qmm", "tp-decode", "sdpa-prefill",
                              "spec-verify"])
     ap.add_argument("--drafts", default="1,3,7", help="draft lengths for --workload spec-verify (1..8)")
@@ -879,6 +1077,7 @@ def main():
     ap.add_argument("--batch", type=int, default=1, help="tp-decode: sequences decoded per step (1..64)")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-sweep", action="store_true", help="decode: skip the config-1 qmv sweep keys")
 
     args = ap.parse_args()
     if args.warmup < 3:

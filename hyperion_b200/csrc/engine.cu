@@ -81,7 +81,17 @@ int num_sms() {
 }
 
 // ---------------------------------------------------------------- synthetic init kernels
+//
+// Every synthetic value is a pure function of (seed, element key) built from integer
+// hashing and IEEE single-rounded float operations only, so a CPU can regenerate the
+// exact model (the parity tests rebuild the 12B-shaped weights this way instead of
+// shipping gigabytes of checkpoints): codes are the low 32 bits of a SplitMix64 hash,
+// normal deviates are looked up in a table of 65536 standard-normal quantiles indexed by
+// the top 16 hash bits.
 namespace {
+
+constexpr int kNormalTableBits = 16;
+constexpr int kNormalTable = 1 << kNormalTableBits;
 
 __device__ __forceinline__ uint64_t mix64(uint64_t z) {
     z += 0x9E3779B97F4A7C15ull;
@@ -89,11 +99,53 @@ __device__ __forceinline__ uint64_t mix64(uint64_t z) {
     z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
     return z ^ (z >> 31);
 }
-__device__ __forceinline__ float hash_normal(uint64_t key) {
-    const uint64_t a = mix64(key), b = mix64(key ^ 0xD1B54A32D192ED03ull);
-    const float u1 = (static_cast<float>(a >> 40) + 1.0f) * (1.0f / 16777217.0f);
-    const float u2 = static_cast<float>(b >> 40) * (1.0f / 16777216.0f);
-    return sqrtf(-2.0f * logf(u1)) * cospif(2.0f * u2);
+__device__ __forceinline__ float hash_normal(uint64_t key, const float* __restrict__ ztab) {
+    return ztab[mix64(key ^ 0xD1B54A32D192ED03ull) >> (64 - kNormalTableBits)];
+}
+
+// Inverse of the standard normal CDF in double precision: Wichura's algorithm AS 241
+// (PPND16, Applied Statistics 37:477-484, 1988), relative error about 1e-16.
+double normal_quantile(double p) {
+    const double q = p - 0.5;
+    if (std::fabs(q) <= 0.425) {
+        const double r = 0.180625 - q * q;
+        const double num = ((((((2509.0809287301226727 * r + 33430.575583588128105) * r + 67265.770927008700853) * r +
+                                45921.953931549871457) * r + 13731.693765509461125) * r + 1971.5909503065514427) * r +
+                             133.14166789178437745) * r + 3.387132872796366608;
+        const double den = ((((((5226.495278852545561 * r + 28729.085735721942674) * r + 39307.89580009271061) * r +
+                                21213.794301586595867) * r + 5394.1960214247511077) * r + 687.1870074920579083) * r +
+                             42.313330701600911252) * r + 1.0;
+        return q * num / den;
+    }
+    double r = q < 0 ? p : 1.0 - p;
+    r = std::sqrt(-std::log(r));
+    double v;
+    if (r <= 5.0) {
+        r -= 1.6;
+        v = (((((((7.7454501427834140764e-4 * r + 0.0227238449892691845833) * r + 0.24178072517745061177) * r +
+                 1.27045825245236838258) * r + 3.64784832476320460504) * r + 5.7694972214606914055) * r +
+              4.6303378461565452959) * r + 1.42343711074968357734) /
+            (((((((1.05075007164441684324e-9 * r + 5.475938084995344946e-4) * r + 0.0151986665636164571966) * r +
+                 0.14810397642748007459) * r + 0.68976733498510000455) * r + 1.6763848301838038494) * r +
+              2.05319162663775882187) * r + 1.0);
+    } else {
+        r -= 5.0;
+        v = (((((((2.01033439929228813265e-7 * r + 2.71155556874348757815e-5) * r + 0.0012426609473880784386) * r +
+                 0.026532189526576123093) * r + 0.29656057182850489123) * r + 1.7848265399172913358) * r +
+              5.4637849111641143699) * r + 6.6579046435011037772) /
+            (((((((2.04426310338993978564e-15 * r + 1.4215117583164458887e-7) * r + 1.8463183175100546818e-5) * r +
+                 7.868691311456132591e-4) * r + 0.0148753612908506148525) * r + 0.13692988092273580531) * r +
+              0.59983220655588793769) * r + 1.0);
+    }
+    return q < 0 ? -v : v;
+}
+
+// ztab[i] = float(quantile((i + 0.5) / 65536)): a deviate from the top 16 bits of a hash
+std::vector<float> normal_table() {
+    std::vector<float> t(kNormalTable);
+    for (int i = 0; i < kNormalTable; ++i)
+        t[i] = static_cast<float>(normal_quantile((i + 0.5) / static_cast<double>(kNormalTable)));
+    return t;
 }
 
 // A [rows, cols] block of a [*, ld] logical matrix whose element (r, c) is keyed by its
@@ -111,20 +163,20 @@ __global__ void synth_words_kernel(uint32_t* w, Block blk, uint64_t seed) {
         w[i] = static_cast<uint32_t>(mix64(seed * 0x100000001B3ull + blk.key(i)));
 }
 // scales = bf16(|N(0, std)|), biases = bf16(-8 * scales)
-__global__ void synth_sb_kernel(bf16* s, bf16* b, Block blk, uint64_t seed, float std) {
+__global__ void synth_sb_kernel(bf16* s, bf16* b, Block blk, uint64_t seed, float std, const float* ztab) {
     const size_t n = blk.rows * blk.cols;
     for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < n;
          i += static_cast<size_t>(gridDim.x) * blockDim.x) {
-        const bf16 sv = f2bf(fabsf(std * hash_normal(seed * 0x100000001B3ull + blk.key(i))));
+        const bf16 sv = f2bf(fabsf(__fmul_rn(std, hash_normal(seed * 0x100000001B3ull + blk.key(i), ztab))));
         s[i] = sv;
         b[i] = f2bf(-8.0f * bf2f(sv));
     }
 }
-// bf16(mean + std * N(0,1))
-__global__ void synth_normal_kernel(bf16* x, size_t n, uint64_t seed, float mean, float std) {
+// bf16(mean + std * N(0,1)), multiply and add rounded separately (no contraction)
+__global__ void synth_normal_kernel(bf16* x, size_t n, uint64_t seed, float mean, float std, const float* ztab) {
     for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < n;
          i += static_cast<size_t>(gridDim.x) * blockDim.x)
-        x[i] = f2bf(mean + std * hash_normal(seed * 0x100000001B3ull + i));
+        x[i] = f2bf(__fadd_rn(mean, __fmul_rn(std, hash_normal(seed * 0x100000001B3ull + i, ztab))));
 }
 
 __global__ void geglu_interleaved_kernel(const bf16* __restrict__ gu, bf16* __restrict__ act, int I) {
@@ -170,7 +222,8 @@ int grid_for(size_t n) { return static_cast<int>(std::min<size_t>((n + 255) / 25
 
 // Rows [row0, row0 + rows) x columns [col0, col0 + K) of a synthetic [*, K_full] Q4
 // matrix, written at row dst_row of q (whose shape is [q.N, q.K]).
-void synth_block(QLin& q, int dst_row, int rows, int row0, int col0, int K_full, uint64_t seed, cudaStream_t st) {
+void synth_block(QLin& q, int dst_row, int rows, int row0, int col0, int K_full, uint64_t seed, const float* ztab,
+                 cudaStream_t st) {
     const int K = q.K;
     const Block bw{static_cast<size_t>(rows), static_cast<size_t>(K / 8), static_cast<size_t>(K_full / 8),
                    static_cast<size_t>(row0), static_cast<size_t>(col0 / 8)};
@@ -180,7 +233,7 @@ void synth_block(QLin& q, int dst_row, int rows, int row0, int col0, int K_full,
                                                                      seed);
     synth_sb_kernel<<<grid_for(bs.rows * bs.cols), 256, 0, st>>>(q.s.p + static_cast<size_t>(dst_row) * (K / 64),
                                                                  q.b.p + static_cast<size_t>(dst_row) * (K / 64), bs,
-                                                                 seed ^ 0x5151, 0.02f);
+                                                                 seed ^ 0x5151, 0.02f, ztab);
     HYB_LAUNCH_CHECK("synth_block");
 }
 
@@ -192,14 +245,14 @@ void alloc_qlin(QLin& q, int N, int K) {
     q.b.reset(static_cast<size_t>(N) * K / 64);
 }
 
-void synth_qlin(QLin& q, int N, int K, uint64_t seed, cudaStream_t st) {
+void synth_qlin(QLin& q, int N, int K, uint64_t seed, const float* ztab, cudaStream_t st) {
     alloc_qlin(q, N, K);
-    synth_block(q, 0, N, 0, 0, K, seed, st);
+    synth_block(q, 0, N, 0, 0, K, seed, ztab, st);
 }
 
-void synth_norm(DevPtr<bf16>& d, size_t n, uint64_t seed, cudaStream_t st) {
+void synth_norm(DevPtr<bf16>& d, size_t n, uint64_t seed, const float* ztab, cudaStream_t st) {
     d.reset(n);
-    synth_normal_kernel<<<grid_for(n), 256, 0, st>>>(d.p, n, seed, 1.0f, 0.02f);
+    synth_normal_kernel<<<grid_for(n), 256, 0, st>>>(d.p, n, seed, 1.0f, 0.02f, ztab);
     HYB_LAUNCH_CHECK("synth_norm");
 }
 
@@ -311,34 +364,38 @@ void Model::load_synthetic(const Geometry& g, uint64_t seed) {
     }
     const int H = static_cast<int>(g.hidden), I = static_cast<int>(g.intermediate);
     const int r = tp_rank_, T = tp_size_;
+    const std::vector<float> table = normal_table();
+    DevPtr<float> zt(table.size());
+    HYB_CUDA(cudaMemcpy(zt.p, table.data(), table.size() * sizeof(float), cudaMemcpyHostToDevice));
+    const float* ztab = zt.p;
     uint64_t tag = seed * 1000003ull;
-    synth_qlin(embed_, static_cast<int>(g.vocab), H, ++tag, stream_);  // replicated table
-    synth_norm(final_norm_, H, ++tag, stream_);
+    synth_qlin(embed_, static_cast<int>(g.vocab), H, ++tag, ztab, stream_);  // replicated table
+    synth_norm(final_norm_, H, ++tag, ztab, stream_);
     for (auto& L : layers_) {
         // q/k/v: this rank's head rows of the TP = 1 [q; k; v] matrix
-        const int qf = static_cast<int>(g.n_heads) * L.hd, kf = L.k_rows * T, vf = L.v_rows * T;
+        const int qf = static_cast<int>(g.n_heads) * L.hd, kf = L.k_rows * T;
         alloc_qlin(L.qkv, L.q_rows + L.k_rows + L.v_rows, H);
         const uint64_t tq = ++tag;
-        synth_block(L.qkv, 0, L.q_rows, r * L.q_rows, 0, H, tq, stream_);
-        synth_block(L.qkv, L.q_rows, L.k_rows, qf + r * L.k_rows, 0, H, tq, stream_);
-        if (L.v_rows) synth_block(L.qkv, L.q_rows + L.k_rows, L.v_rows, qf + kf + r * L.v_rows, 0, H, tq, stream_);
-        (void)vf;
+        synth_block(L.qkv, 0, L.q_rows, r * L.q_rows, 0, H, tq, ztab, stream_);
+        synth_block(L.qkv, L.q_rows, L.k_rows, qf + r * L.k_rows, 0, H, tq, ztab, stream_);
+        if (L.v_rows)
+            synth_block(L.qkv, L.q_rows + L.k_rows, L.v_rows, qf + kf + r * L.v_rows, 0, H, tq, ztab, stream_);
         // o: all rows, this rank's heads' K range
         alloc_qlin(L.o, H, L.q_rows);
-        synth_block(L.o, 0, H, 0, r * L.q_rows, qf, ++tag, stream_);
+        synth_block(L.o, 0, H, 0, r * L.q_rows, qf, ++tag, ztab, stream_);
         // gate/up interleaved by 16-row tiles: this rank's contiguous range of tiles
         alloc_qlin(L.gateup, 2 * inter_local_, H);
-        synth_block(L.gateup, 0, 2 * inter_local_, r * 2 * inter_local_, 0, H, ++tag, stream_);
+        synth_block(L.gateup, 0, 2 * inter_local_, r * 2 * inter_local_, 0, H, ++tag, ztab, stream_);
         // down: all rows, this rank's K range of the MLP
         alloc_qlin(L.down, H, inter_local_);
-        synth_block(L.down, 0, H, 0, r * inter_local_, I, ++tag, stream_);
-        synth_norm(L.q_norm, L.hd, ++tag, stream_);
-        synth_norm(L.k_norm, L.hd, ++tag, stream_);
-        synth_norm(L.in_ln, H, ++tag, stream_);
-        synth_norm(L.post_attn, H, ++tag, stream_);
-        synth_norm(L.pre_ff, H, ++tag, stream_);
-        synth_norm(L.post_ff, H, ++tag, stream_);
-        synth_norm(L.scalar, 1, ++tag, stream_);
+        synth_block(L.down, 0, H, 0, r * inter_local_, I, ++tag, ztab, stream_);
+        synth_norm(L.q_norm, L.hd, ++tag, ztab, stream_);
+        synth_norm(L.k_norm, L.hd, ++tag, ztab, stream_);
+        synth_norm(L.in_ln, H, ++tag, ztab, stream_);
+        synth_norm(L.post_attn, H, ++tag, ztab, stream_);
+        synth_norm(L.pre_ff, H, ++tag, ztab, stream_);
+        synth_norm(L.post_ff, H, ++tag, ztab, stream_);
+        synth_norm(L.scalar, 1, ++tag, ztab, stream_);
     }
     HYB_CUDA(cudaStreamSynchronize(stream_));
     pack_all();

@@ -37,7 +37,7 @@ def build() -> str:
     out = os.path.join(HERE, "liboracle.so")
     src = os.path.join(HERE, "hyp_oracle.c")
     if not os.path.exists(out) or os.path.getmtime(out) < os.path.getmtime(src):
-        _run(["gcc", "-O3", "-march=x86-64-v2", "-fopenmp", "-fPIC", "-shared", "-std=c11",
+        _run(["gcc", "-O3", "-march=x86-64-v2", "-ffp-contract=off", "-fopenmp", "-fPIC", "-shared", "-std=c11",
               src, "-o", out + ".tmp", "-lm"])
         os.replace(out + ".tmp", out)
     return out

@@ -64,6 +64,13 @@ def lib() -> ctypes.CDLL:
                                ctypes.c_float, ctypes.c_float, ctypes.c_int, P, ctypes.c_int]
         L.orc_unpack_row.argtypes = [P, i64, i64, P]
         L.orc_max_threads.restype = ctypes.c_int
+        u64 = ctypes.c_uint64
+        L.orc_normal_quantile.argtypes = [ctypes.c_double]
+        L.orc_normal_quantile.restype = ctypes.c_double
+        L.orc_normal_table.argtypes = [P]
+        L.orc_synth_words.argtypes = [u64, i64, i64, i64, i64, i64, P, ctypes.c_int]
+        L.orc_synth_sb.argtypes = [u64, i64, i64, i64, i64, i64, ctypes.c_float, P, P, P, ctypes.c_int]
+        L.orc_synth_normal.argtypes = [u64, i64, ctypes.c_float, ctypes.c_float, P, P]
         _LIB = L
     return _LIB
 
@@ -440,3 +447,93 @@ class OracleModel:
             kv["last_token"] = tok
             out.append((tok, logit, tie, lg))
         return out
+
+
+# ----------------------------------------------------------------------------- synthetic models
+
+_U64 = (1 << 64) - 1
+
+
+def host_threads() -> int:
+    """Every core this process may run on (OMP_NUM_THREADS, which torchrun sets to 1,
+    does not limit the oracle's explicit thread counts)."""
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:  # pragma: no cover
+        return os.cpu_count() or 1
+
+
+def normal_table() -> np.ndarray:
+    t = np.empty(65536, dtype=np.float32)
+    lib().orc_normal_table(_p(t))
+    return t
+
+
+def synth_q4(seed: int, rows: int, K: int, row0: int = 0, col0: int = 0, K_full: Optional[int] = None,
+             ztab: Optional[np.ndarray] = None, nthreads: int = 0):
+    """Rows [row0, row0 + rows) x columns [col0, col0 + K) of a synthetic [*, K_full]
+    Q4/g64 matrix exactly as the engine's synthetic loader generates them."""
+    K_full = K if K_full is None else K_full
+    ztab = normal_table() if ztab is None else ztab
+    nt = nthreads or host_threads()
+    w = np.empty((rows, K // 8), dtype=np.uint32)
+    s = np.empty((rows, K // 64), dtype=np.uint16)
+    b = np.empty((rows, K // 64), dtype=np.uint16)
+    lib().orc_synth_words(seed & _U64, rows, K // 8, K_full // 8, row0, col0 // 8, _p(w), nt)
+    lib().orc_synth_sb((seed ^ 0x5151) & _U64, rows, K // 64, K_full // 64, row0, col0 // 64, 0.02, _p(ztab),
+                       _p(s), _p(b), nt)
+    return w, s, b
+
+
+def synth_norm(seed: int, n: int, ztab: np.ndarray) -> np.ndarray:
+    out = np.empty(n, dtype=np.uint16)
+    lib().orc_synth_normal(seed & _U64, n, 1.0, 0.02, _p(ztab), _p(out))
+    return out
+
+
+def synthetic_tensors(geo: Geometry, seed: int) -> Dict[str, np.ndarray]:
+    """The checkpoint (mlx-lm names) of the engine's seeded synthetic model at TP = 1,
+    restating Model::load_synthetic tag for tag: the tied table, the final norm, then per
+    layer the fused [q; k; v] matrix (one tag, rows keyed in that order), o_proj, the
+    gate/up matrix interleaved by 16-row tiles (tile 2t = gate rows 16t.., 2t + 1 = up
+    rows), down_proj and the seven norm/scalar vectors."""
+    ztab = normal_table()
+    H, I, V = geo.hidden_size, geo.intermediate_size, geo.vocab_size
+    nh = geo.num_attention_heads
+    t: Dict[str, np.ndarray] = {}
+    pre = "language_model.model."
+    tag = (seed * 1000003) & _U64
+
+    def nxt():
+        nonlocal tag
+        tag = (tag + 1) & _U64
+        return tag
+
+    t[pre + "embed_tokens.weight"], t[pre + "embed_tokens.scales"], t[pre + "embed_tokens.biases"] = \
+        synth_q4(nxt(), V, H, ztab=ztab)
+    t[pre + "norm.weight"] = synth_norm(nxt(), H, ztab)
+    for i in range(geo.num_hidden_layers):
+        hd, nkv, kind = geo.head_dim(i), geo.n_kv(i), geo.layer_types[i]
+        p, a = f"{pre}layers.{i}.", f"{pre}layers.{i}.self_attn."
+        qf, kf = nh * hd, nkv * hd
+        vf = 0 if (kind == 1 and geo.attention_k_eq_v_global) else kf
+        w, s, b = synth_q4(nxt(), qf + kf + vf, H, ztab=ztab)
+        parts = [("q_proj", 0, qf), ("k_proj", qf, qf + kf)] + ([("v_proj", qf + kf, qf + kf + vf)] if vf else [])
+        for nm, r0, r1 in parts:
+            t[a + nm + ".weight"], t[a + nm + ".scales"], t[a + nm + ".biases"] = w[r0:r1], s[r0:r1], b[r0:r1]
+        t[a + "o_proj.weight"], t[a + "o_proj.scales"], t[a + "o_proj.biases"] = synth_q4(nxt(), H, qf, ztab=ztab)
+        gu = synth_q4(nxt(), 2 * I, H, ztab=ztab)
+        for j, nm in enumerate(("gate_proj", "up_proj")):
+            for suf, arr in zip((".weight", ".scales", ".biases"), gu):
+                cols = arr.shape[1]
+                t[p + "mlp." + nm + suf] = np.ascontiguousarray(arr.reshape(I // 16, 2, 16, cols)[:, j].reshape(I, cols))
+        del gu
+        t[p + "mlp.down_proj.weight"], t[p + "mlp.down_proj.scales"], t[p + "mlp.down_proj.biases"] = \
+            synth_q4(nxt(), H, I, ztab=ztab)
+        t[a + "q_norm.weight"] = synth_norm(nxt(), hd, ztab)
+        t[a + "k_norm.weight"] = synth_norm(nxt(), hd, ztab)
+        for nm in ("input_layernorm", "post_attention_layernorm", "pre_feedforward_layernorm",
+                   "post_feedforward_layernorm"):
+            t[p + nm + ".weight"] = synth_norm(nxt(), H, ztab)
+        t[p + "layer_scalar"] = synth_norm(nxt(), 1, ztab)
+    return t

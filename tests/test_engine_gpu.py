@@ -11,7 +11,7 @@ import numpy as np
 import pytest
 
 import hyperion_b200 as hb
-from hyperion_b200.synth import bf16_bits_to_f32, config0, tiny_fixture_geometry, write_checkpoint, Geometry
+from hyperion_b200.synth import bf16_bits_to_f32, config0, config3, tiny_fixture_geometry, write_checkpoint, Geometry
 from tests.conftest import has_gpu
 from tests.gpu_util import max_ulp, rel_l2
 
@@ -58,20 +58,26 @@ def _teacher_forced(eng, orc, prompt, steps):
     return np.asarray(agree), np.asarray(rels)
 
 
-@pytest.mark.parametrize("geo_name", ["cfg0", "tiny"])
+@pytest.mark.parametrize("geo_name", ["cfg0", "tiny", "cfg3_2layers"])
 def test_decode_step_stagewise(built_lib, oracle_lib, tmp_path, geo_name):
     """One decode step replayed stage by stage through the op-level ABI, each stage
     fed the oracle's own input, exactly as the engine wires the fused kernels:
     norm-prologue qkv qmv -> QK-norm/RoPE/cache write -> split-K attention over the
     ring or global cache -> o_proj -> residual+norm prologue gate/up qmv with the
-    GeGLU epilogue -> down. Every stage must sit within the per-op bound."""
+    GeGLU epilogue -> down. Every stage must sit within the per-op bound. cfg3_2layers
+    runs the 12B shapes (hd 256, 16/8 heads, hidden 3840, MLP 15360) on one sliding and
+    one global layer of the seeded synthetic model."""
     import torch
     from hyperion_b200 import ops
     from oracle import gemma_oracle as go
     from tests.gpu_util import dev, host
-    geo = config0() if geo_name == "cfg0" else tiny_fixture_geometry()
-    t = write_checkpoint(geo, str(tmp_path / "w"), seed=7)
-    orc = go.OracleModel(geo, t)
+    if geo_name == "cfg3_2layers":
+        geo = config3(2)
+        t = go.synthetic_tensors(geo, 7)
+    else:
+        geo = config0() if geo_name == "cfg0" else tiny_fixture_geometry()
+        t = write_checkpoint(geo, str(tmp_path / "w"), seed=7)
+    orc = go.OracleModel(geo, t, nthreads=go.host_threads())
     prompt = _prompt(geo, 32, 7)
     okv = orc.new_kv()
     tok = orc.prefill(okv, prompt)[0]
