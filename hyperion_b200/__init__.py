@@ -108,7 +108,7 @@ EXT_FUNCTIONS = [
     "hyb_model_set_attention_rounding", "hyb_model_stream", "hyb_decode_batch", "hyb_kvstate_clone", "hyb_qmv_batched",
     "hyb_verify",
     "hyb_kv_copy_layer", "hyb_kv_cursor", "hyb_prefill_logits", "hyb_decode_logits", "hyb_decode_forced",
-    "hyb_test_arm_post_append_fault",
+    "hyb_test_arm_post_append_fault", "hyb_model_set_memory_budget",
 ]
 
 _lib: Optional[ctypes.CDLL] = None
@@ -173,6 +173,7 @@ def lib() -> ctypes.CDLL:
         "hyb_decode_logits": [P, P, P, P],
         "hyb_decode_forced": [P, P, c.c_uint32, P, P],
         "hyb_test_arm_post_append_fault": [],
+        "hyb_model_set_memory_budget": [P, c.c_uint64],
     }
     for name, args in sig.items():
         fn = getattr(L, name)
@@ -308,6 +309,10 @@ class Engine:
 
     def set_attention_rounding(self, mode: int) -> None:
         check(lib().hyb_model_set_attention_rounding(self._model, mode))
+
+    def set_memory_budget(self, nbytes: int) -> None:
+        """Device-byte ceiling checked by every call's admission (0 = free memory only)."""
+        check(lib().hyb_model_set_memory_budget(self._model, nbytes))
 
     def decode_batch(self, kvs: Sequence["KvState"]):
         """One greedy step of every state in `kvs` together (hyb_decode_batch):

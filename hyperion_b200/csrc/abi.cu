@@ -274,28 +274,31 @@ hyb::StepOut sample_row(const std::vector<uint16_t>& row, const HypSamplingConfi
     return out;
 }
 
-// Predictive admission stand-in: reject when the KV growth of this call would not
-// fit into the device's free memory (keeps the OOM_GOVERNOR status contract).
+// Predictive admission before any work (the reference's governor, model.cc:665-683,
+// governor.h:148-186): the call's transient device bytes (staged global caches, ring
+// backups, new workspace) must fit under the model's memory budget on top of the bytes
+// already allocated, and in the device's free memory with a 1 GiB reserve. A rejected
+// call does nothing: the state and its cursor are untouched.
 bool admit(const hyb::Model& m, const hyb::KvState& kv, uint32_t n_tokens, std::string& why) {
-    uint64_t grow = 0;
-    for (const auto& c : kv.global) {
-        const uint64_t need = (static_cast<uint64_t>(c.committed) + n_tokens + 255) / 256 * 256;
-        if (need > 0xFFFFFFFFull) {
-            why = "KV operation exceeds representable cache dimensions";
-            return false;
-        }
-        if (need > c.capacity) grow += (need - c.capacity) * static_cast<uint64_t>(c.nkv) * c.hd * 2 * 2;
+    uint64_t call = 0;
+    if (!m.predict_call_bytes(kv, n_tokens, &call)) {
+        why = "KV operation exceeds representable cache dimensions";
+        return false;
     }
-    for (const auto& c : kv.local) {
-        if (static_cast<uint64_t>(c.committed) + n_tokens > 0xFFFFFFFFull) {
-            why = "KV operation exceeds representable cache dimensions";
-            return false;
-        }
+    const uint64_t budget = m.memory_budget();
+    const uint64_t active = hyb::dev_active_bytes();
+    if (budget > 0 && active + call > budget) {
+        why = "predicted peak of " + std::to_string(active + call) + " device bytes exceeds the memory budget of " +
+              std::to_string(budget) + " bytes";
+        return false;
     }
-    if (grow == 0) return true;
+    if (call == 0) return true;
     size_t free_b = 0, total_b = 0;
-    if (cudaMemGetInfo(&free_b, &total_b) != cudaSuccess) return true;
-    if (grow + (1ull << 30) > free_b) {
+    if (cudaMemGetInfo(&free_b, &total_b) != cudaSuccess) {
+        (void)cudaGetLastError();
+        return true;
+    }
+    if (call + (1ull << 30) > free_b) {
         why = "predicted KV growth exceeds the device memory budget";
         return false;
     }
@@ -474,12 +477,18 @@ HypStatus prefill_impl(HypModel model, HypKvState kv, const HypTokenStream* toke
         const bool sampled = cfg != nullptr && cfg->temperature != 0.0f;
         std::vector<uint16_t> logits;
         hyb::StepOut o;
+        // a fresh state always grows its global caches: the call is staged, and a failure
+        // leaves the state fresh (model.cc:531-600)
+        hyb::KvTransaction tx = m.begin_kv_transaction(*kv->kv, tokens->count);
         try {
             o = m.prefill(*kv->kv, tokens->tokens, tokens->count, (sampled || host_logits) ? &logits : nullptr);
+            maybe_inject_fault();
         } catch (...) {
-            kv->kv->poisoned = true;  // cache contents are partially written
+            if (tx.active) m.rollback_kv_transaction(*kv->kv, tx);
+            else kv->kv->poisoned = true;  // cache contents are partially written
             throw;
         }
+        tx = hyb::KvTransaction{};  // publish (a fresh state kept no buffers worth freeing)
         if (sampled) {
             o = sample_row(logits, *cfg, cfg->seed);
             kv->kv->last_token = o.token;
@@ -519,13 +528,18 @@ HypStatus decode_impl(HypModel model, HypKvState kv, uint32_t n_tokens, const Hy
         uint32_t near_ties = 0;
         hyb::StepOut o;
         std::vector<uint16_t> logits;
+        // a block that grows a global cache runs staged and rolls back on failure; one
+        // that does not runs directly and a failure consumes the state (model.cc:79-105,
+        // 684-735)
+        hyb::KvTransaction tx = m.begin_kv_transaction(*kv->kv, n_tokens);
         for (uint32_t step = 0; step < n_tokens; ++step) {
             if (forced) kv->kv->last_token = *forced;
             try {
                 o = m.decode_step(*kv->kv, (sampled || host_logits) ? &logits : nullptr);
                 if (step == 0) maybe_inject_fault();
             } catch (...) {
-                kv->kv->poisoned = true;  // model.cc:79-105: a failed direct decode consumes the state
+                if (tx.active) m.rollback_kv_transaction(*kv->kv, tx);
+                else kv->kv->poisoned = true;
                 throw;
             }
             if (sampled) {
@@ -535,6 +549,7 @@ HypStatus decode_impl(HypModel model, HypKvState kv, uint32_t n_tokens, const Hy
             }
             if (o.near_tie) ++near_ties;
         }
+        tx = hyb::KvTransaction{};  // publish: free the live buffers the staged ones replaced
         if (host_logits) std::memcpy(host_logits, logits.data(), logits.size() * 2);
         write_result(out, &o, near_ties, HYP_GOVERNOR_READY, m, *kv->kv, sampled);
         return ok();
@@ -732,6 +747,14 @@ HypStatus hyb_model_set_attention_rounding(HypModel model, int32_t mode) {
     if (!model->loaded) return fail(HYP_STATUS_INVALID_ARGUMENT, "model is not loaded");
     if (mode != 0 && mode != 1) return fail(HYP_STATUS_INVALID_ARGUMENT, "attention rounding mode must be 0 or 1");
     model->model->set_attention_rounding(mode);
+    return ok();
+}
+
+HypStatus hyb_model_set_memory_budget(HypModel model, uint64_t bytes) {
+    HypStatus st = validate_model(model);
+    if (st != HYP_STATUS_OK) return st;
+    if (!model->loaded) return fail(HYP_STATUS_INVALID_ARGUMENT, "model is not loaded");
+    model->model->set_memory_budget(bytes);
     return ok();
 }
 

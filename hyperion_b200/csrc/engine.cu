@@ -613,6 +613,132 @@ void Model::reserve(KvState& kv, uint32_t n_tokens) const {
     }
 }
 
+bool Model::predict_call_bytes(const KvState& kv, uint32_t n_tokens, uint64_t* bytes) const {
+    uint64_t b = 0;
+    bool grows = false;
+    for (const auto& c : kv.global) {
+        const uint64_t need = (static_cast<uint64_t>(c.committed) + n_tokens + 255) / 256 * 256;
+        if (need > 0xFFFFFFFFull) return false;
+        if (need > c.capacity) {
+            b += need * c.nkv * c.hd * 2 * 2;
+            grows = true;
+        }
+    }
+    for (const auto& c : kv.local) {
+        if (static_cast<uint64_t>(c.committed) + n_tokens > 0xFFFFFFFFull) return false;
+        if (grows && n_tokens > static_cast<uint32_t>(kSpecMax)) b += static_cast<uint64_t>(c.cap) * c.nkv * c.hd * 2 * 2;
+    }
+    // workspace the call would newly allocate (ensure_workspace): a prefill runs chunks of
+    // up to 2048 rows, decode one row per forward
+    const Geometry& g = geo_;
+    const bool prefill = kv.offset == 0;
+    const uint64_t rows = prefill ? std::min<uint32_t>(n_tokens, 2048) : 1;
+    if (rows > static_cast<uint64_t>(ws_.chunk_cap)) {
+        uint64_t max_qkv = 0, max_attn = 0, max_kv_row = 0;
+        for (const auto& L : layers_) {
+            max_qkv = std::max<uint64_t>(max_qkv, L.q_rows + L.k_rows + L.v_rows);
+            max_attn = std::max<uint64_t>(max_attn, L.q_rows);
+            max_kv_row = std::max<uint64_t>(max_kv_row, static_cast<uint64_t>(L.nkv) * L.hd);
+        }
+        const uint64_t H = g.hidden, I = static_cast<uint64_t>(inter_local_);
+        b += 2 * rows * (6 * H + max_qkv + 2 * max_attn + 3 * I) + 4 * rows + 2 * 2 * (rows + g.window) * max_kv_row;
+    }
+    const uint64_t keys = std::min<uint64_t>(static_cast<uint64_t>(kv.offset) + n_tokens, 32768);
+    size_t need = 0;
+    for (const auto& L : layers_)
+        need = std::max(need, decode_attn_scratch_bytes(heads_local_, L.nkv, L.hd, static_cast<int>(keys)));
+    if (need > ws_.attn_scratch_bytes) b += std::max(need, ws_.attn_scratch_bytes * 2);
+    *bytes = b;
+    return true;
+}
+
+KvTransaction Model::begin_kv_transaction(KvState& kv, uint32_t n_tokens) const {
+    KvTransaction t;
+    bool grows = false;
+    for (const auto& c : kv.global)
+        if ((static_cast<uint64_t>(c.committed) + n_tokens + 255) / 256 * 256 > c.capacity) grows = true;
+    if (!grows) return t;
+    t.active = true;
+    t.offset = kv.offset;
+    t.last_token = kv.last_token;
+    for (const auto& c : kv.local) t.local_committed.push_back(c.committed);
+    for (const auto& c : kv.global) t.global_committed.push_back(c.committed);
+    if (n_tokens > static_cast<uint32_t>(kSpecMax)) {
+        for (size_t i = 0; i < kv.local.size(); ++i) {
+            const LocalCache& c = kv.local[i];
+            const size_t n = static_cast<size_t>(c.cap) * c.nkv * c.hd;
+            KvTransaction::Ring r;
+            r.index = i;
+            r.k.reset(n);
+            r.v.reset(n);
+            HYB_CUDA(cudaMemcpyAsync(r.k.p, c.k.p, n * 2, cudaMemcpyDeviceToDevice, stream_));
+            HYB_CUDA(cudaMemcpyAsync(r.v.p, c.v.p, n * 2, cudaMemcpyDeviceToDevice, stream_));
+            t.rings.push_back(std::move(r));
+        }
+    }
+    for (size_t i = 0; i < kv.global.size(); ++i) {
+        GlobalCache& c = kv.global[i];
+        const uint64_t need = (static_cast<uint64_t>(c.committed) + n_tokens + 255) / 256 * 256;
+        if (need <= c.capacity) continue;
+        const size_t row = static_cast<size_t>(c.nkv) * c.hd;
+        DevPtr<bf16> nk(need * row), nv(need * row);
+        HYB_CUDA(cudaMemsetAsync(nk.p, 0, need * row * 2, stream_));
+        HYB_CUDA(cudaMemsetAsync(nv.p, 0, need * row * 2, stream_));
+        if (c.capacity > 0) {
+            HYB_CUDA(cudaMemcpyAsync(nk.p, c.k.p, static_cast<size_t>(c.capacity) * row * 2, cudaMemcpyDeviceToDevice,
+                                     stream_));
+            HYB_CUDA(cudaMemcpyAsync(nv.p, c.v.p, static_cast<size_t>(c.capacity) * row * 2, cudaMemcpyDeviceToDevice,
+                                     stream_));
+        }
+        KvTransaction::Global kept;
+        kept.index = i;
+        kept.k = std::move(c.k);
+        kept.v = std::move(c.v);
+        kept.capacity = c.capacity;
+        kept.tk = c.tk;
+        kept.tv = c.tv;
+        t.globals.push_back(std::move(kept));
+        c.k = std::move(nk);
+        c.v = std::move(nv);
+        c.capacity = static_cast<uint32_t>(need);
+        encode_kv_tensor_map(&c.tk, c.k.p, static_cast<int>(c.capacity), c.nkv, c.hd);
+        encode_kv_tensor_map(&c.tv, c.v.p, static_cast<int>(c.capacity), c.nkv, c.hd);
+    }
+    HYB_CUDA(cudaStreamSynchronize(stream_));
+    return t;
+}
+
+void Model::rollback_kv_transaction(KvState& kv, KvTransaction& t) const {
+    if (!t.active) return;
+    // work of the failed call may still be queued: let it finish before buffers change hands
+    cudaError_t e = cudaStreamSynchronize(stream_);
+    if (e != cudaSuccess) {
+        (void)cudaGetLastError();
+        kv.poisoned = true;  // the device is in an error state: the cache contents are unknown
+        return;
+    }
+    for (auto& g : t.globals) {
+        GlobalCache& c = kv.global[g.index];
+        c.k = std::move(g.k);
+        c.v = std::move(g.v);
+        c.capacity = g.capacity;
+        c.tk = g.tk;
+        c.tv = g.tv;
+    }
+    for (auto& r : t.rings) {
+        LocalCache& c = kv.local[r.index];
+        const size_t n = static_cast<size_t>(c.cap) * c.nkv * c.hd;
+        HYB_CUDA(cudaMemcpyAsync(c.k.p, r.k.p, n * 2, cudaMemcpyDeviceToDevice, stream_));
+        HYB_CUDA(cudaMemcpyAsync(c.v.p, r.v.p, n * 2, cudaMemcpyDeviceToDevice, stream_));
+    }
+    for (size_t i = 0; i < kv.local.size(); ++i) kv.local[i].committed = t.local_committed[i];
+    for (size_t i = 0; i < kv.global.size(); ++i) kv.global[i].committed = t.global_committed[i];
+    kv.offset = t.offset;
+    kv.last_token = t.last_token;
+    HYB_CUDA(cudaStreamSynchronize(stream_));
+    t = KvTransaction{};
+}
+
 uint64_t Model::local_kv_bytes(const KvState& kv) const {
     uint64_t b = 0;
     for (const auto& c : kv.local) b += static_cast<uint64_t>(c.cap) * c.nkv * c.hd * 2 * 2;

@@ -98,6 +98,32 @@ struct KvState {
     bool poisoned = false;
 };
 
+// A call that grows a global cache runs against staged buffers and publishes them only
+// when it succeeds (the reference's KvGrowthTransaction, kv_cache.h:220-261,
+// kv_cache.cc:68-128): the larger buffers are filled from the live ones and swapped in,
+// and the live buffers are kept here. On failure rollback restores them, the cursor and
+// every commit count, so the state stays usable; on success the kept buffers are freed.
+// A ring (capacity window + 8) is written in place: a block of at most 8 tokens only
+// overwrites slots of positions the state no longer reads, longer blocks back the rings
+// up first.
+struct KvTransaction {
+    bool active = false;
+    uint32_t offset = 0, last_token = 0;
+    std::vector<uint32_t> local_committed, global_committed;
+    struct Global {
+        size_t index = 0;
+        DevPtr<bf16> k, v;
+        uint32_t capacity = 0;
+        CUtensorMap tk{}, tv{};
+    };
+    struct Ring {
+        size_t index = 0;
+        DevPtr<bf16> k, v;
+    };
+    std::vector<Global> globals;
+    std::vector<Ring> rings;
+};
+
 // Draft tokens one verify pass may check: the speculative slack of the local rings
 // (capacity window + 8). Writing positions offset..offset+8 overwrites only ring slots
 // of positions at least window + 8 back, so after any acceptance every position the next
@@ -169,6 +195,20 @@ class Model {
     // Grow global caches so that `n_tokens` more tokens fit (reference
     // plan_kv_growth / GlobalKvCache::append semantics: 256-token steps).
     void reserve(KvState& kv, uint32_t n_tokens) const;
+    // Device bytes a call of `n_tokens` more tokens adds while it runs (governor admission):
+    // the staged global caches it grows (their full new capacity: the live buffers stay
+    // allocated until the call publishes), ring backups for blocks longer than the ring
+    // slack, and the workspace it would newly allocate. Returns false if a cache dimension
+    // would not be representable.
+    bool predict_call_bytes(const KvState& kv, uint32_t n_tokens, uint64_t* bytes) const;
+    // Stage the growth of a call of `n_tokens` tokens (inactive when no global cache grows).
+    KvTransaction begin_kv_transaction(KvState& kv, uint32_t n_tokens) const;
+    // Undo a failed call: the live buffers, cursor and commit counts come back.
+    void rollback_kv_transaction(KvState& kv, KvTransaction& t) const;
+    // Hard ceiling on the engine's device bytes (0 = device memory only), checked by the
+    // predictive admission before any work (the governor budget of governor.h:148-186).
+    void set_memory_budget(uint64_t bytes) { memory_budget_ = bytes; }
+    uint64_t memory_budget() const { return memory_budget_; }
 
     // Prefill a prompt on a fresh state; returns the greedy sample of the last row.
     StepOut prefill(KvState& kv, const uint32_t* tokens, uint32_t count, std::vector<uint16_t>* logits_out);
@@ -226,6 +266,7 @@ class Model {
     DevPtr<float> inv_freq_local_, inv_freq_global_;
     bf16 embed_scale_{};
     int attn_rounding_ = 0;
+    uint64_t memory_budget_ = 0;
     Workspace ws_;
     BatchWorkspace bws_;
     void ensure_batch_workspace(int n);

@@ -296,12 +296,27 @@ HypStatus hyb_decode_forced(HypModel model, HypKvState kv, uint32_t token, HypSt
                             void* host_logits);
 
 /*
- * Test hook: the next decode call on this thread throws once on the host right
- * after its first forward has been enqueued, like the reference's post-append
- * fault (native/hyperion_mlx/src/test_fault.cc:1-24). The call returns
- * INTERNAL and the KV state is poisoned. No device fault is involved.
+ * Test hook: the next prefill or decode call on this thread throws once on the
+ * host right after its first forward has been enqueued, like the reference's
+ * post-append fault (native/hyperion_mlx/src/test_fault.cc:1-24). The call
+ * returns INTERNAL. A call that grew a global cache ran staged and is rolled
+ * back (the state keeps its cursor and stays usable); any other call leaves the
+ * KV state poisoned. No device fault is involved.
  */
 HypStatus hyb_test_arm_post_append_fault(void);
+
+/*
+ * Memory budget of a loaded model: the ceiling, in device bytes held by the
+ * engine (weights, KV caches, workspaces), that the predictive admission of
+ * every prefill/decode call checks before doing any work (replaces the
+ * platform-derived budget of the reference governor, governor.h:148-186).
+ * A call whose predicted transient (staged global-cache growth, ring backups,
+ * new workspace) would take the engine above it returns OOM_GOVERNOR with the
+ * step result's governor_state = HYP_GOVERNOR_HARD_REJECT, and leaves the KV
+ * state and its cursor untouched. 0 (the default) checks device free memory only.
+ */
+HypStatus hyb_model_set_memory_budget(HypModel model, uint64_t bytes);
+
 
 #ifdef __cplusplus
 }
