@@ -5,11 +5,12 @@
 // ForwardPass::attention (native/hyperion_mlx/src/forward.cc:394-420 norms and
 // RoPE, :459-468 cache append, :474-495 cache read, :498-504 SDPA).
 //
-// Each cluster of CS CTAs (CS <= 8, portable) owns one KV head and its REP query
+// Each cluster of CS CTAs (CS <= 16: above 8 only where the occupancy query says that
+// many clusters of that size are resident at once) owns one KV head and its REP query
 // heads (of one sequence: a batched launch adds gridDim.z = sequences and reads each
 // sequence's caches, position and tensor maps from a DecodeSeq array; CS then shrinks
-// to keep about two CTAs per SM); CTA rank c owns a contiguous slice of the n_keys
-// cache positions. The
+// so that the launch fits the SMs); CTA rank c owns a contiguous slice of the n_keys
+// cache positions, a whole number of 64-key tiles. The
 // slice's K rows and then its V rows stream through a ring of shared-memory tiles
 // of 64 consecutive cache slots of this KV head: HD/64 tensor-map TMA boxes of
 // [64 slots][64 dims] with the 128-byte swizzle, so the tensor-core fragment loads
@@ -46,7 +47,10 @@
 
 #include <algorithm>
 #include <cfloat>
+#include <map>
+#include <mutex>
 #include <string>
+#include <tuple>
 
 namespace hyb {
 
@@ -56,9 +60,10 @@ namespace {
 
 constexpr int kThreads = 256;
 constexpr int kWarps = kThreads / 32;
-constexpr int kMaxCluster = 8;
+constexpr int kMaxCluster = 16;
+constexpr int kPortableCluster = 8;
 constexpr int kTileKeys = 64;       // cache slots per tile (8 per warp)
-constexpr int kRingBytes = 131072;  // tile bytes in flight per CTA
+constexpr int kRingBytes = 196608;  // tile bytes in flight per CTA
 constexpr int kMaxStages = 8;
 constexpr size_t kSmemLimit = 227 * 1024;
 
@@ -113,6 +118,16 @@ __device__ __forceinline__ void merge8(float m, float l, float& M, float& L) {
     for (int o = 1; o < 8; o <<= 1) L += __shfl_xor_sync(0xffffffffu, L, o);
 }
 
+// merge8 over the lanes of one 16-lane group (one entry per CTA of a cluster of <= 16).
+__device__ __forceinline__ void merge16(float m, float l, float& M, float& L) {
+    M = l > 0.f ? m : -FLT_MAX;
+#pragma unroll
+    for (int o = 1; o < 16; o <<= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
+    L = l > 0.f ? l * exp_fast(m - M) : 0.f;
+#pragma unroll
+    for (int o = 1; o < 16; o <<= 1) L += __shfl_xor_sync(0xffffffffu, L, o);
+}
+
 __device__ __forceinline__ float score_round(float dot, float scale, float cap, int rounding) {
     float s = dot * scale;
     if (rounding == 0) s = rbf(s);
@@ -132,25 +147,30 @@ __device__ __noinline__ void norm_rope_row(const bf16* src, const bf16* nw, cons
                               bool rope, float* dst, bf16* cache_dst) {
     const int lane = threadIdx.x & 31;
     constexpr int HD = PER * 32;
-    float v[PER];
-    float ss = 0.f;
+    constexpr int HP = PER / 2;
+    // every operand is loaded up front, so the row costs one memory latency
+    float v[PER], w[PER], fr[HP];
 #pragma unroll
     for (int i = 0; i < PER; ++i) {
         v[i] = bf2f(src[lane + 32 * i]);
-        ss += v[i] * v[i];
+        w[i] = nw ? bf2f(nw[lane + 32 * i]) : 1.f;
     }
+#pragma unroll
+    for (int i = 0; i < HP; ++i) fr[i] = rope ? inv_freq[lane + 32 * i] : 0.f;
+    float ss = 0.f;
+#pragma unroll
+    for (int i = 0; i < PER; ++i) ss += v[i] * v[i];
     ss = warp_sum(ss);
     const float inv = 1.0f / sqrtf(ss / static_cast<float>(HD) + eps);
 #pragma unroll
     for (int i = 0; i < PER; ++i) {
         const float t = rbf(v[i] * inv);
-        v[i] = nw ? rbf(t * bf2f(nw[lane + 32 * i])) : t;
+        v[i] = nw ? rbf(t * w[i]) : t;
     }
     if (rope) {
-        constexpr int HP = PER / 2;
 #pragma unroll
         for (int i = 0; i < HP; ++i) {
-            const float f = inv_freq[lane + 32 * i];
+            const float f = fr[i];
             if (f != 0.f) {
                 float sn, cs;
                 sincosf(__fmul_rn(static_cast<float>(pos), f), &sn, &cs);
@@ -304,13 +324,15 @@ __global__ void __launch_bounds__(kThreads, 1) decode_attn_fused_kernel(const De
             tma_load_3d_hint(tiles_u32 + s * TILE + sub * (T * 128), isv ? map_v : map_k, 64 * sub, hk, tk.z, fb,
                              l2_evict_first());
     };
-    if (threadIdx.x == 0) {
-        if (sq) {  // tensor maps written to global memory by a copy: acquire them for the TMA unit
-            asm volatile("fence.proxy.tensormap::generic.acquire.gpu [%0], 128;" ::"l"(map_k) : "memory");
-            asm volatile("fence.proxy.tensormap::generic.acquire.gpu [%0], 128;" ::"l"(map_v) : "memory");
-        }
-        for (int it = 0; it < stages && it < items; ++it) issue(it);
+    // tensor maps written to global memory by a copy: every thread that may issue a load
+    // with them (the first-stage issuers below, lane 0 of each warp for refills) acquires
+    // them for the TMA unit first
+    if (sq && (lane == 0 || static_cast<int>(threadIdx.x) < stages)) {
+        asm volatile("fence.proxy.tensormap::generic.acquire.gpu [%0], 128;" ::"l"(map_k) : "memory");
+        asm volatile("fence.proxy.tensormap::generic.acquire.gpu [%0], 128;" ::"l"(map_v) : "memory");
     }
+    // the first stages, one issuing thread each
+    if (static_cast<int>(threadIdx.x) < stages && static_cast<int>(threadIdx.x) < items) issue(threadIdx.x);
 
     pdl_wait();
     // ---- phase 0: query heads of this KV head, and the new token's K/V
@@ -445,10 +467,10 @@ __global__ void __launch_bounds__(kThreads, 1) decode_attn_fused_kernel(const De
 #pragma unroll
         for (int h = 0; h < REP; ++h) {
             // lane c (< CS) holds CTA c's pair for head h; the shuffle tree merges them
-            const int c = lane & 7;
+            const int c = lane & 15;
             const bool has = c < CS;
             float M, L;
-            merge8(has ? allml[(c * REP + h) * 2] : -FLT_MAX, has ? allml[(c * REP + h) * 2 + 1] : 0.f, M, L);
+            merge16(has ? allml[(c * REP + h) * 2] : -FLT_MAX, has ? allml[(c * REP + h) * 2 + 1] : 0.f, M, L);
             const float iL = 1.0f / L;
             for (int i = lane; i < my_count; i += 32) {
                 const int k = my_key(i);
@@ -545,21 +567,26 @@ struct FusedPlan {
     size_t smem = 0;
 };
 
-// `units` = independent (KV head, sequence) pairs of the launch. A cluster splits a
-// pair's keys over up to 8 CTAs (128 keys or more each) only while the launch has fewer
-// than two CTAs per SM; a batch of many sequences runs one CTA per pair. A plan whose
-// scores do not fit in shared memory takes more CTAs per cluster.
-FusedPlan plan_fused(int hd, int rep, int n_keys, int units) {
-    const int want = std::max(1, (2 * num_sms() + units - 1) / units);
-    int cs0 = std::min({kMaxCluster, std::max(1, (n_keys + 127) / 128), want});
-    for (int cs = cs0; cs <= kMaxCluster; ++cs) {
+// `units` = independent (KV head, sequence) pairs of the launch, `cs_cap` the largest
+// cluster allowed. While the launch has fewer pairs than SMs, a cluster splits a pair's
+// keys over up to SMs / units CTAs in whole 64-key tiles (the most tiles on any CTA as
+// low as the SMs allow) and each CTA keeps up to 192 KB of tiles in flight; a launch with
+// a pair or more per SM runs one CTA per pair with 128 KB in flight, leaving room for
+// more resident CTAs. A plan whose scores do not fit in shared memory takes more CTAs per
+// cluster.
+FusedPlan plan_fused(int hd, int rep, int n_keys, int units, int cs_cap) {
+    const int sms = num_sms();
+    const int tiles = (n_keys + kTileKeys - 1) / kTileKeys;
+    const int want = std::max(1, std::min(cs_cap, sms / std::max(units, 1)));
+    const int ring = units < sms ? kRingBytes : 131072;
+    const int tile = kTileKeys * hd * 2;
+    for (int c = want; c <= cs_cap; ++c) {
         FusedPlan f;
-        f.chunk = (n_keys + cs - 1) / cs;
+        f.chunk = (tiles + c - 1) / c * kTileKeys;
         f.cs = (n_keys + f.chunk - 1) / f.chunk;
-        const int tile = kTileKeys * hd * 2;
-        // up to 128 KB of tiles in flight; +1 for a possible split at the ring wrap
-        const int items = 2 * ((f.chunk + kTileKeys - 1) / kTileKeys + 1);
-        for (int s = std::min({kMaxStages, items, kRingBytes / tile}); s >= 1; --s) {
+        // +1 tile for a possible split at the ring wrap
+        const int items = 2 * (f.chunk / kTileKeys + 1);
+        for (int s = std::min({kMaxStages, items, ring / tile}); s >= 1; --s) {
             f.stages = s;
             f.smem = fused_layout(hd, rep, f.chunk, s).total + 1024;  // + alignment slack
             if (f.smem <= kSmemLimit) return f;
@@ -568,18 +595,55 @@ FusedPlan plan_fused(int hd, int rep, int n_keys, int units) {
     return FusedPlan{};
 }
 
+// Clusters of `cs` CTAs of `kern` with `smem` bytes each that the device keeps resident
+// at once (cached per device, cluster size and shared memory).
+template <typename K>
+int resident_clusters(K kern, int cs, size_t smem) {
+    static std::mutex mu;
+    static std::map<std::tuple<int, int, size_t>, int> cache;
+    int dev = 0;
+    HYB_CUDA(cudaGetDevice(&dev));
+    std::lock_guard<std::mutex> lk(mu);
+    const auto key = std::make_tuple(dev, cs, smem);
+    auto it = cache.find(key);
+    if (it != cache.end()) return it->second;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(cs);
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = smem;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = cs;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    int n = 0;
+    if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess) {
+        (void)cudaGetLastError();
+        n = 0;
+    }
+    cache[key] = n;
+    return n;
+}
+
 template <int PER, int REP, int ROUND>
 void launch_fused_t(const DecodeFusedParams& p, cudaStream_t stream, bool pdl) {
-    const FusedPlan f = plan_fused(PER * 32, REP, p.n_keys, p.n_kv * (p.seqs ? p.n_seq : 1));
-    if (f.stages == 0) throw ArgError("decode attention: too many keys for the shared-memory plan");
+    const int units = p.n_kv * (p.seqs ? p.n_seq : 1);
     auto kern = decode_attn_fused_kernel<PER, REP, ROUND>;
     static int attr_dev = -1;
     int dev = 0;
     HYB_CUDA(cudaGetDevice(&dev));
     if (attr_dev != dev) {
         HYB_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kSmemLimit)));
+        HYB_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1));
         attr_dev = dev;
     }
+    // clusters above the portable 8 CTAs only where all of the launch's clusters fit at once
+    FusedPlan f = plan_fused(PER * 32, REP, p.n_keys, units, kMaxCluster);
+    if (f.stages != 0 && f.cs > kPortableCluster && resident_clusters(kern, f.cs, f.smem) < units)
+        f = plan_fused(PER * 32, REP, p.n_keys, units, kPortableCluster);
+    if (f.stages == 0) throw ArgError("decode attention: too many keys for the shared-memory plan");
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(f.cs, p.n_kv, p.seqs ? p.n_seq : 1);
     cfg.blockDim = dim3(kThreads);
@@ -642,7 +706,8 @@ bool decode_attn_fused_fits(int n_heads, int n_kv, int hd, int n_keys) {
     if (n_kv <= 0 || n_heads % n_kv != 0 || (hd != 64 && hd != 128 && hd != 256) || n_keys <= 0) return false;
     const int rep = n_heads / n_kv;
     if (rep != 1 && rep != 2 && rep != 4 && rep != 8) return false;
-    return plan_fused(hd, rep, n_keys, n_kv).stages > 0;
+    // the portable plan always launches, so it decides whether the fused kernel applies
+    return plan_fused(hd, rep, n_keys, n_kv, kPortableCluster).stages > 0;
 }
 
 void launch_decode_attn_fused(const DecodeFusedParams& p, cudaStream_t stream, bool pdl) {

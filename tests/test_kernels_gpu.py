@@ -353,7 +353,7 @@ def test_sdpa_decode_fused_rejects_oversized_context(built_lib):
     """Scores that outgrow the cluster's shared memory are refused, not truncated."""
     import torch
     from hyperion_b200 import HypError, ops
-    H, Hkv, hd, n = 8, 1, 128, 60000  # 8 heads x 7500 fp32 scores per CTA > 227 KB
+    H, Hkv, hd, n = 8, 1, 128, 140000  # even over 16 CTAs: 8 heads x 8768 fp32 scores per CTA > 227 KB
     kc = torch.zeros((n, Hkv, hd), dtype=torch.bfloat16, device="cuda")
     vc = torch.zeros_like(kc)
     qkv = torch.zeros((H + 2 * Hkv) * hd, dtype=torch.bfloat16, device="cuda")
