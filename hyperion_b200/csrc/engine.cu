@@ -1214,13 +1214,13 @@ void Model::decode_layers(KvState& kv) {
         pd.N = H;
         if (fused_ar) {
             po.ar_mode = 1;
-            po.ar = tp_.next_fused_ar(qmv_packed_grid(po));
+            po.ar = tp_.next_fused_ar();
             pg.ar_mode = 2;
             pg.ar = po.ar;
             pd.ar_mode = 1;
             launch_qmv(po, st, true);
             launch_qmv(pg, st, true);
-            pd.ar = tp_.next_fused_ar(qmv_packed_grid(pd));
+            pd.ar = tp_.next_fused_ar();
             launch_qmv(pd, st, true);
             dn_ar = pd.ar;
             last_ar_ = pd.ar;

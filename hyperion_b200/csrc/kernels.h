@@ -27,20 +27,22 @@ enum class QmvEpilogue : int {
     kGeglu = 1,   // rows are (gate, up) interleaved by 16-row tiles: y[n] = bf16(gelu(g) * u)
 };
 
-// Tensor-parallel all-reduce fused into the decode qmvs over NVLink peer memory. Every
-// rank's receive buffer (IPC-mapped into every process, own included): [2 sets][T
-// sources][max_count] bf16, then per-source arrival counters (u32). A row-parallel qmv
-// (ar_mode 1) stores its bf16 output rows into slot (set, me) of every rank and each CTA
-// adds 1 to counter[me] on every rank (release at system scope); the next qmv (ar_mode 2)
-// waits (bounded) until counter[src] >= target for every source, then uses
-// x = bf16(sum over sources in rank order) as its input: the same bits on every rank.
+// Tensor-parallel all-reduce fused into the decode qmvs over NVLink peer memory, in words
+// that carry their own flag: a row-parallel qmv (ar_mode 1) writes its bf16 output rows in
+// pairs as 8-byte words {row 2k, row 2k + 1, epoch} into slot (set, me) of every rank's
+// receive buffer (IPC-mapped into every process, own included); an aligned 8-byte store is
+// single-copy atomic, so a word whose epoch matches carries its data, and no fence or
+// counter is needed. The next qmv (ar_mode 2) spins (bounded) on each word of every source
+// until its epoch is this all-reduce's, then uses x = bf16(sum over sources in rank order)
+// as its input: the same bits on every rank. Receive buffer: [2 sets][T sources]
+// [max_count / 2] u64 words at ll_off, a wait-error counter at err_off.
 struct QmvTpFuse {
     unsigned char* peer[8] = {};
     int T = 0, me = 0;
     int set = 0;                // receive set of this all-reduce
-    unsigned target = 0;        // producer CTAs per source counted after this all-reduce
-    size_t max_count = 0;       // elements per (set, source) slot
-    size_t counters_off = 0;    // byte offset of the counters in a buffer
+    unsigned epoch = 0;         // sequence number of this all-reduce (>= 1) carried by its words
+    size_t max_count = 0;       // elements per (set, source) slot (even)
+    size_t ll_off = 0;          // byte offset of the words in a buffer
     size_t err_off = 0;         // byte offset of the wait-error counter
 };
 
@@ -67,8 +69,6 @@ struct QmvParams {
     int ar_mode = 0;
     QmvTpFuse ar;
 };
-// CTAs launch_qmv_packed uses for `p` (the producer count of a fused all-reduce).
-int qmv_packed_grid(const QmvParams& p);
 
 void launch_qmv(const QmvParams& p, cudaStream_t stream, bool pdl = false);
 

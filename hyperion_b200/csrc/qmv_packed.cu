@@ -59,67 +59,53 @@ __device__ __forceinline__ float block_sum(float v, float* tmp) {
 }
 
 // ---- fused tensor-parallel all-reduce (QmvTpFuse)
-__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
-    uint32_t v;
-    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+__device__ __forceinline__ unsigned long long ld_relaxed_sys_u64(const void* p) {
+    unsigned long long v;
+    asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
     return v;
 }
-
-// Producer: output row `row` into slot (set, me) of every rank.
-__device__ __forceinline__ void ar_store(const QmvParams& p, int row, bf16 v) {
-    if (p.ar_mode != 1) return;
-    const size_t off = ((static_cast<size_t>(p.ar.set) * p.ar.T + p.ar.me) * p.ar.max_count + row) * 2;
-    for (int r = 0; r < p.ar.T; ++r) *reinterpret_cast<bf16*>(p.ar.peer[r] + off) = v;
+__device__ __forceinline__ void st_relaxed_sys_u64(void* p, unsigned long long v) {
+    asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
 }
 
-// Producer, end of the CTA: its rows are stored; count it on every rank.
-__device__ __forceinline__ void ar_publish(const QmvParams& p) {
-    if (p.ar_mode != 1) return;
-    __syncthreads();
-    if (threadIdx.x == 0) {
-        __threadfence_system();
-        for (int r = 0; r < p.ar.T; ++r)
-            asm volatile("red.release.sys.global.add.u32 [%0], 1;" ::"l"(p.ar.peer[r] + p.ar.counters_off + 4 * p.ar.me)
-                         : "memory");
-    }
+// Producer: rows 2k and 2k + 1 (row 2k + 1 past N is zero) as one flagged word into slot
+// (set, me) of every rank.
+__device__ __forceinline__ void ar_store_pair(const QmvParams& p, int row2k, bf16 a, bf16 b) {
+    const unsigned long long w =
+        (static_cast<unsigned long long>(p.ar.epoch) << 32) | pack_bf2(a, row2k + 1 < p.N ? b : f2bf(0.f));
+    const size_t off =
+        p.ar.ll_off + ((static_cast<size_t>(p.ar.set) * p.ar.T + p.ar.me) * (p.ar.max_count / 2) + row2k / 2) * 8;
+    for (int r = 0; r < p.ar.T; ++r) st_relaxed_sys_u64(p.ar.peer[r] + off, w);
 }
 
-// Consumer: wait (bounded) until every source's producer CTAs have published.
-__device__ __forceinline__ void ar_wait(const QmvParams& p) {
-    if (threadIdx.x == 0) {
-        const unsigned char* mine = p.ar.peer[p.ar.me];
-        for (int src = 0; src < p.ar.T; ++src) {
-            const uint32_t* c = reinterpret_cast<const uint32_t*>(mine + p.ar.counters_off + 4 * src);
-            bool ok = false;
-            for (int it = 0; it < (1 << 22); ++it) {
-                if (static_cast<int32_t>(ld_acquire_sys(c) - p.ar.target) >= 0) {
-                    ok = true;
-                    break;
-                }
-                if (it > 32) __nanosleep(64);
-            }
-            if (!ok) atomicAdd(reinterpret_cast<int*>(p.ar.peer[p.ar.me] + p.ar.err_off), 1);
-        }
-    }
-    __syncthreads();
-}
-
-// Consumer: chunk j (8 elements) of the all-reduced vector, summed over sources in rank
-// order in fp32 and rounded to bf16 (read through L2: the peers wrote it over NVLink).
+// Consumer: chunk j (8 elements = 4 words per source) of the all-reduced vector, each word
+// awaited (bounded) until it carries this all-reduce's epoch, summed over sources in rank
+// order in fp32 and rounded to bf16.
 __device__ __forceinline__ uint4 ar_chunk(const QmvParams& p, int j) {
     const unsigned char* mine = p.ar.peer[p.ar.me];
     float a[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    bool ok = true;
     for (int src = 0; src < p.ar.T; ++src) {
-        const uint4 v = __ldcg(reinterpret_cast<const uint4*>(
-                                   mine + (static_cast<size_t>(p.ar.set) * p.ar.T + src) * p.ar.max_count * 2) +
-                               j);
-        const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+        const unsigned char* slot =
+            mine + p.ar.ll_off + (static_cast<size_t>(p.ar.set) * p.ar.T + src) * (p.ar.max_count / 2) * 8;
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
-            a[2 * q] += __uint_as_float(w[q] << 16);
-            a[2 * q + 1] += __uint_as_float(w[q] & 0xFFFF0000u);
+            const void* wp = slot + (static_cast<size_t>(4 * j + q)) * 8;
+            unsigned long long w = ld_relaxed_sys_u64(wp);
+            for (int it = 0; static_cast<unsigned>(w >> 32) != p.ar.epoch; ++it) {
+                if (it >= (1 << 22)) {
+                    ok = false;
+                    break;
+                }
+                if (it > 64) __nanosleep(32);
+                w = ld_relaxed_sys_u64(wp);
+            }
+            const uint32_t d = static_cast<uint32_t>(w);
+            a[2 * q] += __uint_as_float(d << 16);
+            a[2 * q + 1] += __uint_as_float(d & 0xFFFF0000u);
         }
     }
+    if (!ok) atomicAdd(reinterpret_cast<int*>(p.ar.peer[p.ar.me] + p.ar.err_off), 1);
     uint4 o;
     o.x = pack_bf2(f2bf(a[0]), f2bf(a[1]));
     o.y = pack_bf2(f2bf(a[2]), f2bf(a[3]));
@@ -172,7 +158,6 @@ __device__ __forceinline__ void stage_input(const QmvParams& p, uint32_t* xp, fl
         const bool resid = p.prologue == QmvPrologue::kResidNorm;
         const uint64_t keep = l2_evict_last();  // norm weights: re-read every token
         const bool ar = AR && p.ar_mode == 2;
-        if (ar) ar_wait(p);
         uint4 xv[kMaxC], nv4[kMaxC], rv[kMaxC], pv[kMaxC];
 #pragma unroll
         for (int c = 0; c < kMaxC; ++c) {
@@ -449,16 +434,19 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) qmv_packed_kernel(const 
             acc1 += __shfl_xor_sync(0xffffffffu, acc1, 2);
             if (W == 1) {
                 // the warp holds the whole sums: lane (g, 0) has rows g and g + 8
+                if (AR && !GEGLU && p.ar_mode == 1) {
+                    // even g pairs its rows with rows g + 1 and g + 9 from lane (g + 1, 0)
+                    const float n0 = __shfl_down_sync(0xffffffffu, acc0, 4);
+                    const float n1 = __shfl_down_sync(0xffffffffu, acc1, 4);
+                    if (t == 0 && (g & 1) == 0) {
+                        if (rb * 16 + g < pg.N) ar_store_pair(p, rb * 16 + g, f2bf(acc0), f2bf(n0));
+                        if (rb * 16 + g + 8 < pg.N) ar_store_pair(p, rb * 16 + g + 8, f2bf(acc1), f2bf(n1));
+                    }
+                }
                 if (t == 0) {
                     if (!GEGLU) {
-                        if (rb * 16 + g < pg.N) {
-                            p.y[rb * 16 + g] = f2bf(acc0);
-                            if (AR) ar_store(p, rb * 16 + g, f2bf(acc0));
-                        }
-                        if (rb * 16 + g + 8 < pg.N) {
-                            p.y[rb * 16 + g + 8] = f2bf(acc1);
-                            if (AR) ar_store(p, rb * 16 + g + 8, f2bf(acc1));
-                        }
+                        if (rb * 16 + g < pg.N) p.y[rb * 16 + g] = f2bf(acc0);
+                        if (rb * 16 + g + 8 < pg.N) p.y[rb * 16 + g + 8] = f2bf(acc1);
                     } else if (j == 0) {
                         gate0 = acc0;
                         gate1 = acc1;
@@ -481,9 +469,11 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) qmv_packed_kernel(const 
                 float* pb = pairbuf + tw * 32;
                 if (!GEGLU) {
                     const int row = rb * 16 + lane;
-                    if (row < pg.N) {
-                        p.y[row] = f2bf(v);
-                        if (AR) ar_store(p, row, f2bf(v));
+                    if (row < pg.N) p.y[row] = f2bf(v);
+                    if (AR && p.ar_mode == 1) {
+                        // even lanes pair their row with the next lane's (lanes 0..15 active)
+                        const float nv = __shfl_down_sync(0x0000ffffu, v, 1);
+                        if ((lane & 1) == 0 && row < pg.N) ar_store_pair(p, row, f2bf(v), f2bf(nv));
                     }
                 } else {
                     pb[j * 16 + lane] = v;  // j = 0 gate rows, j = 1 up rows
@@ -497,7 +487,6 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) qmv_packed_kernel(const 
             buf ^= 1;
         }
     }
-    if (AR) ar_publish(p);
 }
 
 __global__ void qmv_pack_kernel(const uint32_t* __restrict__ w, const bf16* __restrict__ s,
@@ -608,11 +597,6 @@ int choose_team(const QmvParams& p, int max_ctas, int* grid_needed) {
 
 }  // namespace
 
-int qmv_packed_grid(const QmvParams& p) {
-    int grid = 1;
-    choose_team(p, kCtasPerSm * num_sms(), &grid);
-    return grid;
-}
 
 void launch_qmv_packed(const QmvParams& p, cudaStream_t stream, bool pdl) {
     check_packed_stage(p);

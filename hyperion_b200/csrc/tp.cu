@@ -148,7 +148,7 @@ void TpComm::setup_p2p(size_t max_count) {
     if (!active() || size_ > 8) return;
     max_count = (max_count + 7) / 8 * 8;
     p2p_max_ = max_count;
-    const size_t bytes = counters_off() + 4 * 8 + 64;  // data, flags, error count, fused counters
+    const size_t bytes = ll_off() + 2 * static_cast<size_t>(size_) * (max_count / 2) * 8;  // see tp.h
     HYB_CUDA(cudaMalloc(&p2p_local_, bytes));
     HYB_CUDA(cudaMemset(p2p_local_, 0, bytes));
     cudaIpcMemHandle_t mine;
@@ -171,25 +171,23 @@ void TpComm::setup_p2p(size_t max_count) {
     }
     epoch_ = 0;
     ar_seq_ = 0;
-    ar_total_ = 0;
 }
 
-QmvTpFuse TpComm::next_fused_ar(int producer_ctas) {
+QmvTpFuse TpComm::next_fused_ar() {
     if (!fused_ready()) throw CudaError("fused all-reduce: peer buffers are not mapped");
     QmvTpFuse f;
     for (int r = 0; r < size_; ++r) f.peer[r] = static_cast<unsigned char*>(p2p_peer_[r]);
     f.T = size_;
     f.me = rank_;
     f.max_count = p2p_max_;
-    f.counters_off = counters_off();
-    f.err_off = 2 * static_cast<size_t>(size_) * p2p_max_ * 2 + 4 * static_cast<size_t>(size_);
+    f.ll_off = ll_off();
+    f.err_off = err_off();
     // the set alternates: a rank reaches the producer of all-reduce n + 2 only after its
-    // consumer of n + 1, which waited for every rank's producer of n + 1, which each ran
-    // after that rank's consumer of n finished reading set n % 2
+    // consumer of n + 1, which waited for every rank's words of n + 1, which each rank wrote
+    // after its own consumer of n had finished reading set n % 2
     f.set = static_cast<int>(ar_seq_ & 1u);
-    ar_total_ += static_cast<uint32_t>(producer_ctas);
-    f.target = ar_total_;
     ++ar_seq_;
+    f.epoch = ar_seq_;  // words start zeroed, so epoch 0 never matches
     return f;
 }
 
@@ -217,8 +215,7 @@ void TpComm::all_reduce_small_bf16(bf16* buf, size_t count, cudaStream_t stream,
 
 int TpComm::take_wait_errors(cudaStream_t stream) {
     if (!p2p_local_) return 0;
-    int* err = reinterpret_cast<int*>(static_cast<unsigned char*>(p2p_local_) + 2 * static_cast<size_t>(size_) * p2p_max_ * 2 +
-                                      4 * static_cast<size_t>(size_));
+    int* err = reinterpret_cast<int*>(static_cast<unsigned char*>(p2p_local_) + err_off());
     int h = 0;
     HYB_CUDA(cudaMemcpyAsync(&h, err, sizeof(int), cudaMemcpyDeviceToHost, stream));
     HYB_CUDA(cudaStreamSynchronize(stream));

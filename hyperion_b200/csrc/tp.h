@@ -42,24 +42,26 @@ class TpComm {
     // gives up leaves that step's result undefined but never hangs the GPU.
     int take_wait_errors(cudaStream_t stream);
     // Fused all-reduce in the decode qmvs (QmvTpFuse): available once setup_p2p mapped the
-    // peers' buffers. next_fused_ar(ctas) describes the next all-reduce of up to the
-    // set-up count, produced by a qmv of `ctas` CTAs (every rank calls it in the same order
-    // with the same counts, so the receive set and the cumulative target agree).
+    // peers' buffers. next_fused_ar() describes the next all-reduce of up to the set-up
+    // count (every rank calls it in the same order, so the receive set and the epoch agree).
     bool fused_ready() const { return p2p_local_ != nullptr; }
-    QmvTpFuse next_fused_ar(int producer_ctas);
+    QmvTpFuse next_fused_ar();
     // Rank r's `bytes` land at recv + r * bytes on every rank.
     void all_gather_bytes(const void* send, void* recv, size_t bytes, cudaStream_t stream);
 
   private:
     ncclComm_t comm_ = nullptr;
     int rank_ = 0, size_ = 1;
-    // one-shot all-reduce: local buffer = [2 sets][size][max] bf16 + [size] u32 flags + u32 error
+    // local buffer: one-shot all-reduce data [2 sets][size][max] bf16, its flags [size] u32,
+    // the wait-error counter u32, then (16-byte aligned, at ll_off) the fused all-reduce's
+    // flagged words [2 sets][size][max / 2] u64
     void* p2p_local_ = nullptr;
     void* p2p_peer_[8] = {};
     size_t p2p_max_ = 0;
     uint32_t epoch_ = 0;
-    uint32_t ar_seq_ = 0, ar_total_ = 0;  // fused all-reduces issued, producer CTAs counted
-    size_t counters_off() const { return (2 * static_cast<size_t>(size_) * p2p_max_ * 2 + 4 * static_cast<size_t>(size_) + 4 + 15) / 16 * 16; }
+    uint32_t ar_seq_ = 0;  // fused all-reduces issued
+    size_t err_off() const { return 2 * static_cast<size_t>(size_) * p2p_max_ * 2 + 4 * static_cast<size_t>(size_); }
+    size_t ll_off() const { return (err_off() + 4 + 15) / 16 * 16; }
 };
 
 }  // namespace hyb
