@@ -48,14 +48,40 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t phase) {
     return false;
 }
 
-__device__ __forceinline__ float block_sum(float v, float* tmp) {
+// Sum over the CTA in a fixed order (warp trees, then the warps' partials in warp order),
+// so every CTA gets the same bits. `slot` (0 or 1) picks the partials' buffer: each slot
+// is used once per launch, so one barrier suffices.
+__device__ __forceinline__ float block_sum(float v, float* tmp, int slot) {
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     v = warp_sum(v);
+    if (lane == 0) tmp[slot * kWarps + warp] = v;
     __syncthreads();
-    if (lane == 0) tmp[warp] = v;
-    __syncthreads();
-    float r = (lane < kWarps) ? tmp[lane] : 0.f;
+    float r = (lane < kWarps) ? tmp[slot * kWarps + lane] : 0.f;
     return warp_sum(r);
+}
+
+// Operands of a norm prologue that do not depend on earlier kernels (norm weights, the
+// post-norm weights and the layer scalar), loaded before the dependent-launch wait.
+constexpr int kMaxPrologueChunks = kMaxPrologueK / 8 / kThreads;
+struct PrologueWeights {
+    uint4 nw[kMaxPrologueChunks], pw[kMaxPrologueChunks];
+    float scalar = 1.f;
+};
+
+__device__ __forceinline__ PrologueWeights load_prologue_weights(const QmvParams& p) {
+    PrologueWeights w;
+    const int nch = p.K / 8;
+    const uint64_t keep = l2_evict_last();  // norm weights: re-read every token
+    const bool resid = p.prologue == QmvPrologue::kResidNorm;
+#pragma unroll
+    for (int c = 0; c < kMaxPrologueChunks; ++c) {
+        const int j = static_cast<int>(threadIdx.x) + c * kThreads;
+        const uint4 z = make_uint4(0, 0, 0, 0);
+        w.nw[c] = j < nch ? ld_v4_hint(reinterpret_cast<const uint4*>(p.norm_w) + j, keep) : z;
+        w.pw[c] = (resid && j < nch) ? ld_v4_hint(reinterpret_cast<const uint4*>(p.post_w) + j, keep) : z;
+    }
+    if (resid && p.scalar) w.scalar = bf2f(p.scalar[0]);
+    return w;
 }
 
 // ---- fused tensor-parallel all-reduce (QmvTpFuse)
@@ -117,7 +143,8 @@ __device__ __forceinline__ uint4 ar_chunk(const QmvParams& p, int j) {
 // The input vector into shared memory: x (or its norm prologue) as the permuted
 // bf16 pairs the MMA B fragments read, and the per-group sums of x.
 template <bool AR>
-__device__ __forceinline__ void stage_input(const QmvParams& p, uint32_t* xp, float* xsum, float* tmp) {
+__device__ __forceinline__ void stage_input(const QmvParams& p, const PrologueWeights& pw, uint32_t* xp, float* xsum,
+                                            float* tmp) {
     auto ld = [](const uint4* a) { return *a; };
     const int K = p.K;
     if (p.prologue == QmvPrologue::kNone) {
@@ -148,48 +175,52 @@ __device__ __forceinline__ void stage_input(const QmvParams& p, uint32_t* xp, fl
             if (j < K / 8 && (j & 7) == 0) xsum[j >> 3] = part;
         }
     } else {
-        // Norm prologues in one round trip: every thread loads its 16-byte chunks of
-        // x (and resid, post_w, norm_w) with independent vector loads into registers,
-        // then the reductions and the permuted-pair writes work from registers.
-        constexpr int kMaxC = kMaxPrologueK / 8 / kThreads;
+        // Norm prologues in one round trip: every thread loads its 16-byte chunks of x
+        // (and resid) with independent vector loads into registers (the weights came in
+        // before the dependent-launch wait), then the reductions and the permuted-pair
+        // writes work from registers. Chunk c of a thread exists only if K > 4096 c
+        // (block-uniform, so the branch costs nothing).
+        constexpr int kMaxC = kMaxPrologueChunks;
         const int nch = K / 8;
+        const int nc = (nch + kThreads - 1) / kThreads;
         const uint4* x4 = reinterpret_cast<const uint4*>(p.x);
-        const uint4* n4 = reinterpret_cast<const uint4*>(p.norm_w);
         const bool resid = p.prologue == QmvPrologue::kResidNorm;
-        const uint64_t keep = l2_evict_last();  // norm weights: re-read every token
         const bool ar = AR && p.ar_mode == 2;
-        uint4 xv[kMaxC], nv4[kMaxC], rv[kMaxC], pv[kMaxC];
+        uint4 xv[kMaxC], rv[kMaxC];
 #pragma unroll
         for (int c = 0; c < kMaxC; ++c) {
             const int j = static_cast<int>(threadIdx.x) + c * kThreads;
             const uint4 z = make_uint4(0, 0, 0, 0);
-            xv[c] = j < nch ? (ar ? ar_chunk(p, j) : ld(x4 + j)) : z;
-            nv4[c] = j < nch ? ld_v4_hint(n4 + j, keep) : z;
-            rv[c] = (resid && j < nch) ? ld(reinterpret_cast<const uint4*>(p.resid) + j) : z;
-            pv[c] = (resid && j < nch) ? ld_v4_hint(reinterpret_cast<const uint4*>(p.post_w) + j, keep) : z;
+            xv[c] = rv[c] = z;
+            if (c < nc && j < nch) {
+                xv[c] = ar ? ar_chunk(p, j) : ld(x4 + j);
+                if (resid) rv[c] = ld(reinterpret_cast<const uint4*>(p.resid) + j);
+            }
         }
         auto lo = [](uint32_t w) { return __uint_as_float(w << 16); };
         auto hi = [](uint32_t w) { return __uint_as_float(w & 0xFFFF0000u); };
         float ss = 0.f;
 #pragma unroll
         for (int c = 0; c < kMaxC; ++c) {
+            if (c >= nc) break;
             const uint32_t w[4] = {xv[c].x, xv[c].y, xv[c].z, xv[c].w};
 #pragma unroll
             for (int q = 0; q < 4; ++q) ss += lo(w[q]) * lo(w[q]) + hi(w[q]) * hi(w[q]);
         }
-        float inv = 1.0f / sqrtf(block_sum(ss, tmp) / static_cast<float>(K) + p.eps);
+        float inv = 1.0f / sqrtf(block_sum(ss, tmp, 0) / static_cast<float>(K) + p.eps);
         if (resid) {
-            const float sc = p.scalar ? bf2f(p.scalar[0]) : 1.0f;
+            const float sc = pw.scalar;
             float ss2 = 0.f;
 #pragma unroll
             for (int c = 0; c < kMaxC; ++c) {
+                if (c >= nc) break;
                 uint32_t w[4] = {xv[c].x, xv[c].y, xv[c].z, xv[c].w};
                 const uint32_t r[4] = {rv[c].x, rv[c].y, rv[c].z, rv[c].w};
-                const uint32_t pw[4] = {pv[c].x, pv[c].y, pv[c].z, pv[c].w};
+                const uint32_t pw4[4] = {pw.pw[c].x, pw.pw[c].y, pw.pw[c].z, pw.pw[c].w};
 #pragma unroll
                 for (int q = 0; q < 4; ++q) {
-                    float h0 = rbf(lo(r[q]) + rbf(rbf(lo(w[q]) * inv) * lo(pw[q])));
-                    float h1 = rbf(hi(r[q]) + rbf(rbf(hi(w[q]) * inv) * hi(pw[q])));
+                    float h0 = rbf(lo(r[q]) + rbf(rbf(lo(w[q]) * inv) * lo(pw4[q])));
+                    float h1 = rbf(hi(r[q]) + rbf(rbf(hi(w[q]) * inv) * hi(pw4[q])));
                     if (p.scalar) {
                         h0 = rbf(h0 * sc);
                         h1 = rbf(h1 * sc);
@@ -201,13 +232,14 @@ __device__ __forceinline__ void stage_input(const QmvParams& p, uint32_t* xp, fl
                 const int j = static_cast<int>(threadIdx.x) + c * kThreads;
                 if (blockIdx.x == 0 && p.h_out && j < nch) reinterpret_cast<uint4*>(p.h_out)[j] = xv[c];
             }
-            inv = 1.0f / sqrtf(block_sum(ss2, tmp) / static_cast<float>(K) + p.eps);
+            inv = 1.0f / sqrtf(block_sum(ss2, tmp, 1) / static_cast<float>(K) + p.eps);
         }
 #pragma unroll
         for (int c = 0; c < kMaxC; ++c) {
+            if (c >= nc) break;
             const int j = static_cast<int>(threadIdx.x) + c * kThreads;
             const uint32_t w[4] = {xv[c].x, xv[c].y, xv[c].z, xv[c].w};
-            const uint32_t nw[4] = {nv4[c].x, nv4[c].y, nv4[c].z, nv4[c].w};
+            const uint32_t nw[4] = {pw.nw[c].x, pw.nw[c].y, pw.nw[c].z, pw.nw[c].w};
             uint32_t o[4];
             float part = 0.f;
 #pragma unroll
@@ -394,10 +426,12 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) qmv_packed_kernel(const 
     };
     // weights do not depend on the previous kernel: fill the ring before the PDL wait
     while (n_issued < kStages && n_issued < n_items) issue_next();
+    PrologueWeights pw;
+    if (p.prologue != QmvPrologue::kNone) pw = load_prologue_weights(p);
 
     pdl_wait();
     if (threadIdx.x < 32) zero_page[threadIdx.x] = 0u;
-    stage_input<AR>(p, xp, xsum, tmp);
+    stage_input<AR>(p, pw, xp, xsum, tmp);
     __syncthreads();
 
     uint32_t phase_bits = 0;  // one parity bit per stage
