@@ -80,6 +80,12 @@ class HypSamplingConfig(ctypes.Structure):
                 ("min_p", ctypes.c_float), ("seed", ctypes.c_uint64)]
 
 
+class HybSampleResult(ctypes.Structure):
+    _fields_ = [("token", ctypes.c_uint32), ("logit", ctypes.c_float), ("top_k_ids", ctypes.c_uint32 * 8),
+                ("top_k_values", ctypes.c_float * 8), ("top_k_count", ctypes.c_uint32), ("kept", ctypes.c_uint32),
+                ("u", ctypes.c_float), ("total", ctypes.c_float)]
+
+
 class HypStepResultFields(ctypes.Structure):
     _fields_ = [
         ("token_id", ctypes.c_uint32), ("logit", ctypes.c_float), ("peak_mlx_bytes", ctypes.c_uint64),
@@ -108,7 +114,7 @@ EXT_FUNCTIONS = [
     "hyb_model_set_attention_rounding", "hyb_model_stream", "hyb_decode_batch", "hyb_kvstate_clone", "hyb_qmv_batched",
     "hyb_verify",
     "hyb_kv_copy_layer", "hyb_kv_cursor", "hyb_prefill_logits", "hyb_decode_logits", "hyb_decode_forced",
-    "hyb_test_arm_post_append_fault", "hyb_model_set_memory_budget",
+    "hyb_test_arm_post_append_fault", "hyb_model_set_memory_budget", "hyb_sample_logits",
 ]
 
 _lib: Optional[ctypes.CDLL] = None
@@ -174,6 +180,7 @@ def lib() -> ctypes.CDLL:
         "hyb_decode_forced": [P, P, c.c_uint32, P, P],
         "hyb_test_arm_post_append_fault": [],
         "hyb_model_set_memory_budget": [P, c.c_uint64],
+        "hyb_sample_logits": [P, c.c_int32, ctypes.POINTER(HypSamplingConfig), c.c_uint64, P, P],
     }
     for name, args in sig.items():
         fn = getattr(L, name)

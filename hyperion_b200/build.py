@@ -19,7 +19,7 @@ NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 FLAGS = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC,-Wall,-Wuninitialized", "--expt-relaxed-constexpr",
          "-I", os.path.join(REPO, "include"), "-I", CSRC]
-SOURCES = ["qmv.cu", "qmv_packed.cu", "qmv_batched.cu", "qmm.cu", "attention.cu", "attention_fused.cu", "attention_tc.cu", "tma_host.cu", "qmm_tc.cu", "tp.cu", "elementwise.cu", "engine.cu", "abi.cu", "ops_abi.cu",
+SOURCES = ["qmv.cu", "qmv_packed.cu", "qmv_batched.cu", "qmm.cu", "attention.cu", "attention_fused.cu", "attention_tc.cu", "tma_host.cu", "qmm_tc.cu", "tp.cu", "elementwise.cu", "sampler.cu", "engine.cu", "abi.cu", "ops_abi.cu",
            "geometry.cc", "safetensors.cc"]
 
 

@@ -16,9 +16,7 @@
 #include <limits>
 #include <memory>
 #include <new>
-#include <numeric>
 #include <optional>
-#include <random>
 #include <string>
 #include <vector>
 
@@ -183,95 +181,15 @@ std::optional<std::string> validate_sampling(const HypSamplingConfig* c, uint32_
     return std::nullopt;
 }
 
-float bf16_bits_to_float(uint16_t h) {
-    uint32_t u = static_cast<uint32_t>(h) << 16;
-    float f;
-    std::memcpy(&f, &u, 4);
-    return f;
-}
-
-// Host sampler over one post-softcap logit row: temperature, then top-p, min-p,
-// top-k masks, softmax and an inverse-CDF draw from std::mt19937_64 (the steps of
-// forward.cc:191-322).
-hyb::StepOut sample_row(const std::vector<uint16_t>& row, const HypSamplingConfig& cfg, uint64_t rng_state) {
-    const size_t n = row.size();
-    std::vector<float> src(n);
-    for (size_t i = 0; i < n; ++i) src[i] = bf16_bits_to_float(row[i]);
-    const float ninf = -std::numeric_limits<float>::infinity();
-    std::vector<float> lg(src);
-    const float inv_t = 1.0f / cfg.temperature;
-    for (float& v : lg) v *= inv_t;
-    float mx = ninf;
-    for (float v : lg) mx = std::max(mx, v);
-    std::vector<float> pr(n);
-    float z = 0.f;
-    for (size_t i = 0; i < n; ++i) {
-        pr[i] = std::exp(lg[i] - mx);
-        z += pr[i];
-    }
-    if (z > 0.f)
-        for (float& v : pr) v /= z;
-    if (cfg.top_p > 0.0f && cfg.top_p <= 1.0f) {
-        std::vector<uint32_t> idx(n);
-        std::iota(idx.begin(), idx.end(), 0u);
-        std::sort(idx.begin(), idx.end(), [&](uint32_t a, uint32_t b) { return pr[a] > pr[b]; });
-        std::vector<char> keep(n, 0);
-        float cum = 0.f;
-        for (uint32_t i : idx) {
-            keep[i] = 1;
-            cum += pr[i];
-            if (cum >= cfg.top_p) break;
-        }
-        for (size_t i = 0; i < n; ++i)
-            if (!keep[i]) lg[i] = ninf;
-    }
-    if (cfg.min_p > 0.0f && cfg.min_p < 1.0f) {
-        float mp = 0.f;
-        for (float v : pr) mp = std::max(mp, v);
-        const float th = cfg.min_p * mp;
-        for (size_t i = 0; i < n; ++i)
-            if (pr[i] < th) lg[i] = ninf;
-    }
-    if (cfg.top_k > 0 && static_cast<uint32_t>(cfg.top_k) < n) {
-        std::vector<uint32_t> idx(n);
-        std::iota(idx.begin(), idx.end(), 0u);
-        std::partial_sort(idx.begin(), idx.begin() + cfg.top_k, idx.end(),
-                          [&](uint32_t a, uint32_t b) { return lg[a] > lg[b]; });
-        std::vector<char> keep(n, 0);
-        for (int32_t i = 0; i < cfg.top_k; ++i) keep[idx[i]] = 1;
-        for (size_t i = 0; i < n; ++i)
-            if (!keep[i]) lg[i] = ninf;
-    }
-    float fm = ninf;
-    for (float v : lg) fm = std::max(fm, v);
-    std::vector<float> sp(n);
-    float sz = 0.f;
-    for (size_t i = 0; i < n; ++i) {
-        sp[i] = (lg[i] == ninf) ? 0.f : std::exp(lg[i] - fm);
-        sz += sp[i];
-    }
-    std::mt19937_64 rng(rng_state);
-    std::uniform_real_distribution<float> uni(0.0f, sz);
-    const float u = uni(rng);
-    float c = 0.f;
-    uint32_t arg = 0;
-    for (size_t i = 0; i < n; ++i) {
-        c += sp[i];
-        arg = static_cast<uint32_t>(i);
-        if (u <= c) break;
-    }
-    hyb::StepOut out;
-    out.token = arg;
-    out.logit = src[arg];
-    std::vector<uint32_t> idx(n);
-    std::iota(idx.begin(), idx.end(), 0u);
-    const size_t k = std::min<size_t>(HYP_TOP_K_LOGPROBS, n);
-    std::partial_sort(idx.begin(), idx.begin() + k, idx.end(), [&](uint32_t a, uint32_t b) { return src[a] > src[b]; });
-    for (size_t i = 0; i < k; ++i) {
-        out.topk_idx[i] = idx[i];
-        out.topk_val[i] = src[idx[i]];
-    }
-    return out;
+// The device sampler's settings for one step: the call's config with the step's seed.
+hyb::SampleSpec sample_spec(const HypSamplingConfig& c, uint64_t seed) {
+    hyb::SampleSpec sp;
+    sp.temperature = c.temperature;
+    sp.top_k = c.top_k;
+    sp.top_p = std::isnan(c.top_p) ? 0.f : c.top_p;
+    sp.min_p = c.min_p;
+    sp.seed = seed;
+    return sp;
 }
 
 // Predictive admission before any work (the reference's governor, model.cc:665-683,
@@ -480,8 +398,10 @@ HypStatus prefill_impl(HypModel model, HypKvState kv, const HypTokenStream* toke
         // a fresh state always grows its global caches: the call is staged, and a failure
         // leaves the state fresh (model.cc:531-600)
         hyb::KvTransaction tx = m.begin_kv_transaction(*kv->kv, tokens->count);
+        const hyb::SampleSpec spec = sampled ? sample_spec(*cfg, cfg->seed) : hyb::SampleSpec{};
         try {
-            o = m.prefill(*kv->kv, tokens->tokens, tokens->count, (sampled || host_logits) ? &logits : nullptr);
+            o = m.prefill(*kv->kv, tokens->tokens, tokens->count, host_logits ? &logits : nullptr,
+                          sampled ? &spec : nullptr);
             maybe_inject_fault();
         } catch (...) {
             if (tx.active) m.rollback_kv_transaction(*kv->kv, tx);
@@ -489,10 +409,6 @@ HypStatus prefill_impl(HypModel model, HypKvState kv, const HypTokenStream* toke
             throw;
         }
         tx = hyb::KvTransaction{};  // publish (a fresh state kept no buffers worth freeing)
-        if (sampled) {
-            o = sample_row(logits, *cfg, cfg->seed);
-            kv->kv->last_token = o.token;
-        }
         if (host_logits) std::memcpy(host_logits, logits.data(), logits.size() * 2);
         write_result(out, &o, o.near_tie ? 1u : 0u, HYP_GOVERNOR_READY, m, *kv->kv, sampled);
         return ok();
@@ -534,19 +450,16 @@ HypStatus decode_impl(HypModel model, HypKvState kv, uint32_t n_tokens, const Hy
         hyb::KvTransaction tx = m.begin_kv_transaction(*kv->kv, n_tokens);
         for (uint32_t step = 0; step < n_tokens; ++step) {
             if (forced) kv->kv->last_token = *forced;
+            const hyb::SampleSpec spec = sampled ? sample_spec(*cfg, rng) : hyb::SampleSpec{};
             try {
-                o = m.decode_step(*kv->kv, (sampled || host_logits) ? &logits : nullptr);
+                o = m.decode_step(*kv->kv, host_logits ? &logits : nullptr, sampled ? &spec : nullptr);
                 if (step == 0) maybe_inject_fault();
             } catch (...) {
                 if (tx.active) m.rollback_kv_transaction(*kv->kv, tx);
                 else kv->kv->poisoned = true;
                 throw;
             }
-            if (sampled) {
-                o = sample_row(logits, *cfg, rng);
-                kv->kv->last_token = o.token;
-                rng = rng * 6364136223846793005ULL + 1442695040888963407ULL;
-            }
+            if (sampled) rng = rng * 6364136223846793005ULL + 1442695040888963407ULL;  // model.cc:944
             if (o.near_tie) ++near_ties;
         }
         tx = hyb::KvTransaction{};  // publish: free the live buffers the staged ones replaced

@@ -284,6 +284,7 @@ Model::~Model() {
     if (ws_.h_topk_val) cudaFreeHost(ws_.h_topk_val);
     if (ws_.h_cand) cudaFreeHost(ws_.h_cand);
     if (ws_.h_ids) cudaFreeHost(ws_.h_ids);
+    if (ws_.h_sample) cudaFreeHost(ws_.h_sample);
     if (bws_.h_seqs) cudaFreeHost(bws_.h_seqs);
     if (bws_.h_idx) cudaFreeHost(bws_.h_idx);
     if (bws_.h_val) cudaFreeHost(bws_.h_val);
@@ -910,7 +911,7 @@ void Model::forward_chunk(KvState& kv, int L, uint32_t offset) {
 }
 
 StepOut Model::epilogue(const bf16* final_row, bool fused_prologue, const bf16* dn, const bf16* resid,
-                        std::vector<uint16_t>* logits_out) {
+                        std::vector<uint16_t>* logits_out, const SampleSpec* sample) {
     const Geometry& g = geo_;
     const int H = static_cast<int>(g.hidden);
     QmvParams p;  // lm_head over this rank's vocabulary rows (all of them when TP = 1)
@@ -942,6 +943,40 @@ StepOut Model::epilogue(const bf16* final_row, bool fused_prologue, const bf16* 
     launch_softcap_topk(ws_.logits.p, vocab_local_, g.softcap, ws_.topk_scratch.p,
                         static_cast<int>(ws_.topk_scratch.n), ws_.topk_idx.p, ws_.topk_val.p, stream_);
     const int T = tp_size_;
+    if (sample) {
+        // the sampler reads the whole post-softcap row: with tensor parallelism every rank
+        // gathers it and samples the same bits (same row, same seed)
+        const bf16* row = ws_.logits.p;
+        if (T > 1) {
+            tp_.all_gather_bytes(ws_.logits.p, ws_.logits_all.p, static_cast<size_t>(vocab_local_) * 2, stream_);
+            row = ws_.logits_all.p;
+        }
+        if (ws_.sample.n == 0) {
+            ws_.sample.reset(sizeof(SampleResult));
+            HYB_CUDA(cudaMallocHost(&ws_.h_sample, sizeof(SampleResult)));
+        }
+        SampleResult* d = reinterpret_cast<SampleResult*>(ws_.sample.p);
+        launch_sample(row, static_cast<int>(g.vocab), *sample, d, stream_);
+        HYB_CUDA(cudaMemcpyAsync(ws_.h_sample, d, sizeof(SampleResult), cudaMemcpyDeviceToHost, stream_));
+        if (logits_out) {
+            logits_out->resize(g.vocab);
+            HYB_CUDA(cudaMemcpyAsync(logits_out->data(), row, static_cast<size_t>(g.vocab) * 2, cudaMemcpyDeviceToHost,
+                                     stream_));
+        }
+        HYB_CUDA(cudaStreamSynchronize(stream_));
+        if (T > 1 && tp_.take_wait_errors(stream_))
+            throw CudaError("tensor-parallel all-reduce: a wait for a peer's flag gave up");
+        const SampleResult& r = *ws_.h_sample;
+        StepOut out;
+        out.token = r.token;
+        out.logit = r.logit;
+        out.near_tie = false;  // sampled steps report no near-tie events (forward.cc:191-322)
+        for (uint32_t i = 0; i < 8; ++i) {
+            out.topk_idx[i] = r.topk_idx[i];
+            out.topk_val[i] = r.topk_val[i];
+        }
+        return out;
+    }
     if (T > 1) {
         // every rank's (winner, runner-up) with global vocabulary indices, all-gathered
         tp_candidates_kernel<<<1, 32, 0, stream_>>>(ws_.topk_idx.p, ws_.topk_val.p, static_cast<uint32_t>(vocab0_),
@@ -999,7 +1034,8 @@ StepOut Model::epilogue(const bf16* final_row, bool fused_prologue, const bf16* 
     return out;
 }
 
-StepOut Model::prefill(KvState& kv, const uint32_t* tokens, uint32_t count, std::vector<uint16_t>* logits_out) {
+StepOut Model::prefill(KvState& kv, const uint32_t* tokens, uint32_t count, std::vector<uint16_t>* logits_out,
+                       const SampleSpec* sample) {
     constexpr uint32_t kChunk = 2048;  // model.cc:574
     const uint32_t first = std::min(kChunk, count);
     ensure_workspace(static_cast<int>(first), std::min<uint32_t>(count, 32768));
@@ -1015,7 +1051,7 @@ StepOut Model::prefill(KvState& kv, const uint32_t* tokens, uint32_t count, std:
         else {
             // lm_head on the last row only: rows are independent (forward.cc:137-152)
             const bf16* last = ws_.xn.p + static_cast<size_t>(take - 1) * geo_.hidden;
-            StepOut o = epilogue(last, false, nullptr, nullptr, logits_out);
+            StepOut o = epilogue(last, false, nullptr, nullptr, logits_out, sample);
             kv.offset = count;
             kv.last_token = o.token;
             return o;
@@ -1234,14 +1270,14 @@ void Model::decode_layers(KvState& kv) {
     }
 }
 
-StepOut Model::decode_step(KvState& kv, std::vector<uint16_t>* logits_out) {
+StepOut Model::decode_step(KvState& kv, std::vector<uint16_t>* logits_out, const SampleSpec* sample) {
     ensure_workspace(1, std::min<uint32_t>(kv.offset + 1, 32768));
     if (kv.offset + 1 > 32768) throw std::runtime_error("decode beyond 32768 tokens is not supported");
     reserve(kv, 1);
     ws_.h_ids[0] = kv.last_token;
     HYB_CUDA(cudaMemcpyAsync(ws_.ids.p, ws_.h_ids, sizeof(uint32_t), cudaMemcpyHostToDevice, stream_));
     decode_layers(kv);
-    StepOut o = epilogue(nullptr, true, ws_.dn.p, ws_.h_b.p, logits_out);
+    StepOut o = epilogue(nullptr, true, ws_.dn.p, ws_.h_b.p, logits_out, sample);
     kv.offset += 1;
     kv.last_token = o.token;
     return o;

@@ -154,6 +154,8 @@ struct Workspace {
     uint32_t* h_cand = nullptr;      // tensor parallel: gathered candidates
     uint32_t* h_ids = nullptr;
     int h_ids_cap = 0;
+    DevPtr<unsigned char> sample;    // SampleResult of the device sampler
+    SampleResult* h_sample = nullptr;  // pinned mirror
 };
 
 // Buffers of a batched decode step (sized for the largest batch seen).
@@ -211,9 +213,11 @@ class Model {
     uint64_t memory_budget() const { return memory_budget_; }
 
     // Prefill a prompt on a fresh state; returns the greedy sample of the last row.
-    StepOut prefill(KvState& kv, const uint32_t* tokens, uint32_t count, std::vector<uint16_t>* logits_out);
+    // With `sample` the last row is sampled on the device (sampler.cu) instead of taken greedily.
+    StepOut prefill(KvState& kv, const uint32_t* tokens, uint32_t count, std::vector<uint16_t>* logits_out,
+                    const SampleSpec* sample = nullptr);
     // One decode step at kv.offset from kv.last_token.
-    StepOut decode_step(KvState& kv, std::vector<uint16_t>* logits_out);
+    StepOut decode_step(KvState& kv, std::vector<uint16_t>* logits_out, const SampleSpec* sample = nullptr);
     // One greedy decode step of `n` independent sequences together (each at its own
     // offset, from its own last_token): one weight stream per projection for the whole
     // batch. Writes outs[0..n); each state advances by one token.
@@ -254,7 +258,7 @@ class Model {
     std::vector<int> stage_rows(KvState* const* kvs, int B, uint32_t pos_step);
     void rows_forward(int B, const std::vector<int>& keys_max, const KvState* one_seq);
     StepOut epilogue(const bf16* final_row, bool fused_prologue, const bf16* dn, const bf16* resid,
-                     std::vector<uint16_t>* logits_out);
+                     std::vector<uint16_t>* logits_out, const SampleSpec* sample);
 
     Geometry geo_;
     bool loaded_ = false;

@@ -160,6 +160,26 @@ void launch_gather_ring(const bf16* cache, int cap, int pos0, int n, int row_ele
 
 // logits -> bf16 softcap (cap > 0) in place, then per-block top candidates for argmax/top-k.
 // Final result: idx/val of the TOPK largest (first index wins ties), plus top2 for near-tie.
+// Seeded stochastic sampling of one post-softcap logit row on the device (sampler.cu):
+// temperature, top-p, min-p and top-k filters, softmax and a std::mt19937_64-seeded
+// inverse-CDF draw with the reference's step order (forward.cc:191-322). Filters are off at
+// 0 (top_p also at >= 1); temperature must be > 0. One CTA; no scratch memory.
+struct SampleSpec {
+    float temperature = 1.f, top_p = 0.f, min_p = 0.f;
+    int top_k = 0;
+    uint64_t seed = 0;
+};
+struct SampleResult {
+    uint32_t token;
+    float logit;                      // the sampled token's raw (post-softcap) logit
+    uint32_t topk_idx[8];             // the 8 largest raw logits, value desc, index asc
+    float topk_val[8];
+    uint32_t topk_count;
+    uint32_t kept;                    // tokens the filters kept
+    float u, sz;                      // the draw and the kept tokens' total weight
+};
+void launch_sample(const bf16* logits, int n, const SampleSpec& spec, SampleResult* out, cudaStream_t stream);
+
 void launch_softcap_topk(bf16* logits, int N, float cap, float* scratch, int scratch_floats,
                          uint32_t* out_idx, float* out_val, cudaStream_t stream);
 int softcap_topk_scratch_floats(int N);

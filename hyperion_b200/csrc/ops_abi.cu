@@ -3,6 +3,8 @@
 #include "hyperion_b200.h"
 #include "kernels.h"
 
+#include <cmath>
+#include <cstddef>
 #include <cstdio>
 #include <exception>
 #include <string>
@@ -296,6 +298,31 @@ HypStatus hyb_sdpa_prefill(const void* q, const void* k, const void* v, void* ou
         p.softcap = softcap;
         p.rounding = rounding;
         hyb::launch_prefill_attn(p, as_stream(stream));
+    });
+}
+
+static_assert(sizeof(HybSampleResult) == sizeof(hyb::SampleResult), "HybSampleResult mirrors hyb::SampleResult");
+static_assert(offsetof(HybSampleResult, top_k_count) == offsetof(hyb::SampleResult, topk_count),
+              "HybSampleResult mirrors hyb::SampleResult");
+
+HypStatus hyb_sample_logits(const void* logits, int32_t n, const HypSamplingConfig* config, uint64_t rng_state,
+                            void* result, void* stream) {
+    if (!logits || !config || !result) return hyb::abi_fail(HYP_STATUS_INVALID_ARGUMENT, "null pointer argument");
+    if (n <= 0) return hyb::abi_fail(HYP_STATUS_INVALID_ARGUMENT, "sample_logits: empty row");
+    if (!(config->temperature > 0.0f)) return hyb::abi_fail(HYP_STATUS_INVALID_ARGUMENT, "sample_logits: temperature must be > 0");
+    if (config->top_k < 0 || config->top_k > n) return hyb::abi_fail(HYP_STATUS_INVALID_ARGUMENT, "sample_logits: top_k must be in [0, n]");
+    if (!std::isnan(config->top_p) && (config->top_p < 0.0f || config->top_p > 1.0f))
+        return hyb::abi_fail(HYP_STATUS_INVALID_ARGUMENT, "sample_logits: top_p must be in [0, 1]");
+    if (config->min_p < 0.0f || config->min_p >= 1.0f) return hyb::abi_fail(HYP_STATUS_INVALID_ARGUMENT, "sample_logits: min_p must be in [0, 1)");
+    return run([&] {
+        hyb::SampleSpec sp;
+        sp.temperature = config->temperature;
+        sp.top_k = config->top_k;
+        sp.top_p = std::isnan(config->top_p) ? 0.f : config->top_p;
+        sp.min_p = config->min_p;
+        sp.seed = rng_state;
+        hyb::launch_sample(static_cast<const hyb::bf16*>(logits), n, sp, static_cast<hyb::SampleResult*>(result),
+                           as_stream(stream));
     });
 }
 

@@ -186,6 +186,33 @@ HypStatus hyb_sdpa_prefill(const void* q, const void* k, const void* v, void* ou
                            float softcap, int32_t rounding, void* stream);
 
 /*
+ * Result of one device sampling call (hyb_sample_logits), written to device memory.
+ */
+typedef struct HybSampleResult {
+    uint32_t token;             /* the sampled vocabulary index */
+    float logit;                /* its post-softcap logit */
+    uint32_t top_k_ids[8];      /* the 8 largest logits, value descending, index ascending */
+    float top_k_values[8];
+    uint32_t top_k_count;       /* min(8, n) */
+    uint32_t kept;              /* tokens the top-p / min-p / top-k filters kept */
+    float u;                    /* the uniform draw in [0, total) */
+    float total;                /* the kept tokens' softmax weight sum (relative to the max) */
+} HybSampleResult;
+
+/*
+ * Seeded stochastic sampling of one post-softcap bf16 logit row of length n on the
+ * device, the step the sampled ABI calls run after their lm_head (replaces the host
+ * sampler of native/hyperion_mlx/src/forward.cc:191-322 with its step order:
+ * temperature, top-p, min-p, top-k, softmax, a draw u = uniform_real_distribution<float>
+ * (0, total) from std::mt19937_64(rng_state), the first index whose running sum reaches
+ * u). config follows hyp_decode_block_sampled's validation; temperature must be > 0.
+ * `result` is device memory of sizeof(HybSampleResult) bytes. Among equal logits the
+ * filters keep lower indices first. No device memory is allocated.
+ */
+HypStatus hyb_sample_logits(const void* logits, int32_t n, const HypSamplingConfig* config, uint64_t rng_state,
+                            void* result, void* stream);
+
+/*
  * RMSNorm over rows of length D: out = bf16(bf16(x * rsqrt(mean(x^2) + eps)) * w);
  * w may be NULL (the weightless v_norm). Replaces mx::fast::rms_norm
  * (native/hyperion_mlx/src/forward.cc:25-27).

@@ -4,6 +4,7 @@ the reference-compiled checkers under oracle/_ref/.
 TEST INFRASTRUCTURE ONLY (see oracle/hyp_oracle.c).
 
   * oracle/liboracle.so      <- oracle/hyp_oracle.c (gcc -O3 -fopenmp)
+  * oracle/liboracle_rng.so  <- oracle/std_rng.cc (the standard library's mt19937_64 draw)
   * oracle/_ref/libref_index.so <- the reference's MLX-free sources
         native/hyperion_mlx/src/{kv.cc,geometry.cc,dispatch.cc}
     compiled where they lie, plus oracle/ref_shim.cc (a C wrapper of ours), so
@@ -40,6 +41,11 @@ def build() -> str:
         _run(["gcc", "-O3", "-march=x86-64-v2", "-ffp-contract=off", "-fopenmp", "-fPIC", "-shared", "-std=c11",
               src, "-o", out + ".tmp", "-lm"])
         os.replace(out + ".tmp", out)
+    rng_out = os.path.join(HERE, "liboracle_rng.so")
+    rng_src = os.path.join(HERE, "std_rng.cc")
+    if not os.path.exists(rng_out) or os.path.getmtime(rng_out) < os.path.getmtime(rng_src):
+        _run(["g++", "-O2", "-fPIC", "-shared", "-std=c++17", rng_src, "-o", rng_out + ".tmp"])
+        os.replace(rng_out + ".tmp", rng_out)
     return out
 
 

@@ -537,3 +537,66 @@ def synthetic_tensors(geo: Geometry, seed: int) -> Dict[str, np.ndarray]:
             t[p + nm + ".weight"] = synth_norm(nxt(), H, ztab)
         t[p + "layer_scalar"] = synth_norm(nxt(), 1, ztab)
     return t
+
+
+# ----------------------------------------------------------------------------- sampling
+
+_RNG_LIB = None
+
+
+def rng_lib() -> ctypes.CDLL:
+    """The standard library's mt19937_64 / uniform_real_distribution<float> draw."""
+    global _RNG_LIB
+    if _RNG_LIB is None:
+        lib()  # builds both libraries
+        L = ctypes.CDLL(os.path.join(_HERE, "liboracle_rng.so"))
+        L.orc_mt19937_64_first.argtypes = [ctypes.c_uint64]
+        L.orc_mt19937_64_first.restype = ctypes.c_uint64
+        L.orc_uniform_float_draw.argtypes = [ctypes.c_uint64, ctypes.c_float]
+        L.orc_uniform_float_draw.restype = ctypes.c_float
+        _RNG_LIB = L
+    return _RNG_LIB
+
+
+def sample(logits_bits: np.ndarray, temperature: float, top_k: int = 0, top_p: float = 0.0, min_p: float = 0.0,
+           seed: int = 0):
+    """ForwardPass::sample_stochastic (forward.cc:191-322) over one post-softcap bf16 row,
+    in float32 with the reference's sequential sums. Sorts are stable (equal values keep
+    index order), which the reference leaves unspecified. Returns (token, logit, u, sz,
+    kept, top-8 ids, top-8 values)."""
+    f32 = np.float32
+    src = fl(np.asarray(logits_bits, dtype=np.uint16).reshape(-1))
+    n = src.size
+    lg = (src * f32(f32(1.0) / f32(temperature))).astype(f32)
+    mx = lg.max()
+    probs = np.exp((lg - mx).astype(f32)).astype(f32)
+    z = np.cumsum(probs, dtype=f32)[-1]
+    if z > 0:
+        probs = (probs / z).astype(f32)
+    ninf = f32(-np.inf)
+    lg = lg.copy()
+    if 0.0 < top_p <= 1.0:
+        order = np.argsort(-probs, kind="stable")
+        cum = np.cumsum(probs[order], dtype=f32)
+        reach = np.nonzero(cum >= f32(top_p))[0]
+        count = (reach[0] + 1) if reach.size else n
+        keep = np.zeros(n, dtype=bool)
+        keep[order[:count]] = True
+        lg[~keep] = ninf
+    if 0.0 < min_p < 1.0:
+        thr = f32(min_p) * probs.max()
+        lg[probs < thr] = ninf
+    if 0 < top_k < n:
+        order = np.argsort(-lg, kind="stable")
+        keep = np.zeros(n, dtype=bool)
+        keep[order[:top_k]] = True
+        lg[~keep] = ninf
+    fmax = lg.max()
+    sp = np.where(lg == ninf, f32(0), np.exp((lg - fmax).astype(f32))).astype(f32)
+    cum = np.cumsum(sp, dtype=f32)
+    sz = cum[-1]
+    u = f32(rng_lib().orc_uniform_float_draw(seed & ((1 << 64) - 1), float(sz)))
+    hit = np.nonzero(u <= cum)[0]
+    tok = int(hit[0]) if hit.size else n - 1
+    top = np.argsort(-src, kind="stable")[:min(8, n)]
+    return tok, float(src[tok]), float(u), float(sz), int((lg != ninf).sum()), top, src[top]

@@ -1,5 +1,5 @@
 """Tensor parallelism on 2 GPUs (one process per GPU) against the same model at TP = 1,
-through batch-1 decode, a speculative verify pass and a batched decode step.
+through batch-1 decode, a speculative verify pass, a batched decode step and sampled steps.
 
 Both runs load the seeded synthetic 27B-shaped decoder (config 4, 6 layers) through
 the engine; each TP rank generates exactly its shard of the TP = 1 weights. The TP = 2
@@ -48,8 +48,11 @@ def _run(rank, world, uid, prompt, forced, results):
     _, vtoks, _ = v.verify([int(t) for t in np.random.default_rng(5).integers(0, 262144, 6)])
     b1, b2 = kv.clone(last_token=11), kv.clone(last_token=12)
     btoks, _ = eng.decode_batch([b1, b2])
-    results[(world, rank)] = (toks, np.stack(lgs), vtoks, btoks)
-    for k in (v, b1, b2, kv):
+    # sampled steps: every rank gathers the whole row and draws the same token
+    sm = kv.clone(last_token=13)
+    stoks = [sm.decode(1, sampling=hb.HypSamplingConfig(0.8, 40, 0.9, 0.0, 5 + i))[0].token_id for i in range(3)]
+    results[(world, rank)] = (toks, np.stack(lgs), vtoks, btoks, stoks)
+    for k in (v, b1, b2, sm, kv):
         k.close()
     eng.close()
 
@@ -61,15 +64,15 @@ def test_tp2_matches_tp1(built_lib):
     results = ctx.Manager().dict()
     prompt = np.random.default_rng(3).integers(0, 262144, 40).tolist()
     mp.start_processes(_run, args=(1, b"", prompt, None, results), nprocs=1, join=True, start_method="spawn")
-    ref_toks, ref_lg, ref_v, ref_b = results[(1, 0)]
+    ref_toks, ref_lg, ref_v, ref_b, _ = results[(1, 0)]
     # teacher forcing: step i feeds the TP = 1 token of step i
     forced = ref_toks[:STEPS]
     uid = hb.nccl_unique_id()
     mp.start_processes(_run, args=(2, uid, prompt, forced, results), nprocs=2, join=True, start_method="spawn")
-    t0, lg0, v0, b0 = results[(2, 0)]
-    t1, lg1, v1, b1 = results[(2, 1)]
+    t0, lg0, v0, b0, s0 = results[(2, 0)]
+    t1, lg1, v1, b1, s1 = results[(2, 1)]
     assert t0 == t1 and np.array_equal(lg0, lg1)  # every rank returns the same tokens and logits
-    assert v0 == v1 and b0 == b1
+    assert v0 == v1 and b0 == b1 and s0 == s1
     # verify rows and the batched step against TP = 1 (same inputs; caches differ by rounding)
     assert np.mean([a == b for a, b in zip(v0 + b0, ref_v + ref_b)]) >= 7 / 9, (v0, ref_v, b0, ref_b)
     rels = [rel_l2(lg0[i], ref_lg[i]) for i in range(len(ref_lg))]
