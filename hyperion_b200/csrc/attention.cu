@@ -514,13 +514,20 @@ size_t decode_attn_scratch_bytes(int n_heads, int n_kv, int hd, int max_keys) {
            align256(sizeof(float) * static_cast<size_t>(n_heads) * max_keys);
 }
 
-void launch_decode_attn(const DecodeAttnParams& p, cudaStream_t stream) {
+// Every shape check of the split-K decode attention except the scratch size (throws ArgError).
+static void check_decode_attn_shape(const DecodeAttnParams& p) {
     if (p.n_keys <= 0 || p.n_kv <= 0 || p.n_heads % p.n_kv != 0) throw ArgError("decode attention: bad shape");
     if (p.n_heads / p.n_kv > kMaxRep) throw ArgError("decode attention: GQA group too large");
     if (p.n_keys > kMaxSplits * 512) throw ArgError("decode attention: more than 32768 keys");
+    if ((p.n_heads / p.n_kv) * p.hd > 1024) throw ArgError("decode attention: GQA group x head_dim > 1024");
+    if (p.hd != 64 && p.hd != 128 && p.hd != 256 && p.hd != 512)
+        throw ArgError("decode attention: head_dim must be 64, 128, 256 or 512");
+}
+
+void launch_decode_attn(const DecodeAttnParams& p, cudaStream_t stream) {
+    check_decode_attn_shape(p);
     if (p.scratch_bytes < decode_attn_scratch_bytes(p.n_heads, p.n_kv, p.hd, p.n_keys))
         throw ArgError("decode attention: scratch too small");
-    if ((p.n_heads / p.n_kv) * p.hd > 1024) throw ArgError("decode attention: GQA group x head_dim > 1024");
     DecodeScratch sc = carve(p.scratch, p.n_heads, p.n_kv, p.hd, p.n_keys);
     switch (p.hd) {
         case 64: launch_decode_rep<2>(p, sc, stream); break;
@@ -534,6 +541,8 @@ void launch_decode_attn(const DecodeAttnParams& p, cudaStream_t stream) {
 // Device address of g_decode_noalloc_scratch on the current device. Host code only
 // sees a host-side stand-in for the symbol, so the device address is looked up
 // once per device with cudaGetSymbolAddress (with that device current) and cached.
+// A device reset (cudaDeviceReset) reloads the module, possibly elsewhere, and makes
+// the cached address stale; this library does not reset devices.
 static void* noalloc_scratch_on_current_device() {
     static std::mutex mu;
     static void* addr[64] = {};
@@ -552,6 +561,8 @@ static void* noalloc_scratch_on_current_device() {
 size_t decode_attn_noalloc_limit_bytes() { return kNoAllocScratchBytes; }
 
 void launch_decode_attn_noalloc(DecodeAttnParams p, cudaStream_t stream) {
+    // a rejected call queues no GPU work: every check runs before the counters are cleared
+    check_decode_attn_shape(p);
     const size_t need = decode_attn_scratch_bytes(p.n_heads, p.n_kv, p.hd, p.n_keys);
     if (need > kNoAllocScratchBytes)
         throw ArgError("sdpa_decode_noalloc: this call needs " + std::to_string(need) +

@@ -1065,6 +1065,11 @@ int Model::verify(KvState& kv, const uint32_t* draft, int n, StepOut* outs) {
     if (kv.offset == 0) throw ArgError("verify requires a populated KV state (prefill first)");
     const int L = n + 1;
     if (kv.offset + L > 32768) throw std::runtime_error("decode beyond 32768 tokens is not supported");
+    // the rejected tail may only overwrite ring slots no later step reads: a pass of L rows
+    // needs capacity window + L - 1 (the window + kSpecMax rings hold any L <= kSpecMax + 1)
+    for (const auto& c : kv.local)
+        if (c.cap < geo_.window + static_cast<uint32_t>(L) - 1)
+            throw std::logic_error("verify: ring capacity below window + rows - 1");
     ensure_workspace(L, kv.offset + L);
     ensure_batch_workspace(L);
     reserve(kv, static_cast<uint32_t>(L));

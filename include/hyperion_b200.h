@@ -116,6 +116,9 @@ HypStatus hyb_sdpa_decode(const void* q, const void* k_cache, const void* v_cach
  *   ~114k keys; the kernel itself accepts at most 32768).
  *   The first call on a device looks up the array's device address with that
  *   device current and caches it; make that first call before any stream capture.
+ *   A caller that resets the device (cudaDeviceReset) must not call this entry
+ *   point afterwards in the same process: the cached address would be stale.
+ *   A rejected call (bad shape or a request above 8 MiB) queues no GPU work.
  *   All calls share the one array: it keeps the previous call's contents (each
  *   call clears the parts that must start at zero), and calls that overlap on the
  *   GPU (different streams, other threads) race with each other.

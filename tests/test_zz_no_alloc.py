@@ -45,8 +45,11 @@ def test_noalloc_decode_matches_scratch_version_twice(built_lib):
     L = built_lib
     P = ctypes.c_void_p
     stream = P(torch.cuda.current_stream().cuda_stream)
-    # two different calls in a row: a wrapped sliding-window ring, then a global cache
-    cases = [(16, 8, 256, 1032, 2999, 1024, 1 / 16.0, 0), (32, 16, 128, 4352, 4099, 4100, 1 / 11.3, 1)]
+    # calls in a row: a wrapped sliding-window ring, then a global cache, then a call with
+    # few heads of another head_dim and few keys, which follows calls that left the shared
+    # buffer full of nonzero partials (its counters must be cleared, its stale scores unread)
+    cases = [(16, 8, 256, 1032, 2999, 1024, 1 / 16.0, 0), (32, 16, 128, 4352, 4099, 4100, 1 / 11.3, 1),
+             (4, 2, 64, 512, 300, 301, 1 / 8.0, 2)]
     for (H, Hkv, hd, cap, last_pos, n_keys, scale, seed) in cases:
         q, k, v = _case(H, Hkv, hd, cap, last_pos, n_keys, seed)
         # reference result: the same kernel with a caller-provided, freshly zeroed scratch
@@ -61,6 +64,32 @@ def test_noalloc_decode_matches_scratch_version_twice(built_lib):
         torch.cuda.synchronize()
         assert _rel_l2(out, ref) <= REL_L2_BF16
         assert torch.equal(out, ref)  # same kernel, same split order: identical bits
+
+
+def test_noalloc_decode_rejected_call_leaves_next_call_intact(built_lib):
+    """A call refused for its shape queues nothing, so the next call's result is unchanged."""
+    import torch
+    import hyperion_b200 as hb
+    L = built_lib
+    P = ctypes.c_void_p
+    stream = P(torch.cuda.current_stream().cuda_stream)
+    H, Hkv, hd, cap, last_pos, n_keys = 8, 2, 128, 1024, 700, 701
+    q, k, v = _case(H, Hkv, hd, cap, last_pos, n_keys, 3)
+    nbytes = L.hyb_sdpa_decode_scratch_bytes(H, Hkv, hd, n_keys)
+    scratch = torch.zeros(nbytes, dtype=torch.uint8, device="cuda")
+    ref = torch.empty_like(q)
+    hb.check(L.hyb_sdpa_decode(P(q.data_ptr()), P(k.data_ptr()), P(v.data_ptr()), P(ref.data_ptr()), H, Hkv, hd,
+                               cap, last_pos, n_keys, 1.0, 0.0, 0, P(scratch.data_ptr()), nbytes, stream))
+    # 16 query heads over one KV head: past the argument checks, refused by the kernel's shape
+    # checks (GQA group above 8), which run before the shared buffer is touched
+    bad = L.hyb_sdpa_decode_noalloc(P(q.data_ptr()), P(k.data_ptr()), P(v.data_ptr()), P(ref.data_ptr()), 16, 1, 64,
+                                    cap, last_pos, n_keys, 1.0, 0.0, 0, stream)
+    assert bad == hb.INVALID_ARGUMENT and "GQA" in hb.last_error()
+    out = torch.empty_like(q)
+    hb.check(L.hyb_sdpa_decode_noalloc(P(q.data_ptr()), P(k.data_ptr()), P(v.data_ptr()), P(out.data_ptr()), H, Hkv,
+                                       hd, cap, last_pos, n_keys, 1.0, 0.0, 0, stream))
+    torch.cuda.synchronize()
+    assert torch.equal(out, ref)
 
 
 def test_noalloc_decode_rejects_requests_above_the_fixed_buffer(built_lib):
