@@ -115,6 +115,7 @@ EXT_FUNCTIONS = [
     "hyb_verify",
     "hyb_kv_copy_layer", "hyb_kv_cursor", "hyb_prefill_logits", "hyb_decode_logits", "hyb_decode_forced",
     "hyb_test_arm_post_append_fault", "hyb_model_set_memory_budget", "hyb_sample_logits",
+    "hyb_model_weight_bytes", "hyb_qmv_unpack", "hyb_embed_packed",
 ]
 
 _lib: Optional[ctypes.CDLL] = None
@@ -150,6 +151,8 @@ def lib() -> ctypes.CDLL:
         "hyb_quantized_matmul": [P, P, P, P, P, c.c_int64, c.c_int64, c.c_int64, c.c_int32, c.c_int32, P],
         "hyb_qmv_fused": [P, P, P, P, P, c.c_int64, c.c_int64, c.c_int32, c.c_int32, P, P, P, P, P, c.c_float, P],
         "hyb_qmv_pack": [P, P, P, c.c_int64, c.c_int64, P, P],
+        "hyb_qmv_unpack": [P, c.c_int64, c.c_int64, P, P, P, P],
+        "hyb_embed_packed": [P, c.c_int64, P, c.c_int64, c.c_int64, c.c_uint16, P, P],
         "hyb_qmv_packed": [P, P, P, c.c_int64, c.c_int64, c.c_int32, c.c_int32, P, P, P, P, P, c.c_float, P],
         "hyb_sdpa_decode": [P, P, P, P, c.c_int32, c.c_int32, c.c_int32, c.c_int32, c.c_int32, c.c_int32,
                             c.c_float, c.c_float, c.c_int32, P, c.c_size_t, P],
@@ -180,6 +183,7 @@ def lib() -> ctypes.CDLL:
         "hyb_decode_forced": [P, P, c.c_uint32, P, P],
         "hyb_test_arm_post_append_fault": [],
         "hyb_model_set_memory_budget": [P, c.c_uint64],
+        "hyb_model_weight_bytes": [P, c.POINTER(c.c_uint64), c.POINTER(c.c_uint64), c.POINTER(c.c_uint64)],
         "hyb_sample_logits": [P, c.c_int32, ctypes.POINTER(HypSamplingConfig), c.c_uint64, P, P],
     }
     for name, args in sig.items():
@@ -320,6 +324,13 @@ class Engine:
     def set_memory_budget(self, nbytes: int) -> None:
         """Device-byte ceiling checked by every call's admission (0 = free memory only)."""
         check(lib().hyb_model_set_memory_budget(self._model, nbytes))
+
+    def weight_bytes(self) -> dict:
+        """Device bytes of the weights: resident, algorithmic (codes + scales + biases)
+        and the MLX-layout unpack scratch (hyb_model_weight_bytes)."""
+        r, a, s = ctypes.c_uint64(), ctypes.c_uint64(), ctypes.c_uint64()
+        check(lib().hyb_model_weight_bytes(self._model, ctypes.byref(r), ctypes.byref(a), ctypes.byref(s)))
+        return {"resident": r.value, "algorithmic": a.value, "scratch": s.value}
 
     def decode_batch(self, kvs: Sequence["KvState"]):
         """One greedy step of every state in `kvs` together (hyb_decode_batch):

@@ -671,6 +671,16 @@ HypStatus hyb_model_set_memory_budget(HypModel model, uint64_t bytes) {
     return ok();
 }
 
+HypStatus hyb_model_weight_bytes(HypModel model, uint64_t* resident, uint64_t* algorithmic, uint64_t* scratch) {
+    HypStatus st = validate_model(model);
+    if (st != HYP_STATUS_OK) return st;
+    if (!model->loaded) return fail(HYP_STATUS_INVALID_ARGUMENT, "model is not loaded");
+    if (resident) *resident = model->model->weight_bytes_resident();
+    if (algorithmic) *algorithmic = model->model->weight_bytes_algorithmic();
+    if (scratch) *scratch = model->model->unpack_scratch_bytes();
+    return ok();
+}
+
 HypStatus hyb_kv_cursor(HypKvState kv, uint32_t* offset, uint32_t* last_token) {
     if (kv == nullptr || kv->magic != kKvStateMagic) return fail(HYP_STATUS_INVALID_ARGUMENT, "kvstate handle is invalid");
     if (offset) *offset = kv->kv->offset;

@@ -7,6 +7,7 @@
 //   caches         kv_cache.cc:161-347, kv.cc:7-96
 #include "engine.h"
 #include "safetensors.h"
+#include "qmv_pack.cuh"
 
 #include <algorithm>
 #include <atomic>
@@ -19,6 +20,8 @@ namespace hyb {
 
 // ---------------------------------------------------------------- allocation + device info
 namespace {
+size_t round_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
+
 std::atomic<size_t> g_active{0};
 std::atomic<size_t> g_peak{0};
 std::mutex g_size_mu;
@@ -303,10 +306,10 @@ void Model::set_tensor_parallel(int rank, int size, const void* id) {
 void Model::init_common(const Geometry& g) {
     const int T = tp_size_;
     if (T > 1) {
-        if (g.n_heads % T || g.intermediate % (16 * T) || g.vocab % T || (g.n_heads / T) * g.hd_local % 64 ||
+        if (g.n_heads % T || g.intermediate % (16 * T) || g.vocab % (16 * T) || (g.n_heads / T) * g.hd_local % 64 ||
             (g.n_heads / T) * g.hd_global % 64 || (g.intermediate / T) % 64)
-            throw ArgError("tensor parallel: heads, MLP rows (16-row tiles, 64-wide groups) and vocabulary must "
-                           "split evenly over the ranks");
+            throw ArgError("tensor parallel: heads, MLP rows (16-row tiles, 64-wide groups) and vocabulary "
+                           "(16-row blocks) must split evenly over the ranks");
         for (uint32_t i = 0; i < g.n_layers; ++i)
             if (g.n_kv(i) % T) throw ArgError("tensor parallel: KV heads must split evenly over the ranks");
     }
@@ -338,10 +341,34 @@ void Model::init_common(const Geometry& g) {
     }
 }
 
+// Rows [row0, row0 + n) of a packed matrix are themselves a packed matrix of n rows when
+// row0 is a multiple of 16: row blocks are independent and their size depends on K only.
+MlxView Model::unpack_rows(const unsigned char* packed, int K, int row0, int n, cudaStream_t st) {
+    if (row0 % 16) throw std::logic_error("unpack_rows: row0 must start a 16-row block");
+    const size_t wb = round_up(static_cast<size_t>(n) * K / 2, 256);
+    const size_t sb = round_up(static_cast<size_t>(n) * (K / 64) * 2, 256);
+    if (wb + 2 * sb > unpack_.n) throw std::logic_error("unpack_rows: scratch too small");
+    const PackGeo pg = pack_geo(K, n);
+    MlxView v;
+    auto* w = reinterpret_cast<uint32_t*>(unpack_.p);
+    auto* sc = reinterpret_cast<bf16*>(unpack_.p + wb);
+    auto* bi = reinterpret_cast<bf16*>(unpack_.p + wb + sb);
+    launch_qmv_unpack(packed + static_cast<size_t>(row0 / 16) * pg.rb_bytes, K, n, w, sc, bi, st);
+    v.w = w;
+    v.s = sc;
+    v.b = bi;
+    return v;
+}
+
 void Model::pack_all() {
+    auto mlx_bytes = [](int K, int N) {
+        return round_up(static_cast<size_t>(N) * K / 2, 256) + 2 * round_up(static_cast<size_t>(N) * (K / 64) * 2, 256);
+    };
+    size_t scratch = 0;
     auto pack = [&](QLin& q) {
         q.packed.reset(qmv_packed_bytes(q.K, q.N));
         launch_qmv_pack(q.w.p, q.s.p, q.b.p, q.K, q.N, q.packed.p, stream_);
+        scratch = std::max(scratch, mlx_bytes(q.K, q.N));
     };
     for (auto& L : layers_) {
         pack(L.qkv);
@@ -349,12 +376,67 @@ void Model::pack_all() {
         pack(L.gateup);
         pack(L.down);
     }
-    // the lm_head: this rank's rows of the tied embedding table
+    // the whole embedding table: the embedding gather reads it, and this rank's rows of it
+    // (vocab0_ is a multiple of 16) are the tied lm_head
     const int H = embed_.K;
-    lm_packed_.reset(qmv_packed_bytes(H, vocab_local_));
-    launch_qmv_pack(embed_.w.p + static_cast<size_t>(vocab0_) * (H / 8), embed_.s.p + static_cast<size_t>(vocab0_) * (H / 64),
-                    embed_.b.p + static_cast<size_t>(vocab0_) * (H / 64), H, vocab_local_, lm_packed_.p, stream_);
+    embed_.packed.reset(qmv_packed_bytes(H, embed_.N));
+    launch_qmv_pack(embed_.w.p, embed_.s.p, embed_.b.p, H, embed_.N, embed_.packed.p, stream_);
+    lm_packed_ = embed_.packed.p + static_cast<size_t>(vocab0_ / 16) * pack_geo(H, embed_.N).rb_bytes;
     HYB_CUDA(cudaStreamSynchronize(stream_));
+    auto drop = [](QLin& q) {
+        q.w = DevPtr<uint32_t>();
+        q.s = DevPtr<bf16>();
+        q.b = DevPtr<bf16>();
+    };
+    for (auto& L : layers_) {
+        drop(L.qkv);
+        drop(L.o);
+        drop(L.gateup);
+        drop(L.down);
+    }
+    drop(embed_);
+    // the lm_head of a batch above the qmv's reach unpacks slices of the same scratch
+    const size_t row_bytes = mlx_bytes(H, 16) / 16;
+    lm_slice_rows_ = static_cast<int>(std::min<size_t>(vocab_local_, std::max<size_t>(16, scratch / row_bytes / 16 * 16)));
+    while (lm_slice_rows_ > 16 && mlx_bytes(H, lm_slice_rows_) > scratch) lm_slice_rows_ -= 16;
+    scratch = std::max(scratch, mlx_bytes(H, lm_slice_rows_));
+    unpack_.reset(scratch);
+}
+
+uint64_t Model::weight_bytes_resident() const {
+    uint64_t n = 0;
+    auto q = [&](const QLin& x) { n += x.packed.n + x.w.n * 4 + x.s.n * 2 + x.b.n * 2; };
+    auto v = [&](const DevPtr<bf16>& x) { n += x.n * 2; };
+    for (const auto& L : layers_) {
+        q(L.qkv);
+        q(L.o);
+        q(L.gateup);
+        q(L.down);
+        v(L.q_norm);
+        v(L.k_norm);
+        v(L.in_ln);
+        v(L.post_attn);
+        v(L.pre_ff);
+        v(L.post_ff);
+        v(L.scalar);
+    }
+    q(embed_);
+    v(final_norm_);
+    n += (inv_freq_local_.n + inv_freq_global_.n) * 4;
+    return n;
+}
+
+uint64_t Model::weight_bytes_algorithmic() const {
+    uint64_t n = 0;
+    auto q = [&](const QLin& x) { n += static_cast<uint64_t>(x.N) * x.K / 2 + static_cast<uint64_t>(x.N) * (x.K / 64) * 4; };
+    for (const auto& L : layers_) {
+        q(L.qkv);
+        q(L.o);
+        q(L.gateup);
+        q(L.down);
+    }
+    q(embed_);
+    return n;
 }
 
 void Model::load_synthetic(const Geometry& g, uint64_t seed) {
@@ -819,14 +901,20 @@ void Model::forward_chunk(KvState& kv, int L, uint32_t offset) {
     cudaStream_t st = stream_;
     bf16* h_cur = ws_.h_a.p;
     bf16* h_alt = ws_.h_b.p;
-    launch_embed(ws_.ids.p, L, embed_.w.p, embed_.s.p, embed_.b.p, H, embed_scale_, h_cur, st);
+    // y[L, q.N] = x[L, q.K] · qᵀ through the tcgen05 GEMM over the MLX layout, re-derived
+    // from the packed copy per projection
+    auto gemm = [&](const bf16* x, const QLin& q, bf16* y) {
+        const MlxView m = unpack_rows(q.packed.p, q.K, 0, q.N, st);
+        launch_quantized_matmul(x, m.w, m.s, m.b, y, L, q.K, q.N, st);
+    };
+    launch_embed_packed(ws_.ids.p, L, embed_.packed.p, H, embed_.N, embed_scale_, h_cur, st);
     launch_rms_norm(h_cur, layers_[0].in_ln.p, ws_.xn.p, L, H, g.eps, st);
     size_t li = 0, gi = 0;
     for (uint32_t layer = 0; layer < g.n_layers; ++layer) {
         LayerW& W = layers_[layer];
         const int hd = W.hd, nkv = W.nkv;
         const int qkv_ld = W.q_rows + W.k_rows + W.v_rows;
-        launch_quantized_matmul(ws_.xn.p, W.qkv.w.p, W.qkv.s.p, W.qkv.b.p, ws_.qkv.p, L, H, qkv_ld, st);
+        gemm(ws_.xn.p, W.qkv, ws_.qkv.p);
         const uint32_t committed = offset + static_cast<uint32_t>(L);
         QkvPostParams qp;
         qp.qkv = ws_.qkv.p;
@@ -894,16 +982,16 @@ void Model::forward_chunk(KvState& kv, int L, uint32_t offset) {
             ap.window = 0;
         }
         launch_prefill_attn(ap, st);
-        launch_quantized_matmul(ws_.attn.p, W.o.w.p, W.o.s.p, W.o.b.p, ws_.o.p, L, W.o.K, H, st);
+        gemm(ws_.attn.p, W.o, ws_.o.p);
         tp_.all_reduce_sum_bf16(ws_.o.p, static_cast<size_t>(L) * H, st);  // row-parallel o_proj
         launch_resid_norm(ws_.o.p, W.post_attn.p, h_cur, nullptr, h_alt, W.pre_ff.p, ws_.xn.p, L, H, g.eps, st);
-        launch_quantized_matmul(ws_.xn.p, W.gateup.w.p, W.gateup.s.p, W.gateup.b.p, ws_.gu.p, L, H, 2 * I, st);
+        gemm(ws_.xn.p, W.gateup, ws_.gu.p);
         {
             dim3 grid(std::min((I + 255) / 256, 64), L);
             geglu_interleaved_kernel<<<grid, 256, 0, st>>>(ws_.gu.p, ws_.act.p, I);
             HYB_LAUNCH_CHECK("geglu_interleaved_kernel");
         }
-        launch_quantized_matmul(ws_.act.p, W.down.w.p, W.down.s.p, W.down.b.p, ws_.dn.p, L, I, H, st);
+        gemm(ws_.act.p, W.down, ws_.dn.p);
         tp_.all_reduce_sum_bf16(ws_.dn.p, static_cast<size_t>(L) * H, st);  // row-parallel down_proj
         const bf16* next_w = (layer + 1 < g.n_layers) ? layers_[layer + 1].in_ln.p : final_norm_.p;
         launch_resid_norm(ws_.dn.p, W.post_ff.p, h_alt, W.scalar.p, h_cur, next_w, ws_.xn.p, L, H, g.eps, st);
@@ -915,10 +1003,7 @@ StepOut Model::epilogue(const bf16* final_row, bool fused_prologue, const bf16* 
     const Geometry& g = geo_;
     const int H = static_cast<int>(g.hidden);
     QmvParams p;  // lm_head over this rank's vocabulary rows (all of them when TP = 1)
-    p.w = embed_.w.p + static_cast<size_t>(vocab0_) * (H / 8);
-    p.packed = lm_packed_.p;
-    p.s = embed_.s.p + static_cast<size_t>(vocab0_) * (H / 64);
-    p.b = embed_.b.p + static_cast<size_t>(vocab0_) * (H / 64);
+    p.packed = lm_packed_;
     p.y = ws_.logits.p;
     p.K = H;
     p.N = vocab_local_;
@@ -1098,7 +1183,7 @@ void Model::decode_layers(KvState& kv) {
     const int nh = heads_local_;
     cudaStream_t st = stream_;
     const uint32_t pos = kv.offset;  // position of the token being decoded
-    launch_embed(ws_.ids.p, 1, embed_.w.p, embed_.s.p, embed_.b.p, H, embed_scale_, ws_.h_e.p, st);
+    launch_embed_packed(ws_.ids.p, 1, embed_.packed.p, H, embed_.N, embed_scale_, ws_.h_e.p, st);
     // Tensor parallel over mapped NVLink peers: the all-reduces after o_proj and down_proj
     // run inside the qmvs (the row-parallel one stores its rows to every rank, the next
     // one's residual+norm prologue sums them); otherwise a separate all-reduce.
@@ -1109,10 +1194,7 @@ void Model::decode_layers(KvState& kv) {
     auto qkv_params = [&](uint32_t layer) {
         const LayerW& W = layers_[layer];
         QmvParams p;
-        p.w = W.qkv.w.p;
         p.packed = W.qkv.packed.p;
-        p.s = W.qkv.s.p;
-        p.b = W.qkv.b.p;
         p.y = ws_.qkv.p;
         p.K = H;
         p.N = W.q_rows + W.k_rows + W.v_rows;
@@ -1217,10 +1299,7 @@ void Model::decode_layers(KvState& kv) {
             launch_decode_attn(dp, st);
         }
         QmvParams po;
-        po.w = W.o.w.p;
         po.packed = W.o.packed.p;
-        po.s = W.o.s.p;
-        po.b = W.o.b.p;
         po.x = ws_.attn.p;
         po.y = ws_.o.p;
         po.K = W.o.K;
@@ -1228,10 +1307,7 @@ void Model::decode_layers(KvState& kv) {
         // gate/up with the post-attention residual + pre-MLP norm in the prologue
         // and GeGLU in the epilogue
         QmvParams pg;
-        pg.w = W.gateup.w.p;
         pg.packed = W.gateup.packed.p;
-        pg.s = W.gateup.s.p;
-        pg.b = W.gateup.b.p;
         pg.x = ws_.o.p;
         pg.y = ws_.act.p;
         pg.K = H;
@@ -1245,10 +1321,7 @@ void Model::decode_layers(KvState& kv) {
         pg.h_out = ws_.h_b.p;
         pg.eps = g.eps;
         QmvParams pd;
-        pd.w = W.down.w.p;
         pd.packed = W.down.packed.p;
-        pd.s = W.down.s.p;
-        pd.b = W.down.b.p;
         pd.x = ws_.act.p;
         pd.y = ws_.dn.p;
         pd.K = W.down.K;
@@ -1288,6 +1361,9 @@ StepOut Model::decode_step(KvState& kv, std::vector<uint16_t>* logits_out, const
     return o;
 }
 
+// Batches up to this size project through qmv_batched; larger ones through the tcgen05 GEMM.
+constexpr int kBatchQmvMax = 16;
+
 void Model::ensure_batch_workspace(int n) {
     if (n <= bws_.cap) return;
     const Geometry& g = geo_;
@@ -1295,6 +1371,7 @@ void Model::ensure_batch_workspace(int n) {
     for (const auto& L : layers_) max_k = std::max({max_k, L.q_rows, L.down.K});
     bws_.x16.reset(qmv_batch_x16_words(n, max_k));
     bws_.logits.reset(static_cast<size_t>(n) * vocab_local_);
+    bws_.lm_slice.reset(n > kBatchQmvMax ? static_cast<size_t>(n) * lm_slice_rows_ : 0);
     bws_.topk_scratch.reset(static_cast<size_t>(n) * softcap_topk_scratch_floats(vocab_local_));
     bws_.topk_idx.reset(static_cast<size_t>(n) * kTopkRowStride);
     bws_.topk_val.reset(static_cast<size_t>(n) * kTopkRowStride);
@@ -1311,8 +1388,6 @@ void Model::ensure_batch_workspace(int n) {
     bws_.cap = n;
 }
 
-// Batches up to this size project through qmv_batched; larger ones through the tcgen05 GEMM.
-constexpr int kBatchQmvMax = 16;
 
 // lm_head over this rank's vocabulary rows for the B final-normed rows in ws_.xn, then
 // soft-cap and top-2 per row (forward.cc:137-189); with tensor parallelism every rank's
@@ -1322,15 +1397,19 @@ void Model::lm_head_rows(int B, StepOut* outs) {
     const int H = static_cast<int>(g.hidden);
     cudaStream_t st = stream_;
     if (B > kBatchQmvMax) {
-        launch_quantized_matmul(ws_.xn.p, embed_.w.p + static_cast<size_t>(vocab0_) * (H / 8),
-                                embed_.s.p + static_cast<size_t>(vocab0_) * (H / 64),
-                                embed_.b.p + static_cast<size_t>(vocab0_) * (H / 64), bws_.logits.p, B, H,
-                                vocab_local_, st);
+        // the tcgen05 GEMM over slices of the lm_head unpacked in turn into the scratch
+        for (int v0 = 0; v0 < vocab_local_; v0 += lm_slice_rows_) {
+            const int n = std::min(lm_slice_rows_, vocab_local_ - v0);
+            const MlxView m = unpack_rows(lm_packed_, H, v0, n, st);
+            launch_quantized_matmul(ws_.xn.p, m.w, m.s, m.b, bws_.lm_slice.p, B, H, n, st);
+            HYB_CUDA(cudaMemcpy2DAsync(bws_.logits.p + v0, sizeof(bf16) * vocab_local_, bws_.lm_slice.p,
+                                       sizeof(bf16) * n, sizeof(bf16) * n, B, cudaMemcpyDeviceToDevice, st));
+        }
     } else {
         launch_qmv_batched_x16(ws_.xn.p, B, H, H, bws_.x16.p, st);
         QmvBatchParams q;
         q.x16 = bws_.x16.p;
-        q.packed = lm_packed_.p;
+        q.packed = lm_packed_;
         q.y = bws_.logits.p;
         q.K = H;
         q.N = vocab_local_;
@@ -1422,13 +1501,14 @@ void Model::rows_forward(int B, const std::vector<int>& keys_max, const KvState*
     // fill the GPU); GeGLU then runs on the interleaved gate/up output. Measured on the
     // 27B shape: the batched qmv wins at 8 sequences (402 vs 286 tok/s), the GEMM at 64
     // (1045 vs 628 tok/s), where the qmv's eight MMA column groups per k-step bind it.
-    auto proj_tc = [&](const bf16* x, int K, const uint32_t* w, const bf16* s, const bf16* b, int N, bf16* y,
-                       bool geglu) {
+    auto proj_tc = [&](const bf16* x, const QLin& q, bf16* y, bool geglu) {
+        const int K = q.K, N = q.N;
+        const MlxView m = unpack_rows(q.packed.p, K, 0, N, st);
         if (!geglu) {
-            launch_quantized_matmul(x, w, s, b, y, B, K, N, st);
+            launch_quantized_matmul(x, m.w, m.s, m.b, y, B, K, N, st);
             return;
         }
-        launch_quantized_matmul(x, w, s, b, ws_.gu.p, B, K, N, st);
+        launch_quantized_matmul(x, m.w, m.s, m.b, ws_.gu.p, B, K, N, st);
         dim3 grid(std::min((N / 2 + 255) / 256, 64), B);
         geglu_interleaved_kernel<<<grid, 256, 0, st>>>(ws_.gu.p, y, N / 2);
         HYB_LAUNCH_CHECK("geglu_interleaved_kernel");
@@ -1436,12 +1516,12 @@ void Model::rows_forward(int B, const std::vector<int>& keys_max, const KvState*
     const bool tc = B > kBatchQmvMax;
     bf16* h_cur = ws_.h_a.p;
     bf16* h_alt = ws_.h_b.p;
-    launch_embed(ws_.ids.p, B, embed_.w.p, embed_.s.p, embed_.b.p, H, embed_scale_, h_cur, st);
+    launch_embed_packed(ws_.ids.p, B, embed_.packed.p, H, embed_.N, embed_scale_, h_cur, st);
     launch_rms_norm(h_cur, layers_[0].in_ln.p, ws_.xn.p, B, H, g.eps, st);
     for (uint32_t layer = 0; layer < g.n_layers; ++layer) {
         LayerW& W = layers_[layer];
         const int qkv_ld = W.q_rows + W.k_rows + W.v_rows;
-        if (tc) proj_tc(ws_.xn.p, H, W.qkv.w.p, W.qkv.s.p, W.qkv.b.p, qkv_ld, ws_.qkv.p, false);
+        if (tc) proj_tc(ws_.xn.p, W.qkv, ws_.qkv.p, false);
         else proj(ws_.xn.p, H, H, W.qkv.packed.p, qkv_ld, ws_.qkv.p, qkv_ld, false);
         if (one_seq) {
             // rows of one sequence: every row's K/V goes into the caches first (one launch),
@@ -1541,13 +1621,13 @@ void Model::rows_forward(int B, const std::vector<int>& keys_max, const KvState*
                 launch_decode_attn(dp, st);
             }
         }
-        if (tc) proj_tc(ws_.attn.p, W.o.K, W.o.w.p, W.o.s.p, W.o.b.p, H, ws_.o.p, false);
+        if (tc) proj_tc(ws_.attn.p, W.o, ws_.o.p, false);
         else proj(ws_.attn.p, W.q_rows, W.o.K, W.o.packed.p, H, ws_.o.p, H, false);
         tp_.all_reduce_sum_bf16(ws_.o.p, static_cast<size_t>(B) * H, st);  // row-parallel o_proj
         launch_resid_norm(ws_.o.p, W.post_attn.p, h_cur, nullptr, h_alt, W.pre_ff.p, ws_.xn.p, B, H, g.eps, st);
         if (tc) {
-            proj_tc(ws_.xn.p, H, W.gateup.w.p, W.gateup.s.p, W.gateup.b.p, W.gateup.N, ws_.act.p, true);
-            proj_tc(ws_.act.p, W.down.K, W.down.w.p, W.down.s.p, W.down.b.p, H, ws_.dn.p, false);
+            proj_tc(ws_.xn.p, W.gateup, ws_.act.p, true);
+            proj_tc(ws_.act.p, W.down, ws_.dn.p, false);
         } else {
             proj(ws_.xn.p, H, H, W.gateup.packed.p, W.gateup.N, ws_.act.p, I, true);
             proj(ws_.act.p, I, W.down.K, W.down.packed.p, H, ws_.dn.p, H, false);

@@ -61,10 +61,17 @@ struct DevPtr {
 };
 
 struct QLin {
-    DevPtr<uint32_t> w;               // MLX layout (prefill GEMM, embedding gather)
+    DevPtr<uint32_t> w;               // MLX layout: only while loading, freed once packed
     DevPtr<bf16> s, b;
-    DevPtr<unsigned char> packed;     // packed resident layout streamed by the decode qmv
+    DevPtr<unsigned char> packed;     // the one resident copy: the packed layout
     int N = 0, K = 0;
+};
+
+// Pointers to an MLX-layout view of a matrix (codes [N, K/8] u32, scales/biases [N, K/64]).
+struct MlxView {
+    const uint32_t* w = nullptr;
+    const bf16* s = nullptr;
+    const bf16* b = nullptr;
 };
 
 struct LayerW {
@@ -163,6 +170,7 @@ struct BatchWorkspace {
     int cap = 0;                       // sequences
     DevPtr<uint32_t> x16;              // [pad(cap)][max K / 2] fp16 activation pairs
     DevPtr<bf16> logits;               // [cap][vocab_local]
+    DevPtr<bf16> lm_slice;             // [cap][lm_slice_rows] one unpacked lm_head slice's GEMM output
     DevPtr<float> topk_scratch;
     DevPtr<uint32_t> topk_idx;         // [cap][8]
     DevPtr<float> topk_val;
@@ -236,6 +244,13 @@ class Model {
     void set_attention_rounding(int mode) { attn_rounding_ = mode; }
     int attention_rounding() const { return attn_rounding_; }
 
+    // Device bytes of the weights held (packed matrices, norms, RoPE tables), the
+    // algorithmic size of the quantised matrices (codes + scales + biases) and the
+    // transient MLX-layout scratch the tensor-core GEMMs unpack into.
+    uint64_t weight_bytes_resident() const;
+    uint64_t weight_bytes_algorithmic() const;
+    uint64_t unpack_scratch_bytes() const { return unpack_.n; }
+
     uint64_t local_kv_bytes(const KvState& kv) const;
     uint64_t global_kv_bytes(const KvState& kv) const;
 
@@ -250,7 +265,12 @@ class Model {
 
   private:
     void init_common(const Geometry& g);
-    void pack_all();  // build the packed decode layout of every projection and the lm_head
+    // Build the packed layout of every projection and of the embedding table, then free
+    // the MLX-layout copies.
+    void pack_all();
+    // The MLX layout of rows [row0, row0 + n) of a packed [?, K] matrix, re-derived into the
+    // shared unpack scratch on `st` (valid until the next call on the same stream).
+    MlxView unpack_rows(const unsigned char* packed, int K, int row0, int n, cudaStream_t st);
     void ensure_workspace(int tokens, uint32_t max_keys);
     void forward_chunk(KvState& kv, int L, uint32_t offset);  // ids already in ws_.ids
     void decode_layers(KvState& kv);
@@ -282,7 +302,9 @@ class Model {
     int inter_local_ = 0;   // MLP intermediate rows on this rank
     int vocab_local_ = 0;   // lm_head rows on this rank, starting at vocab0_
     int vocab0_ = 0;
-    DevPtr<unsigned char> lm_packed_;  // packed lm_head rows of this rank
+    const unsigned char* lm_packed_ = nullptr;  // this rank's lm_head rows inside embed_.packed
+    DevPtr<unsigned char> unpack_;              // MLX-layout scratch of the largest projection
+    int lm_slice_rows_ = 0;                     // lm_head rows one unpack of the scratch holds
     QmvTpFuse last_ar_;                // the last decode layer's down_proj all-reduce (lm_head input)
 };
 

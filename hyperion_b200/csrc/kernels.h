@@ -78,6 +78,11 @@ size_t qmv_packed_bytes(int K, int N);
 void launch_qmv_pack(const uint32_t* w, const bf16* s, const bf16* b, int K, int N, void* packed,
                      cudaStream_t stream);
 void launch_qmv_packed(const QmvParams& p, cudaStream_t stream, bool pdl = false);
+// The MLX layout of a packed matrix's N rows (the inverse of launch_qmv_pack).
+void launch_qmv_unpack(const void* packed, int K, int N, uint32_t* w, bf16* s, bf16* b, cudaStream_t stream);
+// Embedding gather (+ dequantise, x scale) of L token rows from a packed [N, H] table.
+void launch_embed_packed(const uint32_t* ids, int L, const void* packed, int H, int N, bf16 scale, bf16* out,
+                         cudaStream_t stream);
 
 // Batched decode qmv (qmv_batched.cu): B <= kMaxDecodeBatch sequences over the packed
 // layout, one weight stream for the whole batch. x16 is the activation batch converted by

@@ -6,6 +6,7 @@
 #include <cmath>
 #include <cstddef>
 #include <cstdio>
+#include <cstring>
 #include <exception>
 #include <string>
 
@@ -109,6 +110,32 @@ HypStatus hyb_qmv_pack(const uint32_t* w, const void* scales, const void* biases
     return run([&] {
         hyb::launch_qmv_pack(w, static_cast<const hyb::bf16*>(scales), static_cast<const hyb::bf16*>(biases),
                              static_cast<int>(K), static_cast<int>(N), packed, as_stream(stream));
+    });
+}
+
+HypStatus hyb_qmv_unpack(const void* packed, int64_t K, int64_t N, uint32_t* w, void* scales, void* biases,
+                         void* stream) {
+    if (!w || !scales || !biases || !packed) return hyb::abi_fail(HYP_STATUS_INVALID_ARGUMENT, "null pointer argument");
+    if (K <= 0 || K % 64 != 0 || N <= 0 || K > (1 << 20) || N > (1 << 30))
+        return hyb::abi_fail(HYP_STATUS_INVALID_ARGUMENT, "qmv_unpack: bad shape");
+    if (!aligned16(w) || !aligned16(packed)) return hyb::abi_fail(HYP_STATUS_INVALID_ARGUMENT, "qmv_unpack: w and packed must be 16-byte aligned");
+    return run([&] {
+        hyb::launch_qmv_unpack(packed, static_cast<int>(K), static_cast<int>(N), w, static_cast<hyb::bf16*>(scales),
+                               static_cast<hyb::bf16*>(biases), as_stream(stream));
+    });
+}
+
+HypStatus hyb_embed_packed(const uint32_t* ids, int64_t L, const void* packed, int64_t H, int64_t N,
+                           uint16_t embed_scale_bf16, void* out, void* stream) {
+    if (!ids || !packed || !out) return hyb::abi_fail(HYP_STATUS_INVALID_ARGUMENT, "null pointer argument");
+    if (L <= 0 || L > 65535 || H <= 0 || H % 64 != 0 || H > (1 << 20) || N <= 0 || N > (1 << 30))
+        return hyb::abi_fail(HYP_STATUS_INVALID_ARGUMENT, "embed_packed: bad shape");
+    if (!aligned16(packed) || !aligned16(out)) return hyb::abi_fail(HYP_STATUS_INVALID_ARGUMENT, "embed_packed: packed and out must be 16-byte aligned");
+    hyb::bf16 sc;
+    std::memcpy(&sc, &embed_scale_bf16, 2);
+    return run([&] {
+        hyb::launch_embed_packed(ids, static_cast<int>(L), packed, static_cast<int>(H), static_cast<int>(N), sc,
+                                 static_cast<hyb::bf16*>(out), as_stream(stream));
     });
 }
 

@@ -566,6 +566,92 @@ __global__ void qmv_pack_kernel(const uint32_t* __restrict__ w, const bf16* __re
     }
 }
 
+// The inverse of qmv_pack_kernel: the MLX layout (codes [N, K/8] u32, scales and biases
+// [N, K/64] bf16) of the rows a packed matrix holds; same thread mapping as the pack.
+__global__ void qmv_unpack_kernel(const unsigned char* __restrict__ in, int K, int N, uint32_t* __restrict__ w,
+                                  bf16* __restrict__ s, bf16* __restrict__ b) {
+    const PackGeo pg = pack_geo(K, N);
+    const long long total = static_cast<long long>(pg.nrb) * pg.nunits * 32;
+    for (long long idx = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; idx < total;
+         idx += static_cast<long long>(gridDim.x) * blockDim.x) {
+        const int L = static_cast<int>(idx % 32);
+        const long long ru = idx / 32;
+        const int unit = static_cast<int>(ru % pg.nunits);
+        const int rb = static_cast<int>(ru / pg.nunits);
+        const int gc = (unit == pg.nunits - 1) ? pg.gc_last : 8;
+        const int tv = (gc + 1) / 2;
+        const int nv = 8 * tv;
+        const int g = L / 4, t = L % 4;
+        if (t >= tv) continue;
+        const int rank = g * tv + t;
+        const unsigned char* item = in + rb * pg.rb_bytes + static_cast<long long>(unit) * kItemMax;
+        const int gA = unit * 8 + 2 * t, gB = gA + 1;
+        const int K8 = K / 8, G = pg.G;
+        for (int c = 0; c < 8; ++c) {
+            const int h = c / 4, q = c % 4;
+            const int row = rb * 16 + g + 8 * h;
+            const int grp = (q < 2) ? gA : gB;
+            if (row < N && grp < G)
+                *reinterpret_cast<uint4*>(w + static_cast<size_t>(row) * K8 + grp * 8 + 4 * (q & 1)) =
+                    *reinterpret_cast<const uint4*>(item + (c * nv + rank) * 16);
+        }
+        const uint4 rv = *reinterpret_cast<const uint4*>(item + (8 * nv + rank) * 16);
+        const uint16_t* rec = reinterpret_cast<const uint16_t*>(&rv);
+        for (int h = 0; h < 2; ++h) {
+            const int row = rb * 16 + g + 8 * h;
+            if (row >= N) continue;
+            uint16_t* sr = reinterpret_cast<uint16_t*>(s) + static_cast<size_t>(row) * G;
+            uint16_t* br = reinterpret_cast<uint16_t*>(b) + static_cast<size_t>(row) * G;
+            if (gA < G) {
+                sr[gA] = rec[2 * h + 0];
+                br[gA] = rec[4 + 2 * h + 0];
+            }
+            if (gB < G) {
+                sr[gB] = rec[2 * h + 1];
+                br[gB] = rec[4 + 2 * h + 1];
+            }
+        }
+    }
+}
+
+// Embedding rows gathered from a packed table (the tied lm_head): row id's group gi lives in
+// 16-row block id / 16, unit gi / 8, lane (g = id % 8, t = (gi % 8) / 2) as chunks
+// 4 h + 2 (gi % 2) and + 1 (h = (id % 16) / 8) and record entries 2 h + gi % 2 (scale),
+// 4 + 2 h + gi % 2 (bias). Dequantised and scaled exactly as embed_kernel does.
+__global__ void embed_packed_kernel(const uint32_t* __restrict__ ids, const unsigned char* __restrict__ packed, int H,
+                                    int N, bf16 scale, bf16* __restrict__ out) {
+    const int l = blockIdx.y;
+    const uint32_t id = ids[l];
+    const PackGeo pg = pack_geo(H, N);
+    const float sc = bf2f(scale);
+    const int rb = static_cast<int>(id / 16), rr = static_cast<int>(id % 16), g = rr % 8, h = rr / 8;
+    for (int gi = blockIdx.x * blockDim.x + threadIdx.x; gi < pg.G; gi += gridDim.x * blockDim.x) {
+        const int unit = gi / 8, t = (gi % 8) / 2, which = gi % 2;
+        const int gc = (unit == pg.nunits - 1) ? pg.gc_last : 8;
+        const int tv = (gc + 1) / 2, nv = 8 * tv, rank = g * tv + t;
+        const unsigned char* item = packed + rb * pg.rb_bytes + static_cast<long long>(unit) * kItemMax;
+        const uint4 rv = *reinterpret_cast<const uint4*>(item + (8 * nv + rank) * 16);
+        const uint16_t* rec = reinterpret_cast<const uint16_t*>(&rv);
+        const float sv = __uint_as_float(static_cast<uint32_t>(rec[2 * h + which]) << 16);
+        const float bv = __uint_as_float(static_cast<uint32_t>(rec[4 + 2 * h + which]) << 16);
+        for (int half = 0; half < 2; ++half) {
+            const int c = 4 * h + 2 * which + half;
+            const uint4 wv = *reinterpret_cast<const uint4*>(item + (c * nv + rank) * 16);
+            const uint32_t words[4] = {wv.x, wv.y, wv.z, wv.w};
+            for (int k = 0; k < 4; ++k) {
+                bf16 o[8];
+#pragma unroll
+                for (int i = 0; i < 8; ++i) {
+                    const float deq = rbf(fmaf(sv, static_cast<float>((words[k] >> (4 * i)) & 0xF), bv));
+                    o[i] = f2bf(deq * sc);
+                }
+                *reinterpret_cast<uint4*>(out + static_cast<size_t>(l) * H + gi * 64 + (4 * half + k) * 8) =
+                    *reinterpret_cast<uint4*>(o);
+            }
+        }
+    }
+}
+
 size_t packed_smem_bytes(int K, bool prologue) {
     const int G = K / 64;
     size_t b = static_cast<size_t>(kWarps) * kStages * kItemMax + kWarps * kStages * 8 +
@@ -590,6 +676,24 @@ void launch_qmv_pack(const uint32_t* w, const bf16* s, const bf16* b, int K, int
     const int grid = static_cast<int>(std::min<long long>((total + 255) / 256, 65535));
     qmv_pack_kernel<<<grid, 256, 0, stream>>>(w, s, b, K, N, static_cast<unsigned char*>(packed));
     HYB_LAUNCH_CHECK("qmv_pack_kernel");
+}
+
+void launch_qmv_unpack(const void* packed, int K, int N, uint32_t* w, bf16* s, bf16* b, cudaStream_t stream) {
+    if (K <= 0 || K % 64 != 0 || N <= 0) throw ArgError("qmv_unpack: K must be a positive multiple of 64");
+    const PackGeo pg = pack_geo(K, N);
+    const long long total = static_cast<long long>(pg.nrb) * pg.nunits * 32;
+    const int grid = static_cast<int>(std::min<long long>((total + 255) / 256, 65535));
+    qmv_unpack_kernel<<<grid, 256, 0, stream>>>(static_cast<const unsigned char*>(packed), K, N, w, s, b);
+    HYB_LAUNCH_CHECK("qmv_unpack_kernel");
+}
+
+void launch_embed_packed(const uint32_t* ids, int L, const void* packed, int H, int N, bf16 scale, bf16* out,
+                         cudaStream_t stream) {
+    if (L <= 0) return;
+    if (H % 64 != 0) throw ArgError("embed: hidden size must be a multiple of 64");
+    dim3 grid((H / 64 + 63) / 64, L);
+    embed_packed_kernel<<<grid, 64, 0, stream>>>(ids, static_cast<const unsigned char*>(packed), H, N, scale, out);
+    HYB_LAUNCH_CHECK("embed_packed_kernel");
 }
 
 namespace {

@@ -55,6 +55,23 @@ def qmv_pack(w, scales, biases, stream=None) -> torch.Tensor:
     return out
 
 
+def qmv_unpack(packed, K, N, stream=None):
+    """The MLX layout (w [N, K/8] uint32, scales/biases [N, K/64] bf16) of a packed matrix."""
+    w = torch.empty((N, K // 8), dtype=torch.int32, device=packed.device)
+    s = torch.empty((N, K // 64), dtype=torch.bfloat16, device=packed.device)
+    b = torch.empty((N, K // 64), dtype=torch.bfloat16, device=packed.device)
+    check(lib().hyb_qmv_unpack(_p(packed), K, N, _p(w), _p(s), _p(b), _stream(stream)))
+    return w, s, b
+
+
+def embed_packed(ids, packed, H, N, embed_scale_bits, stream=None):
+    """Embedding rows of a packed [N, H] table (dequantised, x embed scale): [L, H] bf16."""
+    L = ids.numel()
+    out = torch.empty((L, H), dtype=torch.bfloat16, device=packed.device)
+    check(lib().hyb_embed_packed(_p(ids), L, _p(packed), H, N, embed_scale_bits, _p(out), _stream(stream)))
+    return out
+
+
 def qmv_packed(x, packed, K, N, prologue=0, epilogue=0, norm_w=None, resid=None, post_w=None, scalar=None,
                h_out=None, eps=1e-6, out=None, stream=None):
     """Batch-1 qmv over packed weights (TMA-streamed kernel), same options as qmv_fused."""

@@ -86,10 +86,20 @@ HypStatus hyb_qmv_fused(const void* x, const uint32_t* w, const void* scales, co
  *   16-byte aligned). The MLX tensors may be freed afterwards.
  *   hyb_qmv_packed: the batch-1 qmv (with the hyb_qmv_fused prologue/epilogue
  *   options) reading the packed form; same results as hyb_qmv_fused.
+ *   hyb_qmv_unpack: the inverse of hyb_qmv_pack (the engine's prefill GEMM
+ *   re-derives each projection's MLX layout with it: the packed form is the only
+ *   resident copy of the weights).
+ *   hyb_embed_packed: embedding rows ids[0..L) of a packed [N, H] table,
+ *   dequantised to bf16 and multiplied by embed_scale (bf16 bits), written to
+ *   out [L][H]; ids must be < N (not checked on the device).
  */
 size_t hyb_qmv_packed_bytes(int64_t K, int64_t N);
 HypStatus hyb_qmv_pack(const uint32_t* w, const void* scales, const void* biases, int64_t K,
                        int64_t N, void* packed, void* stream);
+HypStatus hyb_qmv_unpack(const void* packed, int64_t K, int64_t N, uint32_t* w, void* scales,
+                         void* biases, void* stream);
+HypStatus hyb_embed_packed(const uint32_t* ids, int64_t L, const void* packed, int64_t H, int64_t N,
+                           uint16_t embed_scale_bf16, void* out, void* stream);
 HypStatus hyb_qmv_packed(const void* x, const void* packed, void* y, int64_t K, int64_t N,
                          int32_t prologue, int32_t epilogue, const void* norm_w,
                          const void* resid, const void* post_w, const void* scalar,
@@ -346,6 +356,16 @@ HypStatus hyb_test_arm_post_append_fault(void);
  * state and its cursor untouched. 0 (the default) checks device free memory only.
  */
 HypStatus hyb_model_set_memory_budget(HypModel model, uint64_t bytes);
+
+/*
+ * Weight memory of a loaded model (no reference counterpart: the reference holds
+ * MLX arrays). resident = device bytes of the weights this rank holds: every
+ * quantised matrix once, in the packed decode layout, plus norms and RoPE tables.
+ * algorithmic = codes + scales + biases of those matrices (N*K/2 + N*K/16 bytes
+ * each). scratch = the transient MLX-layout buffer the tensor-core prefill GEMM
+ * re-derives one projection (or one lm_head slice) into. Any pointer may be NULL.
+ */
+HypStatus hyb_model_weight_bytes(HypModel model, uint64_t* resident, uint64_t* algorithmic, uint64_t* scratch);
 
 
 #ifdef __cplusplus

@@ -58,6 +58,14 @@ def test_decode_batch_matches_single(built_lib, name, geo, lens, steps):
     assert dlog.max() <= 2 ** -6, dlog.max()
 
 
+def test_decode_batch_above_qmv_reach_262k_vocab(built_lib):
+    """20 sequences take the tcgen05 GEMM path, whose lm_head runs over the 262144-row
+    vocabulary in slices unpacked in turn from the packed table (a ragged last slice)."""
+    agree, dlog = _run(config3(2), 33, [9 + 5 * i for i in range(20)], 2)
+    assert agree.mean() >= 0.97, agree
+    assert dlog.max() <= 2 ** -6, dlog.max()
+
+
 def test_decode_batch_64(built_lib):
     """The largest batch (8 MMA column groups), sequences at 64 different positions."""
     geo = config0()

@@ -38,6 +38,24 @@ def test_canary_on_gpu(built_lib):
     assert info.recommended_working_set_bytes > 100 * 2 ** 30
 
 
+@pytest.mark.parametrize("geo_name", ["cfg0", "cfg3_2layers"])
+def test_weights_resident_once(built_lib, geo_name):
+    """Every quantised matrix is held once, in the packed layout: resident weight bytes are
+    the algorithmic size (codes + scales + biases) plus norms, and the MLX-layout scratch the
+    prefill GEMM unpacks into is one projection (or one lm_head slice)."""
+    geo = {"cfg0": config0(), "cfg3_2layers": config3(2)}[geo_name]
+    eng = hb.Engine(geo, synthetic_seed=5)
+    wb = eng.weight_bytes()
+    H, V = geo.hidden_size, geo.vocab_size
+    assert wb["algorithmic"] >= V * H * 9 // 16
+    small = geo.num_hidden_layers * (6 * H + 2 * 512 + 2) * 2 + 2 * H + 4 * 1024  # norms, RoPE
+    pad = (4 * geo.num_hidden_layers + 1) * 15 * max(H, geo.intermediate_size) * 9 // 16  # 16-row blocks
+    assert wb["algorithmic"] <= wb["resident"] <= wb["algorithmic"] + pad + small, wb
+    assert wb["scratch"] <= 0.6 * wb["algorithmic"], wb
+    if geo_name == "cfg3_2layers":
+        assert wb["scratch"] <= 80 * 2 ** 20, wb  # one 30720 x 3840 gate/up matrix
+
+
 def _teacher_forced(eng, orc, prompt, steps):
     """Run the engine greedily; the oracle consumes the engine's token stream.
     Returns (token agreement per step, logits rel-L2 per step incl. prefill)."""

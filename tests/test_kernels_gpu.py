@@ -361,3 +361,40 @@ def test_sdpa_decode_fused_rejects_oversized_context(built_lib):
     inv = torch.ones(hd // 2, dtype=torch.float32, device="cuda")
     with pytest.raises(HypError, match="too many keys"):
         ops.sdpa_decode_fused(qkv, False, nw, nw, inv, kc, vc, n - 1, n, H)
+
+
+@pytest.mark.parametrize("K,N", [(64, 8), (576, 33), (832, 50), (3840, 100008), (5376, 17)])
+def test_qmv_unpack_inverts_pack(built_lib, K, N):
+    """hyb_qmv_unpack(hyb_qmv_pack(W)) == W bit for bit: ragged last row block, odd and even
+    group counts in the last 512-code unit (the engine's prefill GEMM reads this)."""
+    from hyperion_b200 import ops
+    import torch
+    rng = np.random.default_rng(K + 7 * N)
+    w, s, b = random_q4(rng, N, K)
+    packed = ops.qmv_pack(dev(w), dev(s), dev(b))
+    w2, s2, b2 = ops.qmv_unpack(packed, K, N)
+    torch.cuda.synchronize()
+    assert np.array_equal(host(w2).view(np.uint32), w)
+    assert np.array_equal(host(s2), s) and np.array_equal(host(b2), b)
+
+
+@pytest.mark.parametrize("H,N", [(256, 1024), (832, 999), (3840, 4099)])
+def test_embed_packed_matches_oracle(built_lib, H, N):
+    """The embedding gather from the packed table against the oracle's dequantise + scale."""
+    from hyperion_b200 import ops
+    from oracle import gemma_oracle as go
+    import torch
+    rng = np.random.default_rng(H + N)
+    w, s, b = random_q4(rng, N, H)
+    ids = np.concatenate([[0, N - 1, N - 16 if N > 16 else 0], rng.integers(0, N, 61)]).astype(np.uint32)
+    scale = f32_to_bf16_bits(np.array([np.sqrt(np.float32(H))], dtype=np.float32))[0]
+    packed = ops.qmv_pack(dev(w), dev(s), dev(b))
+    got = host(ops.embed_packed(dev(ids), packed, H, N, int(scale)))
+    torch.cuda.synchronize()
+    codes = np.zeros((ids.size, H), dtype=np.float32)
+    for i in range(8):
+        codes[:, i::8] = ((w[ids] >> np.uint32(4 * i)) & np.uint32(0xF)).astype(np.float32)
+    deq = go.bf((codes.reshape(ids.size, -1, 64) * go.fl(s[ids])[:, :, None]
+                 + go.fl(b[ids])[:, :, None]).reshape(ids.size, -1))
+    want = go.bf(go.fl(deq) * go.fl(np.uint16(scale)))
+    assert np.array_equal(got, want)
