@@ -704,12 +704,12 @@ HypStatus hyb_kv_copy_layer(HypModel model, HypKvState kv, uint32_t layer, int32
         size_t row;
         if (g.kinds[layer] == hyb::LayerKind::Sliding) {
             const auto& c = kv->kv->local[li];
-            src = which == 0 ? c.k.p : c.v.p;
+            src = which == 0 ? c.k : c.v;
             cap = c.cap;
             row = static_cast<size_t>(c.nkv) * c.hd;
         } else {
             const auto& c = kv->kv->global[gi];
-            src = which == 0 ? c.k.p : c.v.p;
+            src = which == 0 ? c.k : c.v;
             cap = c.capacity;
             row = static_cast<size_t>(c.nkv) * c.hd;
         }

@@ -607,26 +607,33 @@ void Model::load_dir(const Geometry& g, const std::string& dir) {
 
 std::unique_ptr<KvState> Model::new_kv() const {
     auto kv = std::make_unique<KvState>();
-    for (uint32_t i = 0; i < geo_.n_layers; ++i) {
-        const LayerW& L = layers_[i];
+    const uint32_t cap = geo_.window + 8;  // window + gamma_max (kv_cache.h:16, kv.cc:233-235)
+    size_t total = 0;
+    for (const auto& L : layers_)
+        if (L.kind == LayerKind::Sliding) total += 2 * static_cast<size_t>(cap) * L.nkv * L.hd;
+    if (total) {
+        kv->ring_arena.reset(total);
+        HYB_CUDA(cudaMemsetAsync(kv->ring_arena.p, 0, total * 2, stream_));
+    }
+    size_t at = 0;
+    for (const auto& L : layers_) {
         if (L.kind == LayerKind::Sliding) {
             LocalCache c;
             c.nkv = L.nkv;
             c.hd = L.hd;
-            c.cap = geo_.window + 8;  // window + gamma_max (kv_cache.h:16, kv.cc:233-235)
+            c.cap = cap;
             const size_t n = static_cast<size_t>(c.cap) * c.nkv * c.hd;
-            c.k.reset(n);
-            c.v.reset(n);
-            HYB_CUDA(cudaMemsetAsync(c.k.p, 0, n * 2, stream_));
-            HYB_CUDA(cudaMemsetAsync(c.v.p, 0, n * 2, stream_));
-            encode_kv_tensor_map(&c.tk, c.k.p, static_cast<int>(c.cap), c.nkv, c.hd);
-            encode_kv_tensor_map(&c.tv, c.v.p, static_cast<int>(c.cap), c.nkv, c.hd);
-            kv->local.push_back(std::move(c));
+            c.k = kv->ring_arena.p + at;
+            c.v = c.k + n;
+            at += 2 * n;
+            encode_kv_tensor_map(&c.tk, c.k, static_cast<int>(c.cap), c.nkv, c.hd);
+            encode_kv_tensor_map(&c.tv, c.v, static_cast<int>(c.cap), c.nkv, c.hd);
+            kv->local.push_back(c);
         } else {
             GlobalCache c;
             c.nkv = L.nkv;
             c.hd = L.hd;
-            kv->global.push_back(std::move(c));
+            kv->global.push_back(c);
         }
     }
     HYB_CUDA(cudaStreamSynchronize(stream_));
@@ -635,37 +642,31 @@ std::unique_ptr<KvState> Model::new_kv() const {
 
 std::unique_ptr<KvState> Model::clone_kv(const KvState& src, uint32_t last_token) const {
     auto kv = std::make_unique<KvState>();
-    for (const auto& s : src.local) {
-        LocalCache c;
-        c.nkv = s.nkv;
-        c.hd = s.hd;
-        c.cap = s.cap;
-        c.committed = s.committed;
-        const size_t n = static_cast<size_t>(c.cap) * c.nkv * c.hd;
-        c.k.reset(n);
-        c.v.reset(n);
-        HYB_CUDA(cudaMemcpyAsync(c.k.p, s.k.p, n * 2, cudaMemcpyDeviceToDevice, stream_));
-        HYB_CUDA(cudaMemcpyAsync(c.v.p, s.v.p, n * 2, cudaMemcpyDeviceToDevice, stream_));
-        encode_kv_tensor_map(&c.tk, c.k.p, static_cast<int>(c.cap), c.nkv, c.hd);
-        encode_kv_tensor_map(&c.tv, c.v.p, static_cast<int>(c.cap), c.nkv, c.hd);
-        kv->local.push_back(std::move(c));
-    }
-    for (const auto& s : src.global) {
-        GlobalCache c;
-        c.nkv = s.nkv;
-        c.hd = s.hd;
-        c.capacity = s.capacity;
-        c.committed = s.committed;
-        if (c.capacity > 0) {
-            const size_t n = static_cast<size_t>(c.capacity) * c.nkv * c.hd;
-            c.k.reset(n);
-            c.v.reset(n);
-            HYB_CUDA(cudaMemcpyAsync(c.k.p, s.k.p, n * 2, cudaMemcpyDeviceToDevice, stream_));
-            HYB_CUDA(cudaMemcpyAsync(c.v.p, s.v.p, n * 2, cudaMemcpyDeviceToDevice, stream_));
-            encode_kv_tensor_map(&c.tk, c.k.p, static_cast<int>(c.capacity), c.nkv, c.hd);
-            encode_kv_tensor_map(&c.tv, c.v.p, static_cast<int>(c.capacity), c.nkv, c.hd);
+    kv->local = src.local;
+    kv->global = src.global;
+    // the same layout in new arenas: every pointer moves by the arenas' distance
+    if (src.ring_arena.n) {
+        kv->ring_arena.reset(src.ring_arena.n);
+        HYB_CUDA(cudaMemcpyAsync(kv->ring_arena.p, src.ring_arena.p, src.ring_arena.n * 2, cudaMemcpyDeviceToDevice,
+                                 stream_));
+        for (auto& c : kv->local) {
+            c.k = kv->ring_arena.p + (c.k - src.ring_arena.p);
+            c.v = kv->ring_arena.p + (c.v - src.ring_arena.p);
+            encode_kv_tensor_map(&c.tk, c.k, static_cast<int>(c.cap), c.nkv, c.hd);
+            encode_kv_tensor_map(&c.tv, c.v, static_cast<int>(c.cap), c.nkv, c.hd);
         }
-        kv->global.push_back(std::move(c));
+    }
+    if (src.global_arena.n) {
+        kv->global_arena.reset(src.global_arena.n);
+        HYB_CUDA(cudaMemcpyAsync(kv->global_arena.p, src.global_arena.p, src.global_arena.n * 2,
+                                 cudaMemcpyDeviceToDevice, stream_));
+        for (auto& c : kv->global) {
+            if (c.capacity == 0) continue;
+            c.k = kv->global_arena.p + (c.k - src.global_arena.p);
+            c.v = kv->global_arena.p + (c.v - src.global_arena.p);
+            encode_kv_tensor_map(&c.tk, c.k, static_cast<int>(c.capacity), c.nkv, c.hd);
+            encode_kv_tensor_map(&c.tv, c.v, static_cast<int>(c.capacity), c.nkv, c.hd);
+        }
     }
     kv->offset = src.offset;
     kv->last_token = last_token;
@@ -673,44 +674,62 @@ std::unique_ptr<KvState> Model::clone_kv(const KvState& src, uint32_t last_token
     return kv;
 }
 
-void Model::reserve(KvState& kv, uint32_t n_tokens) const {
-    for (auto& c : kv.global) {
-        const uint64_t need_tokens = static_cast<uint64_t>(c.committed) + n_tokens;
-        const uint64_t need = (need_tokens + 255) / 256 * 256;
+bool Model::grow_globals(KvState& kv, uint32_t n_tokens, DevPtr<bf16>* old) const {
+    std::vector<uint32_t> caps(kv.global.size());
+    bool grows = false;
+    size_t total = 0;
+    for (size_t i = 0; i < kv.global.size(); ++i) {
+        const GlobalCache& c = kv.global[i];
+        const uint64_t need = (static_cast<uint64_t>(c.committed) + n_tokens + 255) / 256 * 256;
         if (need > 0xFFFFFFFFull) throw std::overflow_error("KV operation exceeds representable cache dimensions");
-        if (need <= c.capacity) continue;
-        const size_t row = static_cast<size_t>(c.nkv) * c.hd;
-        DevPtr<bf16> nk(need * row), nv(need * row);
-        HYB_CUDA(cudaMemsetAsync(nk.p, 0, need * row * 2, stream_));
-        HYB_CUDA(cudaMemsetAsync(nv.p, 0, need * row * 2, stream_));
-        if (c.capacity > 0) {
-            HYB_CUDA(cudaMemcpyAsync(nk.p, c.k.p, static_cast<size_t>(c.capacity) * row * 2, cudaMemcpyDeviceToDevice, stream_));
-            HYB_CUDA(cudaMemcpyAsync(nv.p, c.v.p, static_cast<size_t>(c.capacity) * row * 2, cudaMemcpyDeviceToDevice, stream_));
-        }
-        HYB_CUDA(cudaStreamSynchronize(stream_));
-        c.k = std::move(nk);
-        c.v = std::move(nv);
-        c.capacity = static_cast<uint32_t>(need);
-        encode_kv_tensor_map(&c.tk, c.k.p, static_cast<int>(c.capacity), c.nkv, c.hd);
-        encode_kv_tensor_map(&c.tv, c.v.p, static_cast<int>(c.capacity), c.nkv, c.hd);
+        if (need > c.capacity) grows = true;
+        caps[i] = static_cast<uint32_t>(std::max<uint64_t>(need, c.capacity));
+        total += 2 * static_cast<size_t>(caps[i]) * c.nkv * c.hd;
     }
+    if (!grows) return false;
+    DevPtr<bf16> arena(total);
+    HYB_CUDA(cudaMemsetAsync(arena.p, 0, total * 2, stream_));
+    size_t at = 0;
+    for (size_t i = 0; i < kv.global.size(); ++i) {
+        GlobalCache& c = kv.global[i];
+        const size_t row = static_cast<size_t>(c.nkv) * c.hd;
+        bf16* nk = arena.p + at;
+        bf16* nv = nk + caps[i] * row;
+        at += 2 * caps[i] * row;
+        if (c.capacity > 0) {
+            HYB_CUDA(cudaMemcpyAsync(nk, c.k, c.capacity * row * 2, cudaMemcpyDeviceToDevice, stream_));
+            HYB_CUDA(cudaMemcpyAsync(nv, c.v, c.capacity * row * 2, cudaMemcpyDeviceToDevice, stream_));
+        }
+        c.k = nk;
+        c.v = nv;
+        c.capacity = caps[i];
+        encode_kv_tensor_map(&c.tk, c.k, static_cast<int>(c.capacity), c.nkv, c.hd);
+        encode_kv_tensor_map(&c.tv, c.v, static_cast<int>(c.capacity), c.nkv, c.hd);
+    }
+    HYB_CUDA(cudaStreamSynchronize(stream_));
+    *old = std::move(kv.global_arena);
+    kv.global_arena = std::move(arena);
+    return true;
+}
+
+void Model::reserve(KvState& kv, uint32_t n_tokens) const {
+    DevPtr<bf16> old;
+    grow_globals(kv, n_tokens, &old);  // the old arena is freed here, after the copies
 }
 
 bool Model::predict_call_bytes(const KvState& kv, uint32_t n_tokens, uint64_t* bytes) const {
-    uint64_t b = 0;
+    uint64_t b = 0, arena = 0;
     bool grows = false;
     for (const auto& c : kv.global) {
         const uint64_t need = (static_cast<uint64_t>(c.committed) + n_tokens + 255) / 256 * 256;
         if (need > 0xFFFFFFFFull) return false;
-        if (need > c.capacity) {
-            b += need * c.nkv * c.hd * 2 * 2;
-            grows = true;
-        }
+        if (need > c.capacity) grows = true;
+        arena += std::max<uint64_t>(need, c.capacity) * c.nkv * c.hd * 2 * 2;
     }
-    for (const auto& c : kv.local) {
+    if (grows) b += arena;  // the staged arena holds every global cache
+    for (const auto& c : kv.local)
         if (static_cast<uint64_t>(c.committed) + n_tokens > 0xFFFFFFFFull) return false;
-        if (grows && n_tokens > static_cast<uint32_t>(kSpecMax)) b += static_cast<uint64_t>(c.cap) * c.nkv * c.hd * 2 * 2;
-    }
+    if (grows && n_tokens > static_cast<uint32_t>(kSpecMax) && kv.offset > 0) b += kv.ring_arena.n * 2;
     // workspace the call would newly allocate (ensure_workspace): a prefill runs chunks of
     // up to 2048 rows, decode one row per forward
     const Geometry& g = geo_;
@@ -745,49 +764,22 @@ KvTransaction Model::begin_kv_transaction(KvState& kv, uint32_t n_tokens) const 
     t.offset = kv.offset;
     t.last_token = kv.last_token;
     for (const auto& c : kv.local) t.local_committed.push_back(c.committed);
-    for (const auto& c : kv.global) t.global_committed.push_back(c.committed);
-    if (n_tokens > static_cast<uint32_t>(kSpecMax)) {
-        for (size_t i = 0; i < kv.local.size(); ++i) {
-            const LocalCache& c = kv.local[i];
-            const size_t n = static_cast<size_t>(c.cap) * c.nkv * c.hd;
-            KvTransaction::Ring r;
-            r.index = i;
-            r.k.reset(n);
-            r.v.reset(n);
-            HYB_CUDA(cudaMemcpyAsync(r.k.p, c.k.p, n * 2, cudaMemcpyDeviceToDevice, stream_));
-            HYB_CUDA(cudaMemcpyAsync(r.v.p, c.v.p, n * 2, cudaMemcpyDeviceToDevice, stream_));
-            t.rings.push_back(std::move(r));
-        }
+    for (const auto& c : kv.global) {
+        t.global_committed.push_back(c.committed);
+        KvTransaction::Global gk;
+        gk.k = c.k;
+        gk.v = c.v;
+        gk.capacity = c.capacity;
+        gk.tk = c.tk;
+        gk.tv = c.tv;
+        t.globals.push_back(gk);
     }
-    for (size_t i = 0; i < kv.global.size(); ++i) {
-        GlobalCache& c = kv.global[i];
-        const uint64_t need = (static_cast<uint64_t>(c.committed) + n_tokens + 255) / 256 * 256;
-        if (need <= c.capacity) continue;
-        const size_t row = static_cast<size_t>(c.nkv) * c.hd;
-        DevPtr<bf16> nk(need * row), nv(need * row);
-        HYB_CUDA(cudaMemsetAsync(nk.p, 0, need * row * 2, stream_));
-        HYB_CUDA(cudaMemsetAsync(nv.p, 0, need * row * 2, stream_));
-        if (c.capacity > 0) {
-            HYB_CUDA(cudaMemcpyAsync(nk.p, c.k.p, static_cast<size_t>(c.capacity) * row * 2, cudaMemcpyDeviceToDevice,
-                                     stream_));
-            HYB_CUDA(cudaMemcpyAsync(nv.p, c.v.p, static_cast<size_t>(c.capacity) * row * 2, cudaMemcpyDeviceToDevice,
-                                     stream_));
-        }
-        KvTransaction::Global kept;
-        kept.index = i;
-        kept.k = std::move(c.k);
-        kept.v = std::move(c.v);
-        kept.capacity = c.capacity;
-        kept.tk = c.tk;
-        kept.tv = c.tv;
-        t.globals.push_back(std::move(kept));
-        c.k = std::move(nk);
-        c.v = std::move(nv);
-        c.capacity = static_cast<uint32_t>(need);
-        encode_kv_tensor_map(&c.tk, c.k.p, static_cast<int>(c.capacity), c.nkv, c.hd);
-        encode_kv_tensor_map(&c.tv, c.v.p, static_cast<int>(c.capacity), c.nkv, c.hd);
+    if (n_tokens > static_cast<uint32_t>(kSpecMax) && kv.offset > 0 && kv.ring_arena.n) {
+        t.ring_backup.reset(kv.ring_arena.n);
+        HYB_CUDA(cudaMemcpyAsync(t.ring_backup.p, kv.ring_arena.p, kv.ring_arena.n * 2, cudaMemcpyDeviceToDevice,
+                                 stream_));
     }
-    HYB_CUDA(cudaStreamSynchronize(stream_));
+    grow_globals(kv, n_tokens, &t.global_arena);  // synchronises the stream
     return t;
 }
 
@@ -800,20 +792,18 @@ void Model::rollback_kv_transaction(KvState& kv, KvTransaction& t) const {
         kv.poisoned = true;  // the device is in an error state: the cache contents are unknown
         return;
     }
-    for (auto& g : t.globals) {
-        GlobalCache& c = kv.global[g.index];
-        c.k = std::move(g.k);
-        c.v = std::move(g.v);
-        c.capacity = g.capacity;
-        c.tk = g.tk;
-        c.tv = g.tv;
+    for (size_t i = 0; i < t.globals.size(); ++i) {
+        GlobalCache& c = kv.global[i];
+        c.k = t.globals[i].k;
+        c.v = t.globals[i].v;
+        c.capacity = t.globals[i].capacity;
+        c.tk = t.globals[i].tk;
+        c.tv = t.globals[i].tv;
     }
-    for (auto& r : t.rings) {
-        LocalCache& c = kv.local[r.index];
-        const size_t n = static_cast<size_t>(c.cap) * c.nkv * c.hd;
-        HYB_CUDA(cudaMemcpyAsync(c.k.p, r.k.p, n * 2, cudaMemcpyDeviceToDevice, stream_));
-        HYB_CUDA(cudaMemcpyAsync(c.v.p, r.v.p, n * 2, cudaMemcpyDeviceToDevice, stream_));
-    }
+    kv.global_arena = std::move(t.global_arena);
+    if (t.ring_backup.n)
+        HYB_CUDA(cudaMemcpyAsync(kv.ring_arena.p, t.ring_backup.p, t.ring_backup.n * 2, cudaMemcpyDeviceToDevice,
+                                 stream_));
     for (size_t i = 0; i < kv.local.size(); ++i) kv.local[i].committed = t.local_committed[i];
     for (size_t i = 0; i < kv.global.size(); ++i) kv.global[i].committed = t.global_committed[i];
     kv.offset = t.offset;
@@ -947,15 +937,15 @@ void Model::forward_chunk(KvState& kv, int L, uint32_t offset) {
             // (forward.cc:444-457); the chunk's own K/V follow it contiguously
             const uint32_t pre = offset > 0 ? std::min(g.window, offset) : 0;
             if (pre > 0) {
-                launch_gather_ring(c.k.p, static_cast<int>(c.cap), static_cast<int>(offset - pre), static_cast<int>(pre),
+                launch_gather_ring(c.k, static_cast<int>(c.cap), static_cast<int>(offset - pre), static_cast<int>(pre),
                                    static_cast<int>(row), ws_.kbuf.p, st);
-                launch_gather_ring(c.v.p, static_cast<int>(c.cap), static_cast<int>(offset - pre), static_cast<int>(pre),
+                launch_gather_ring(c.v, static_cast<int>(c.cap), static_cast<int>(offset - pre), static_cast<int>(pre),
                                    static_cast<int>(row), ws_.vbuf.p, st);
             }
             qp.k_out = ws_.kbuf.p + pre * row;
             qp.v_out = ws_.vbuf.p + pre * row;
-            qp.k_cache = c.k.p;
-            qp.v_cache = c.v.p;
+            qp.k_cache = c.k;
+            qp.v_cache = c.v;
             qp.cache_cap = static_cast<int>(c.cap);
             // a chunk longer than the ring leaves only its last `cap` tokens resident
             qp.cache_first = std::max(0, L - static_cast<int>(c.cap));
@@ -969,14 +959,14 @@ void Model::forward_chunk(KvState& kv, int L, uint32_t offset) {
         } else {
             GlobalCache& c = kv.global[gi++];
             if (c.capacity < committed) throw std::runtime_error("global cache not reserved");
-            qp.k_cache = c.k.p;
-            qp.v_cache = c.v.p;
+            qp.k_cache = c.k;
+            qp.v_cache = c.v;
             qp.cache_cap = static_cast<int>(c.capacity);
             qp.cache_first = 0;
             launch_qkv_post(qp, st);
             c.committed = committed;
-            ap.k = c.k.p;
-            ap.v = c.v.p;
+            ap.k = c.k;
+            ap.v = c.v;
             ap.Lk = static_cast<int>(committed);
             ap.k_pos0 = 0;
             ap.window = 0;
@@ -1241,8 +1231,8 @@ void Model::decode_layers(KvState& kv) {
         ap.out = ws_.attn.p;
         if (W.kind == LayerKind::Sliding) {
             LocalCache& c = kv.local[li++];
-            ap.k_cache = c.k.p;
-            ap.v_cache = c.v.p;
+            ap.k_cache = c.k;
+            ap.v_cache = c.v;
             ap.cap = static_cast<int>(c.cap);
             ap.tmap_k = &c.tk;
             ap.tmap_v = &c.tv;
@@ -1251,8 +1241,8 @@ void Model::decode_layers(KvState& kv) {
         } else {
             GlobalCache& c = kv.global[gi++];
             if (c.capacity < pos + 1) throw std::runtime_error("global cache not reserved");
-            ap.k_cache = c.k.p;
-            ap.v_cache = c.v.p;
+            ap.k_cache = c.k;
+            ap.v_cache = c.v;
             ap.cap = static_cast<int>(c.capacity);
             ap.tmap_k = &c.tk;
             ap.tmap_v = &c.tv;
@@ -1663,8 +1653,8 @@ std::vector<int> Model::stage_rows(KvState* const* kvs, int B, uint32_t pos_step
                     LocalCache& c = kv.local[li[b]++];
                     d.tk = c.tk;
                     d.tv = c.tv;
-                    d.k_cache = c.k.p;
-                    d.v_cache = c.v.p;
+                    d.k_cache = c.k;
+                    d.v_cache = c.v;
                     d.cap = static_cast<int>(c.cap);
                     d.n_keys = static_cast<int>(std::min(g.window, pos + 1));  // forward.cc:55-57
                 } else {
@@ -1672,8 +1662,8 @@ std::vector<int> Model::stage_rows(KvState* const* kvs, int B, uint32_t pos_step
                     if (c.capacity < pos + 1) throw std::runtime_error("global cache not reserved");
                     d.tk = c.tk;
                     d.tv = c.tv;
-                    d.k_cache = c.k.p;
-                    d.v_cache = c.v.p;
+                    d.k_cache = c.k;
+                    d.v_cache = c.v;
                     d.cap = static_cast<int>(c.capacity);
                     d.n_keys = static_cast<int>(pos + 1);
                 }

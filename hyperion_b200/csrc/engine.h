@@ -84,20 +84,28 @@ struct LayerW {
 };
 
 struct LocalCache {
-    DevPtr<bf16> k, v;
+    bf16* k = nullptr;  // [cap][nkv][hd] rows inside KvState::ring_arena
+    bf16* v = nullptr;
     uint32_t cap = 0, committed = 0;
     int nkv = 0, hd = 0;
     CUtensorMap tk{}, tv{};  // decode-attention tile maps of k / v (encode_kv_tensor_map)
 };
 
 struct GlobalCache {
-    DevPtr<bf16> k, v;
+    bf16* k = nullptr;  // [capacity][nkv][hd] rows inside KvState::global_arena
+    bf16* v = nullptr;
     uint32_t capacity = 0, committed = 0;
     int nkv = 0, hd = 0;
     CUtensorMap tk{}, tv{};  // re-encoded whenever the buffers grow
 };
 
+// A state's caches live in two allocations: every ring (K then V per sliding layer) in
+// ring_arena, every global cache in global_arena, which a growth replaces as a whole.
+// One allocation each keeps creating, growing, cloning and freeing a state to a single
+// cudaMalloc / cudaFree instead of one per layer.
 struct KvState {
+    DevPtr<bf16> ring_arena;
+    DevPtr<bf16> global_arena;
     std::vector<LocalCache> local;
     std::vector<GlobalCache> global;
     uint32_t offset = 0;
@@ -107,28 +115,26 @@ struct KvState {
 
 // A call that grows a global cache runs against staged buffers and publishes them only
 // when it succeeds (the reference's KvGrowthTransaction, kv_cache.h:220-261,
-// kv_cache.cc:68-128): the larger buffers are filled from the live ones and swapped in,
-// and the live buffers are kept here. On failure rollback restores them, the cursor and
-// every commit count, so the state stays usable; on success the kept buffers are freed.
+// kv_cache.cc:68-128): the larger arena is filled from the live one and swapped in, and
+// the live arena is kept here. On failure rollback restores it, the cursor and every
+// commit count, so the state stays usable; on success the kept arena is freed.
 // A ring (capacity window + 8) is written in place: a block of at most 8 tokens only
-// overwrites slots of positions the state no longer reads, longer blocks back the rings
-// up first.
+// overwrites slots of positions the state no longer reads, and a state at offset 0 holds
+// no position a later step reads before rewriting it; a longer block on a populated state
+// backs the ring arena up first.
 struct KvTransaction {
     bool active = false;
     uint32_t offset = 0, last_token = 0;
     std::vector<uint32_t> local_committed, global_committed;
     struct Global {
-        size_t index = 0;
-        DevPtr<bf16> k, v;
+        bf16* k = nullptr;
+        bf16* v = nullptr;
         uint32_t capacity = 0;
         CUtensorMap tk{}, tv{};
     };
-    struct Ring {
-        size_t index = 0;
-        DevPtr<bf16> k, v;
-    };
+    DevPtr<bf16> global_arena;  // the arena the staged one replaced
     std::vector<Global> globals;
-    std::vector<Ring> rings;
+    DevPtr<bf16> ring_backup;   // a copy of ring_arena, or empty
 };
 
 // Draft tokens one verify pass may check: the speculative slack of the local rings
@@ -206,10 +212,10 @@ class Model {
     // plan_kv_growth / GlobalKvCache::append semantics: 256-token steps).
     void reserve(KvState& kv, uint32_t n_tokens) const;
     // Device bytes a call of `n_tokens` more tokens adds while it runs (governor admission):
-    // the staged global caches it grows (their full new capacity: the live buffers stay
-    // allocated until the call publishes), ring backups for blocks longer than the ring
-    // slack, and the workspace it would newly allocate. Returns false if a cache dimension
-    // would not be representable.
+    // the staged global arena it grows (its full new size: the live arena stays allocated
+    // until the call publishes), the ring backup of a populated state for blocks longer
+    // than the ring slack, and the workspace it would newly allocate. Returns false if a
+    // cache dimension would not be representable.
     bool predict_call_bytes(const KvState& kv, uint32_t n_tokens, uint64_t* bytes) const;
     // Stage the growth of a call of `n_tokens` tokens (inactive when no global cache grows).
     KvTransaction begin_kv_transaction(KvState& kv, uint32_t n_tokens) const;
@@ -268,6 +274,10 @@ class Model {
     // Build the packed layout of every projection and of the embedding table, then free
     // the MLX-layout copies.
     void pack_all();
+    // Replace kv's global arena by one with room for `n_tokens` more tokens per global cache
+    // (256-token steps), the contents copied; the old arena goes to *old. False (nothing
+    // changed) when every cache already has room.
+    bool grow_globals(KvState& kv, uint32_t n_tokens, DevPtr<bf16>* old) const;
     // The MLX layout of rows [row0, row0 + n) of a packed [?, K] matrix, re-derived into the
     // shared unpack scratch on `st` (valid until the next call on the same stream).
     MlxView unpack_rows(const unsigned char* packed, int K, int row0, int n, cudaStream_t st);

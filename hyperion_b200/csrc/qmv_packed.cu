@@ -148,31 +148,42 @@ __device__ __forceinline__ void stage_input(const QmvParams& p, const PrologueWe
     auto ld = [](const uint4* a) { return *a; };
     const int K = p.K;
     if (p.prologue == QmvPrologue::kNone) {
-        // One cooperative round trip: 16-byte chunk j of x holds x[8j .. 8j+7], which is
-        // exactly the four permuted pairs xp[4j .. 4j+3] = (x[8j+p], x[8j+p+4]), p < 4.
-        // The 8 chunks of a group sit in 8 consecutive lanes, which reduce its sum.
+        // 16-byte chunk j of x holds x[8j .. 8j+7], which is exactly the four permuted
+        // pairs xp[4j .. 4j+3] = (x[8j+p], x[8j+p+4]), p < 4. The 8 chunks of a group sit
+        // in 8 consecutive lanes, which reduce its sum. Every thread issues all its loads
+        // of a round (up to kRound chunks: K <= 16384 in one round trip) before using any.
+        constexpr int kRound = 4;
+        const int nch = K / 8;
         const uint4* xv = reinterpret_cast<const uint4*>(p.x);
-        for (int j0 = 0; j0 < K / 8; j0 += kThreads) {
-            const int j = j0 + static_cast<int>(threadIdx.x);
-            uint4 v = make_uint4(0, 0, 0, 0);
-            if (j < K / 8) v = ld(xv + j);
-            const uint32_t w[4] = {v.x, v.y, v.z, v.w};
-            float part = 0.f;
+        for (int base = 0; base < nch; base += kRound * kThreads) {
+            uint4 v[kRound];
 #pragma unroll
-            for (int q = 0; q < 4; ++q) part += __uint_as_float(w[q] << 16) + __uint_as_float(w[q] & 0xFFFF0000u);
-            if (j < K / 8) {
-                // pairs: p = 0: (w0.lo, w2.lo), p = 1: (w0.hi, w2.hi), p = 2: (w1.lo, w3.lo), p = 3: (w1.hi, w3.hi)
-                uint4 o;
-                o.x = (w[0] & 0xFFFFu) | (w[2] << 16);
-                o.y = (w[0] >> 16) | (w[2] & 0xFFFF0000u);
-                o.z = (w[1] & 0xFFFFu) | (w[3] << 16);
-                o.w = (w[1] >> 16) | (w[3] & 0xFFFF0000u);
-                *reinterpret_cast<uint4*>(xp + 4 * j) = o;
+            for (int c = 0; c < kRound; ++c) {
+                const int j = base + static_cast<int>(threadIdx.x) + c * kThreads;
+                v[c] = j < nch ? ld(xv + j) : make_uint4(0, 0, 0, 0);
             }
-            part += __shfl_xor_sync(0xffffffffu, part, 1);
-            part += __shfl_xor_sync(0xffffffffu, part, 2);
-            part += __shfl_xor_sync(0xffffffffu, part, 4);
-            if (j < K / 8 && (j & 7) == 0) xsum[j >> 3] = part;
+#pragma unroll
+            for (int c = 0; c < kRound; ++c) {
+                if (base + c * kThreads >= nch) break;  // block-uniform
+                const int j = base + static_cast<int>(threadIdx.x) + c * kThreads;
+                const uint32_t w[4] = {v[c].x, v[c].y, v[c].z, v[c].w};
+                float part = 0.f;
+#pragma unroll
+                for (int q = 0; q < 4; ++q) part += __uint_as_float(w[q] << 16) + __uint_as_float(w[q] & 0xFFFF0000u);
+                if (j < nch) {
+                    // pairs: p = 0: (w0.lo, w2.lo), p = 1: (w0.hi, w2.hi), p = 2: (w1.lo, w3.lo), p = 3: (w1.hi, w3.hi)
+                    uint4 o;
+                    o.x = (w[0] & 0xFFFFu) | (w[2] << 16);
+                    o.y = (w[0] >> 16) | (w[2] & 0xFFFF0000u);
+                    o.z = (w[1] & 0xFFFFu) | (w[3] << 16);
+                    o.w = (w[1] >> 16) | (w[3] & 0xFFFF0000u);
+                    *reinterpret_cast<uint4*>(xp + 4 * j) = o;
+                }
+                part += __shfl_xor_sync(0xffffffffu, part, 1);
+                part += __shfl_xor_sync(0xffffffffu, part, 2);
+                part += __shfl_xor_sync(0xffffffffu, part, 4);
+                if (j < nch && (j & 7) == 0) xsum[j >> 3] = part;
+            }
         }
     } else {
         // Norm prologues in one round trip: every thread loads its 16-byte chunks of x

@@ -24,7 +24,9 @@ import sys
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 REPO = os.path.dirname(HERE)
-REF = os.environ.get("HYPERION_REFERENCE_ROOT", "/root/reference")
+# The reference checkout: $HYPERION_REFERENCE_ROOT, else a directory named `reference`
+# beside this repository's checkout. Without either, only the oracle's own libraries build.
+REF = os.environ.get("HYPERION_REFERENCE_ROOT") or os.path.join(os.path.dirname(REPO), "reference")
 REF_SRC = os.path.join(REF, "native", "hyperion_mlx", "src")
 REF_TESTS = os.path.join(REF, "native", "hyperion_mlx", "tests")
 REF_INC = os.path.join(REF, "native", "hyperion_mlx", "include")
