@@ -62,7 +62,7 @@ __device__ __forceinline__ float block_sum(float v, float* tmp, int slot) {
 
 // Operands of a norm prologue that do not depend on earlier kernels (norm weights, the
 // post-norm weights and the layer scalar), loaded before the dependent-launch wait.
-constexpr int kMaxPrologueChunks = kMaxPrologueK / 8 / kThreads;
+constexpr int kMaxPrologueChunks = (kMaxPrologueK / 8 + kThreads - 1) / kThreads;
 struct PrologueWeights {
     uint4 nw[kMaxPrologueChunks], pw[kMaxPrologueChunks];
     float scalar = 1.f;
