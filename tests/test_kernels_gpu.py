@@ -69,6 +69,29 @@ def test_qmm_prefill_shapes(built_lib, oracle_lib, M, K, N):
     assert within_one_ulp(y, want) >= 0.999
 
 
+# the config-2 layer projections at M = 8192 (the 256 x 256 tile path with every SM busy);
+# a seeded 96-row x 160-column sample of each output is checked against the oracle
+@pytest.mark.parametrize("K,N", [(3840, 8192), (4096, 3840), (3840, 30720), (15360, 3840)])
+def test_qmm_cfg2_shapes_m8192_sampled(built_lib, oracle_lib, K, N):
+    from hyperion_b200 import ops
+    from oracle import gemma_oracle as go
+    import torch
+    M = 8192
+    rng = np.random.default_rng(K + N)
+    w, s, b = random_q4(rng, N, K)
+    x = f32_to_bf16_bits(rng.standard_normal((M, K), dtype=np.float32))
+    y = ops.quantized_matmul(dev(x), dev(w), dev(s), dev(b))
+    torch.cuda.synchronize()
+    pick = np.random.default_rng(3)
+    rows = np.sort(pick.choice(M, 96, replace=False))
+    cols = np.sort(pick.choice(N, 160, replace=False))
+    rows[-1], cols[-1] = M - 1, N - 1  # the last tile row and column
+    got = host(y[torch.from_numpy(rows).cuda()][:, torch.from_numpy(cols).cuda()].contiguous())
+    want = go.qmm(x[rows], w[cols], s[cols], b[cols])
+    assert rel_l2(got, want) <= REL_L2_QMM
+    assert within_one_ulp(got, want) >= 0.999
+
+
 def test_qmm_general_affine_within_fp16_bound(built_lib, oracle_lib):
     """Codes quantized from real-valued weights (bias != -8 s): w_hat is rounded to fp16 once."""
     from hyperion_b200.synth import affine_quantize

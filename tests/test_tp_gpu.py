@@ -25,7 +25,7 @@ def _n_gpus():
 
 pytestmark = [pytest.mark.gpu, pytest.mark.skipif(_n_gpus() < 2, reason="needs 2 GPUs")]
 
-N_LAYERS, STEPS, SEED = 6, 16, 11
+N_LAYERS, STEPS, SEED = 6, 48, 11
 
 
 def _run(rank, world, uid, prompt, forced, results):
@@ -76,6 +76,13 @@ def test_tp2_matches_tp1(built_lib):
     # verify rows and the batched step against TP = 1 (same inputs; caches differ by rounding)
     assert np.mean([a == b for a, b in zip(v0 + b0, ref_v + ref_b)]) >= 7 / 9, (v0, ref_v, b0, ref_b)
     rels = [rel_l2(lg0[i], ref_lg[i]) for i in range(len(ref_lg))]
-    agree = np.mean([a == b for a, b in zip(t0, ref_toks)])
+    same = np.asarray([a == b for a, b in zip(t0, ref_toks)])
+    # steps whose TP = 1 winner leads its runner-up by more than two bf16 ulps must agree;
+    # near-ties may flip with the order of the row-parallel sums
+    from tests.test_parity_12b_gpu import _gap_ulps
+    decisive = np.asarray([_gap_ulps(ref_lg[i]) > 2.0 for i in range(len(ref_lg))])
+    print(f"\nTP 2 vs TP 1: {same.mean():.3f} of {same.size} steps agree, decisive {decisive.sum()} all agree: "
+          f"{bool(same[decisive].all())}; logit rel-L2 max {max(rels):.2e}")
     assert max(rels) <= 5e-2 and np.mean(rels) <= 2e-2, rels
-    assert agree >= 15 / 17, (t0, ref_toks)
+    assert same[decisive].all(), (t0, ref_toks)
+    assert same.mean() >= 0.9, (t0, ref_toks)
