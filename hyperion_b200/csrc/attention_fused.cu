@@ -639,10 +639,11 @@ void launch_fused_t(const DecodeFusedParams& p, cudaStream_t stream, bool pdl) {
         HYB_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1));
         attr_dev = dev;
     }
-    // clusters above the portable 8 CTAs only where all of the launch's clusters fit at once
+    // clusters above the portable 8 CTAs only where all of the launch's clusters fit at
+    // once: the largest such size (each smaller cap may give fewer tiles per CTA than 8)
     FusedPlan f = plan_fused(PER * 32, REP, p.n_keys, units, kMaxCluster);
-    if (f.stages != 0 && f.cs > kPortableCluster && resident_clusters(kern, f.cs, f.smem) < units)
-        f = plan_fused(PER * 32, REP, p.n_keys, units, kPortableCluster);
+    while (f.stages != 0 && f.cs > kPortableCluster && resident_clusters(kern, f.cs, f.smem) < units)
+        f = plan_fused(PER * 32, REP, p.n_keys, units, f.cs - 1);
     if (f.stages == 0) throw ArgError("decode attention: too many keys for the shared-memory plan");
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(f.cs, p.n_kv, p.seqs ? p.n_seq : 1);
