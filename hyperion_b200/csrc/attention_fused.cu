@@ -331,8 +331,10 @@ __global__ void __launch_bounds__(kThreads, 1) decode_attn_fused_kernel(const De
         asm volatile("fence.proxy.tensormap::generic.acquire.gpu [%0], 128;" ::"l"(map_k) : "memory");
         asm volatile("fence.proxy.tensormap::generic.acquire.gpu [%0], 128;" ::"l"(map_v) : "memory");
     }
-    // the first stages, one issuing thread each
-    if (static_cast<int>(threadIdx.x) < stages && static_cast<int>(threadIdx.x) < items) issue(threadIdx.x);
+    // the first stages, one issuing thread each: K tiles now, the first V tiles after
+    // phase 0 (whose loads of the projection row would otherwise queue behind them)
+    const int first_v = min(stages, min(items, nt));
+    if (static_cast<int>(threadIdx.x) < first_v) issue(threadIdx.x);
 
     pdl_wait();
     // ---- phase 0: query heads of this KV head, and the new token's K/V
@@ -352,6 +354,8 @@ __global__ void __launch_bounds__(kThreads, 1) decode_attn_fused_kernel(const De
                                v_cache + (static_cast<size_t>(slot) * p.n_kv + hk) * HD);
     }
     __syncthreads();
+    if (static_cast<int>(threadIdx.x) >= first_v && static_cast<int>(threadIdx.x) < min(stages, items))
+        issue(threadIdx.x);
 
     bool waits_ok = true;
     auto wait_full = [&](int it) {
