@@ -142,9 +142,11 @@ __device__ __forceinline__ uint4 ar_chunk(const QmvParams& p, int j) {
 
 // The input vector into shared memory: x (or its norm prologue) as the permuted
 // bf16 pairs the MMA B fragments read, and the per-group sums of x.
-template <bool AR>
+// `after_loads` runs once every load of x (and resid) is issued: the kernel issues the rest
+// of its first weight stages there, so those loads do not queue behind the bulk copies.
+template <bool AR, typename AfterLoads>
 __device__ __forceinline__ void stage_input(const QmvParams& p, const PrologueWeights& pw, uint32_t* xp, float* xsum,
-                                            float* tmp) {
+                                            float* tmp, AfterLoads after_loads) {
     auto ld = [](const uint4* a) { return *a; };
     const int K = p.K;
     if (p.prologue == QmvPrologue::kNone) {
@@ -162,6 +164,7 @@ __device__ __forceinline__ void stage_input(const QmvParams& p, const PrologueWe
                 const int j = base + static_cast<int>(threadIdx.x) + c * kThreads;
                 v[c] = j < nch ? ld(xv + j) : make_uint4(0, 0, 0, 0);
             }
+            if (base == 0) after_loads();
 #pragma unroll
             for (int c = 0; c < kRound; ++c) {
                 if (base + c * kThreads >= nch) break;  // block-uniform
@@ -208,6 +211,7 @@ __device__ __forceinline__ void stage_input(const QmvParams& p, const PrologueWe
                 if (resid) rv[c] = ld(reinterpret_cast<const uint4*>(p.resid) + j);
             }
         }
+        after_loads();
         auto lo = [](uint32_t w) { return __uint_as_float(w << 16); };
         auto hi = [](uint32_t w) { return __uint_as_float(w & 0xFFFF0000u); };
         float ss = 0.f;
@@ -435,14 +439,19 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) qmv_packed_kernel(const 
             }
         }
     };
-    // weights do not depend on the previous kernel: fill the ring before the PDL wait
-    while (n_issued < kStages && n_issued < n_items) issue_next();
+    // weights do not depend on the previous kernel: the first stage before the PDL wait,
+    // the others once the input's loads are issued (all of them before the wait when the
+    // input arrives through the fused all-reduce, whose wait would delay them)
+    const int pre = (AR && p.ar_mode == 2) ? kStages : 1;
+    while (n_issued < pre && n_issued < n_items) issue_next();
     PrologueWeights pw;
     if (p.prologue != QmvPrologue::kNone) pw = load_prologue_weights(p);
 
     pdl_wait();
     if (threadIdx.x < 32) zero_page[threadIdx.x] = 0u;
-    stage_input<AR>(p, pw, xp, xsum, tmp);
+    stage_input<AR>(p, pw, xp, xsum, tmp, [&]() {
+        while (n_issued < kStages && n_issued < n_items) issue_next();
+    });
     __syncthreads();
 
     uint32_t phase_bits = 0;  // one parity bit per stage
