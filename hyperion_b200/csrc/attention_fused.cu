@@ -417,15 +417,19 @@ __global__ void __launch_bounds__(kThreads, 1) decode_attn_fused_kernel(const De
             const int kb = tk.x, ke = tk.y;
             if (owns_newest && newest >= kb + 8 * warp && newest < kb + 8 * warp + 8 && newest < ke)
                 patch_row(tile, newest - kb, knew, 0, HD / 8);
-            float acc[4] = {0.f, 0.f, 0.f, 0.f};
+            // two independent accumulator chains (even and odd k-steps) halve the MMA
+            // dependency chain; they are added once at the end
+            float acc[4] = {0.f, 0.f, 0.f, 0.f}, acc2[4] = {0.f, 0.f, 0.f, 0.f};
             const int lr = 8 * warp + (lane & 7);  // this lane's ldmatrix row
 #pragma unroll
             for (int k2 = 0; k2 < KSTEPS / 2; ++k2) {
                 uint32_t b0, b1, b2, b3;
                 ldsm_x4(tile + tile_off(lr, 4 * k2 + (lane >> 3)), b0, b1, b2, b3);
                 mma_bf16_16816(acc, qa[2 * k2][0], 0u, qa[2 * k2][1], 0u, b0, b1);
-                mma_bf16_16816(acc, qa[2 * k2 + 1][0], 0u, qa[2 * k2 + 1][1], 0u, b2, b3);
+                mma_bf16_16816(acc2, qa[2 * k2 + 1][0], 0u, qa[2 * k2 + 1][1], 0u, b2, b3);
             }
+            acc[0] += acc2[0];
+            acc[1] += acc2[1];
             if (g < REP) {
                 const int j = kb + 8 * warp + 2 * t4;
                 if (j < ke) s_sc[g * chunk + (j - j0)] = score_round(acc[0], p.scale, p.softcap, ROUND);
@@ -434,24 +438,43 @@ __global__ void __launch_bounds__(kThreads, 1) decode_attn_fused_kernel(const De
             release(it);
         }
     }
-    // ---- this warp's (max, sum of exp) per head over its own keys
+    // ---- this warp's (max, sum of exp) per head over its own keys, every head in the
+    // same passes (independent shuffle chains)
+    {
+        float m[REP], l[REP];
 #pragma unroll
-    for (int h = 0; h < REP; ++h) {
-        float m = -FLT_MAX;
+        for (int h = 0; h < REP; ++h) {
+            m[h] = -FLT_MAX;
+            l[h] = 0.f;
+        }
         for (int i = lane; i < my_count; i += 32) {
             const int k = my_key(i);
-            if (k >= 0) m = fmaxf(m, s_sc[h * chunk + k]);
+            if (k >= 0) {
+#pragma unroll
+                for (int h = 0; h < REP; ++h) m[h] = fmaxf(m[h], s_sc[h * chunk + k]);
+            }
         }
-        m = warp_max(m);
-        float l = 0.f;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+            for (int h = 0; h < REP; ++h) m[h] = fmaxf(m[h], __shfl_xor_sync(0xffffffffu, m[h], o));
         for (int i = lane; i < my_count; i += 32) {
             const int k = my_key(i);
-            if (k >= 0) l += exp_fast(s_sc[h * chunk + k] - m);
+            if (k >= 0) {
+#pragma unroll
+                for (int h = 0; h < REP; ++h) l[h] += exp_fast(s_sc[h * chunk + k] - m[h]);
+            }
         }
-        l = warp_sum(l);
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+            for (int h = 0; h < REP; ++h) l[h] += __shfl_xor_sync(0xffffffffu, l[h], o);
         if (lane == 0) {
-            wml[(warp * REP + h) * 2] = m;
-            wml[(warp * REP + h) * 2 + 1] = l;
+#pragma unroll
+            for (int h = 0; h < REP; ++h) {
+                wml[(warp * REP + h) * 2] = m[h];
+                wml[(warp * REP + h) * 2 + 1] = l[h];
+            }
         }
     }
     __syncthreads();
