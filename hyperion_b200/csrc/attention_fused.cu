@@ -491,18 +491,30 @@ __global__ void __launch_bounds__(kThreads, 1) decode_attn_fused_kernel(const De
     cluster_sync();
     // ---- row statistics (lane h < REP), then p in place over this warp's keys
     {
+        // heads in pairs, one per 16-lane half: lane c (< CS) of a half holds CTA c's pair
+        // for its head, and the half's shuffle tree merges them
+        float Mh[REP], iLh[REP];
 #pragma unroll
-        for (int h = 0; h < REP; ++h) {
-            // lane c (< CS) holds CTA c's pair for head h; the shuffle tree merges them
+        for (int h0 = 0; h0 < REP; h0 += 2) {
+            const int hh = h0 + (lane >> 4);
             const int c = lane & 15;
-            const bool has = c < CS;
+            const bool has = c < CS && hh < REP;
             float M, L;
-            merge16(has ? allml[(c * REP + h) * 2] : -FLT_MAX, has ? allml[(c * REP + h) * 2 + 1] : 0.f, M, L);
+            merge16(has ? allml[(c * REP + hh) * 2] : -FLT_MAX, has ? allml[(c * REP + hh) * 2 + 1] : 0.f, M, L);
             const float iL = 1.0f / L;
-            for (int i = lane; i < my_count; i += 32) {
-                const int k = my_key(i);
-                if (k >= 0) {
-                    const float e = exp_fast(s_sc[h * chunk + k] - M) * iL;
+            Mh[h0] = __shfl_sync(0xffffffffu, M, 0);
+            iLh[h0] = __shfl_sync(0xffffffffu, iL, 0);
+            if (h0 + 1 < REP) {
+                Mh[h0 + 1] = __shfl_sync(0xffffffffu, M, 16);
+                iLh[h0 + 1] = __shfl_sync(0xffffffffu, iL, 16);
+            }
+        }
+        for (int i = lane; i < my_count; i += 32) {
+            const int k = my_key(i);
+            if (k >= 0) {
+#pragma unroll
+                for (int h = 0; h < REP; ++h) {
+                    const float e = exp_fast(s_sc[h * chunk + k] - Mh[h]) * iLh[h];
                     s_sc[h * chunk + k] = (ROUND == 0) ? rbf(e) : e;
                 }
             }
