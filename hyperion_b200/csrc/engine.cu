@@ -975,8 +975,12 @@ void Model::forward_chunk(KvState& kv, int L, uint32_t offset) {
         gemm(ws_.attn.p, W.o, ws_.o.p);
         tp_.all_reduce_sum_bf16(ws_.o.p, static_cast<size_t>(L) * H, st);  // row-parallel o_proj
         launch_resid_norm(ws_.o.p, W.post_attn.p, h_cur, nullptr, h_alt, W.pre_ff.p, ws_.xn.p, L, H, g.eps, st);
-        gemm(ws_.xn.p, W.gateup, ws_.gu.p);
-        {
+        if (qmm_tc_geglu_supported(L, H, W.gateup.N)) {
+            // GeGLU in the GEMM's epilogue: the interleaved gate/up output never reaches memory
+            const MlxView m = unpack_rows(W.gateup.packed.p, H, 0, W.gateup.N, st);
+            launch_qmm_tc(ws_.xn.p, m.w, m.s, m.b, ws_.act.p, L, H, W.gateup.N, st, true);
+        } else {
+            gemm(ws_.xn.p, W.gateup, ws_.gu.p);
             dim3 grid(std::min((I + 255) / 256, 64), L);
             geglu_interleaved_kernel<<<grid, 256, 0, st>>>(ws_.gu.p, ws_.act.p, I);
             HYB_LAUNCH_CHECK("geglu_interleaved_kernel");
@@ -1496,6 +1500,10 @@ void Model::rows_forward(int B, const std::vector<int>& keys_max, const KvState*
         const MlxView m = unpack_rows(q.packed.p, K, 0, N, st);
         if (!geglu) {
             launch_quantized_matmul(x, m.w, m.s, m.b, y, B, K, N, st);
+            return;
+        }
+        if (qmm_tc_geglu_supported(B, K, N)) {
+            launch_qmm_tc(x, m.w, m.s, m.b, y, B, K, N, st, true);
             return;
         }
         launch_quantized_matmul(x, m.w, m.s, m.b, ws_.gu.p, B, K, N, st);

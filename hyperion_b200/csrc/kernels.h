@@ -107,7 +107,10 @@ int64_t read_qmvb_wait_timeouts();
 // tiles, f16 operands dequantised in shared memory, fp32 accumulation.
 bool qmm_tc_supported(int M, int K, int N);
 void launch_qmm_tc(const bf16* x, const uint32_t* w, const bf16* s, const bf16* b, bf16* y, int M, int K, int N,
-                   cudaStream_t stream);
+                   cudaStream_t stream, bool geglu = false);
+// geglu: W is the interleaved gate/up matrix (16-row tiles) and y [M, N/2] receives
+// GeGLU(gate, up) from the epilogue; shapes the split-K plan would take are not supported.
+bool qmm_tc_geglu_supported(int M, int K, int N);
 int64_t read_qmm_wait_timeouts();
 // Legacy prefill qmm on mma.sync (qmm.cu).
 void launch_qmm(const bf16* x, const uint32_t* w, const bf16* s, const bf16* b, bf16* y,

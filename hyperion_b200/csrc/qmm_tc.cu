@@ -26,6 +26,7 @@
 // bf16 activations convert to f16 exactly inside f16's range (|x| < 65504).
 // Every mbarrier wait is bounded; TMEM is always freed before the CTA exits.
 #include "kernels.h"
+#include "qmv_pack.cuh"
 #include "tcgen05.cuh"
 #include "tma.cuh"
 
@@ -120,7 +121,7 @@ template <int MT>
 __global__ void __launch_bounds__(kThreads, 1)
     qmm_tc_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_w,
                   const bf16* __restrict__ scales, const bf16* __restrict__ biases, bf16* __restrict__ y, int M,
-                  int K, int N, int kper, float* __restrict__ part) {
+                  int K, int N, int kper, float* __restrict__ part, int geglu) {
     using P = Plan<MT>;
     constexpr int S = P::S;
     extern __shared__ unsigned char smem_dyn[];
@@ -271,6 +272,28 @@ __global__ void __launch_bounds__(kThreads, 1)
                         for (int v = 0; v < 32; ++v)
                             if (n0 + col + v < N) dst[v] = __uint_as_float(rr[v]);
                     }
+                } else if (m < M && geglu) {
+                    // interleaved gate/up: these 32 columns are one 16-row gate tile and its
+                    // up tile, i.e. outputs (n0 + col) / 2 .. + 15 of the GeGLU row
+                    if (n0 + col + 32 <= N) {
+                        bf16* dst = y + static_cast<size_t>(m) * (N / 2) + (n0 + col) / 2;
+#pragma unroll
+                        for (int v = 0; v < 2; ++v) {
+                            float o[8];
+#pragma unroll
+                            for (int r = 0; r < 8; ++r) {
+                                const float gv = rbf(__uint_as_float(rr[8 * v + r]));
+                                const float uv = rbf(__uint_as_float(rr[16 + 8 * v + r]));
+                                o[r] = gelu_tanh_bf16ops(gv) * uv;
+                            }
+                            uint4 q;
+                            q.x = pack_bf2(f2bf(o[0]), f2bf(o[1]));
+                            q.y = pack_bf2(f2bf(o[2]), f2bf(o[3]));
+                            q.z = pack_bf2(f2bf(o[4]), f2bf(o[5]));
+                            q.w = pack_bf2(f2bf(o[6]), f2bf(o[7]));
+                            *reinterpret_cast<uint4*>(dst + 8 * v) = q;
+                        }
+                    }
                 } else if (m < M) {
                     bf16* dst = y + static_cast<size_t>(m) * N + n0 + col;
                     if (n0 + col + 32 <= N && (N % 8) == 0) {
@@ -330,7 +353,7 @@ __global__ void splitk_reduce_kernel(const float* __restrict__ part, int splits,
 
 template <int MT>
 void launch_tc(const CUtensorMap& tx, const CUtensorMap& tw, const bf16* s, const bf16* b, bf16* y, int M, int K,
-               int N, int splits, int kper, float* part, cudaStream_t stream) {
+               int N, int splits, int kper, float* part, bool geglu, cudaStream_t stream) {
     static int attr_dev = -1;
     int dev = 0;
     HYB_CUDA(cudaGetDevice(&dev));
@@ -339,7 +362,8 @@ void launch_tc(const CUtensorMap& tx, const CUtensorMap& tw, const bf16* s, cons
         attr_dev = dev;
     }
     const dim3 grid((M + kBM * MT - 1) / (kBM * MT), (N + kBN - 1) / kBN, splits);
-    qmm_tc_kernel<MT><<<grid, kThreads, Plan<MT>::kSmem, stream>>>(tx, tw, s, b, y, M, K, N, kper, part);
+    qmm_tc_kernel<MT><<<grid, kThreads, Plan<MT>::kSmem, stream>>>(tx, tw, s, b, y, M, K, N, kper, part,
+                                                                  geglu ? 1 : 0);
     HYB_LAUNCH_CHECK("qmm_tc_kernel");
 }
 
@@ -349,9 +373,28 @@ bool qmm_tc_supported(int M, int K, int N) {
     return M >= 2 && K >= 64 && K % 64 == 0 && N >= 1;
 }
 
+namespace {
+
+// The tile plan of an M x N x K product: 2 or 1 token blocks per CTA, or split-K (0).
+int tc_plan(int M, int K, int N) {
+    const long long tiles2 = static_cast<long long>((M + 255) / 256) * ((N + kBN - 1) / kBN);
+    const long long tiles1 = static_cast<long long>((M + kBM - 1) / kBM) * ((N + kBN - 1) / kBN);
+    const int nk = K / kBK;
+    if (tiles2 >= num_sms()) return 2;
+    if (tiles1 >= num_sms() || nk < 8) return 1;
+    return 0;
+}
+
+}  // namespace
+
+bool qmm_tc_geglu_supported(int M, int K, int N) {
+    return qmm_tc_supported(M, K, N) && N % 32 == 0 && tc_plan(M, K, N) != 0;
+}
+
 void launch_qmm_tc(const bf16* x, const uint32_t* w, const bf16* s, const bf16* b, bf16* y, int M, int K, int N,
-                   cudaStream_t stream) {
+                   cudaStream_t stream, bool geglu) {
     if (!qmm_tc_supported(M, K, N)) throw ArgError("qmm: shape not supported by the tensor-core path");
+    if (geglu && !qmm_tc_geglu_supported(M, K, N)) throw ArgError("qmm: GeGLU epilogue not supported for this shape");
     if ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(w)) & 15)
         throw ArgError("qmm: x and w must be 16-byte aligned");
     // X to f16 (K-permuted) once; every N tile then loads it straight into the MMA operand ring
@@ -376,13 +419,13 @@ void launch_qmm_tc(const bf16* x, const uint32_t* w, const bf16* s, const bf16* 
         encode_tma(&tw, CU_TENSOR_MAP_DATA_TYPE_UINT32, 2, w, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_NONE);
     }
     // two 128-token blocks per CTA once there are enough tiles to fill the GPU
-    const long long tiles2 = static_cast<long long>((M + 255) / 256) * ((N + kBN - 1) / kBN);
     const long long tiles1 = static_cast<long long>((M + kBM - 1) / kBM) * ((N + kBN - 1) / kBN);
     const int nk = K / kBK;
-    if (tiles2 >= num_sms()) {
-        launch_tc<2>(tx, tw, s, b, y, M, K, N, 1, nk, nullptr, stream);
-    } else if (tiles1 >= num_sms() || nk < 8) {
-        launch_tc<1>(tx, tw, s, b, y, M, K, N, 1, nk, nullptr, stream);
+    const int plan = tc_plan(M, K, N);
+    if (plan == 2) {
+        launch_tc<2>(tx, tw, s, b, y, M, K, N, 1, nk, nullptr, geglu, stream);
+    } else if (plan == 1) {
+        launch_tc<1>(tx, tw, s, b, y, M, K, N, 1, nk, nullptr, geglu, stream);
     } else {
         // split K so that about two CTAs per SM work, each slice at least 4 k-blocks
         int splits = static_cast<int>(std::min<long long>(nk / 4, (2LL * num_sms() + tiles1 - 1) / tiles1));
@@ -392,7 +435,7 @@ void launch_qmm_tc(const bf16* x, const uint32_t* w, const bf16* s, const bf16* 
         const size_t mn = static_cast<size_t>(M) * N;
         float* part = nullptr;
         HYB_CUDA(cudaMallocAsync(reinterpret_cast<void**>(&part), mn * splits * sizeof(float), stream));
-        launch_tc<1>(tx, tw, s, b, y, M, K, N, splits, kper, part, stream);
+        launch_tc<1>(tx, tw, s, b, y, M, K, N, splits, kper, part, false, stream);
         const int rgrid = static_cast<int>(std::min<size_t>((mn / 4 + 255) / 256 + 1, 8 * static_cast<size_t>(num_sms())));
         splitk_reduce_kernel<<<rgrid, 256, 0, stream>>>(part, splits, mn, y);
         HYB_LAUNCH_CHECK("splitk_reduce_kernel");
