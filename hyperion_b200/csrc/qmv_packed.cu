@@ -114,10 +114,15 @@ __device__ __forceinline__ uint4 ar_chunk(const QmvParams& p, int j) {
     for (int src = 0; src < p.ar.T; ++src) {
         const unsigned char* slot =
             mine + p.ar.ll_off + (static_cast<size_t>(p.ar.set) * p.ar.T + src) * (p.ar.max_count / 2) * 8;
+        // the source's four words as independent loads (one round trip), then each
+        // re-read only while it does not yet carry this all-reduce's epoch
+        unsigned long long ws[4];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) ws[q] = ld_relaxed_sys_u64(slot + (static_cast<size_t>(4 * j + q)) * 8);
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
             const void* wp = slot + (static_cast<size_t>(4 * j + q)) * 8;
-            unsigned long long w = ld_relaxed_sys_u64(wp);
+            unsigned long long w = ws[q];
             for (int it = 0; static_cast<unsigned>(w >> 32) != p.ar.epoch; ++it) {
                 if (it >= (1 << 22)) {
                     ok = false;
