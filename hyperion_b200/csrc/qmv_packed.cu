@@ -290,10 +290,11 @@ __device__ __forceinline__ void stage_input(const QmvParams& p, const PrologueWe
 // pairs on the tensor cores, then the per-group scale and bias fold in fp32). Full
 // units (8 groups: every lane valid) skip the per-lane validity selects; only the
 // last unit of a row can be partial.
-template <bool FULL>
+// `after_reads` runs once the item's bytes are in registers: its ring stage is free then.
+template <bool FULL, typename AfterReads>
 __device__ __forceinline__ void qmv_item(const unsigned char* st, const uint32_t* xp, const uint32_t* zero_page,
                                          const float* xsum, const PackGeo& pg, int unit, int g, int t, float& acc0,
-                                         float& acc1) {
+                                         float& acc1, AfterReads after_reads) {
     const int tv = FULL ? 4 : (pg.gc_last + 1) / 2;
     const int nv = 8 * tv;
     const bool valid = FULL || t < tv;
@@ -304,6 +305,7 @@ __device__ __forceinline__ void qmv_item(const unsigned char* st, const uint32_t
         wv[c] = valid ? *reinterpret_cast<const uint4*>(st + (c * nv + rank) * 16) : make_uint4(0, 0, 0, 0);
     const uint4 sb =
         valid ? *reinterpret_cast<const uint4*>(st + (8 * nv + rank) * 16) : make_uint4(0, 0, 0, 0);
+    after_reads();
     const int gA = unit * 8 + 2 * t;
     const uint32_t* src0 = (g == 2 * t && (FULL || gA < pg.G)) ? xp + gA * 32 : zero_page;
     const uint32_t* src1 = (g == 2 * t + 1 && (FULL || gA + 1 < pg.G)) ? xp + (gA + 1) * 32 : zero_page;
@@ -469,23 +471,30 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) qmv_packed_kernel(const 
             float acc0 = 0.f, acc1 = 0.f;
             for (int ui = 0; ui < my_units; ++ui, ++it) {
                 const int unit = wt + ui * W;
-                if (it >= 1 && n_issued < n_items) {
-                    // refill the stage item it - 1 used; its reads ended before this
-                    // warp's previous mma.sync
-                    fence_proxy_async();
-                    issue_next();
-                }
                 const int s = it % kStages;
                 const bool ok = mbar_wait(my_bar0 + 8 * s, (phase_bits >> s) & 1u);
                 phase_bits ^= (1u << s);
-                if (!ok || rb >= pg.nrb) continue;
+                // Refill this item's stage with item it + kStages as soon as its bytes are
+                // in registers (every lane's reads ordered before lane 0's bulk copy), so
+                // two items stay in flight while this one is computed.
+                auto refill = [&]() {
+                    if (n_issued < n_items) {
+                        fence_proxy_async();
+                        __syncwarp();
+                        issue_next();
+                    }
+                };
+                if (!ok || rb >= pg.nrb) {
+                    refill();
+                    continue;
+                }
                 const unsigned char* st = my_ring + s * kItemMax;
                 // Full units (8 groups: every lane valid) take a path without the
                 // per-lane validity selects; only the last unit can be partial.
                 if (unit != pg.nunits - 1 || pg.gc_last == 8)
-                    qmv_item<true>(st, xp, zero_page, xsum, pg, unit, g, t, acc0, acc1);
+                    qmv_item<true>(st, xp, zero_page, xsum, pg, unit, g, t, acc0, acc1, refill);
                 else
-                    qmv_item<false>(st, xp, zero_page, xsum, pg, unit, g, t, acc0, acc1);
+                    qmv_item<false>(st, xp, zero_page, xsum, pg, unit, g, t, acc0, acc1, refill);
             }
             acc0 += __shfl_xor_sync(0xffffffffu, acc0, 1);
             acc0 += __shfl_xor_sync(0xffffffffu, acc0, 2);
