@@ -158,14 +158,22 @@ __global__ void __launch_bounds__(kThreads) qmv_batched_kernel(const QmvBatchPar
             for (int o = 0; o < NB8; ++o) acc[o][0] = acc[o][1] = acc[o][2] = acc[o][3] = 0.f;
             for (int ui = 0; ui < my_units; ++ui, ++it) {
                 const int unit = wt + ui * W;
-                if (it >= 1 && n_issued < n_items) {
-                    fence_proxy_async();
-                    issue_next();
-                }
                 const int s = it % kStages;
                 const bool ok = mbar_wait_b(my_bar0 + 8 * s, (phase_bits >> s) & 1u);
                 phase_bits ^= (1u << s);
-                if (!ok || rb >= pg.nrb) continue;
+                // refill this item's stage with item it + kStages once its bytes are in
+                // registers (every lane's reads ordered before lane 0's bulk copy)
+                auto refill = [&]() {
+                    if (n_issued < n_items) {
+                        fence_proxy_async();
+                        __syncwarp();
+                        issue_next();
+                    }
+                };
+                if (!ok || rb >= pg.nrb) {
+                    refill();
+                    continue;
+                }
                 const unsigned char* st = my_ring + s * kItemMax;
                 const bool full = unit != pg.nunits - 1 || pg.gc_last == 8;
                 const int tv = full ? 4 : (pg.gc_last + 1) / 2;
@@ -177,6 +185,7 @@ __global__ void __launch_bounds__(kThreads) qmv_batched_kernel(const QmvBatchPar
                 for (int c = 0; c < 8; ++c)
                     wv[c] = valid ? *reinterpret_cast<const uint4*>(st + (c * nv + rank) * 16) : make_uint4(0, 0, 0, 0);
                 const uint4 sb = valid ? *reinterpret_cast<const uint4*>(st + (8 * nv + rank) * 16) : make_uint4(0, 0, 0, 0);
+                refill();
 #pragma unroll
                 for (int sel = 0; sel < 2; ++sel) {  // group 2t (sel 0) or 2t + 1 of the unit
                     const int G = unit * 8 + 2 * t + sel;
